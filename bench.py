@@ -1,0 +1,527 @@
+#!/usr/bin/env python
+"""Decode benchmark of the 12.7B-class q4 GDA model on B200 (one JSON line on stdout).
+
+Headline (BASELINE.json metric, config[1]): greedy decode tok/s after a
+164-token random prompt, random-init weights (std 0.02, q4 group 64, fp16
+scales/biases), fp16 4-slot KV cache, batch 1. A "step" is one decode token:
+one replay of the captured CUDA graph (48 layers + lm_head + argmax); the
+next input token never leaves the GPU. Weights (6.85 GB) are far larger than
+L2, so every step streams them from HBM (no flush needed).
+
+Also reported in the same line:
+  e2e           the same metric through the public per-token API
+                (``MotifDecoder.decode_host``): pinned-host token -> device,
+                one replay, argmax -> pinned host, sync, every step.
+  roofline      dominant kernel = the q4 GEMV (``motif_quantized_linear``):
+                algorithmic bytes (packed weights + scales + biases + x + y)
+                of one step's 193 GEMV launches / their CUDA-event time.
+  extra.p16k_*  config[2]: decode at a 16000-token context (KV cache filled
+                with synthetic N(0,1)·0.5 rows), q4 and fp16 4-slot caches,
+                with the attention kernels' HBM GB/s.
+  cpu_baseline  the CPU oracle (numpy restatement of the reference path) on
+                one full-size layer, scaled to a token.
+
+Multi-GPU (``torchrun --nproc-per-node N``): tensor parallel over N ranks
+(GDA groups and MLP columns sharded, NCCL all-reduce after o_proj and
+down_proj, PolyNorm statistics all-reduced); the timed region is the max over
+ranks; the token stream is shared, so value = tokens/s of the one stream
+(scaling "strong": the model is fixed while N grows).
+
+``--impl reference`` times the reference's CPU implementation of the path
+(the oracle port: MLX is not installable here) on the host cores.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+for _p in (str(ROOT), str(ROOT / "mlx-motif_b200")):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+METRIC = "12.7B-class q4 decode tok/s at p164 (config[1]); p16k in extra"
+PROMPT_LEN = 164
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=128)
+    ap.add_argument("--warmup", type=int, default=8)
+    ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    ap.add_argument("--cache", choices=["fp16", "q4", "q8"], default="fp16")
+    ap.add_argument("--no-long", action="store_true", help="skip the p16k extras")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--layers", type=int, default=48, help="(debug) model depth; 48 is the benchmark")
+    return ap.parse_args()
+
+
+# --------------------------------------------------------------------------- #
+# clocks during the timed region
+# --------------------------------------------------------------------------- #
+class ClockSampler:
+    QUERY = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.lines: list[str] = []
+        self.t0 = self.t1 = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+                 "-lms", "20"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            threading.Thread(target=self._read, daemon=True).start()
+            time.sleep(0.15)
+        except OSError:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append((time.time(), line.strip()))
+
+    def mark(self, which: str):
+        setattr(self, which, time.time())
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"], "samples": 0}
+        time.sleep(0.1)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        rows = []
+        for ts, line in self.lines:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 10:
+                continue
+            rows.append((ts, parts))
+        inside = [r for r in rows if self.t0 is not None and self.t0 - 0.02 <= r[0] <= self.t1 + 0.02]
+        use = inside or rows
+        if not use:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"], "samples": 0}
+        sm = [float(p[2]) for _, p in use if p[2].replace(".", "").isdigit()]
+        smax = [float(p[3]) for _, p in use if p[3].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for _, p in use for i in range(4) if p[6 + i].lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(smax) if smax else None,
+                "reasons": reasons, "samples": len(use), "samples_inside_timed_region": len(inside)}
+
+
+# --------------------------------------------------------------------------- #
+# distributed plumbing
+# --------------------------------------------------------------------------- #
+def dist_setup(n_gpus: int):
+    import torch
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != n_gpus:
+        raise SystemExit(f"--gpus {n_gpus} but WORLD_SIZE={world}: launch N>1 with torchrun")
+    group = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180),
+                                device_id=torch.device("cuda", local))
+        group = dist.group.WORLD
+    return rank, world, local, group
+
+
+def max_over_ranks(v: float, world: int) -> float:
+    if world == 1:
+        return v
+    import torch
+    import torch.distributed as dist
+
+    t = torch.tensor([v], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(world: int):
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+# --------------------------------------------------------------------------- #
+# CPU baseline: the oracle on one full-size layer, scaled to a token
+# --------------------------------------------------------------------------- #
+class CpuOracleSample:
+    """The numpy oracle's decode of one full-size GDA layer at kv_len (weights built once),
+    scaled to a token: 48 layers plus lm_head at the layer's measured per-weight GEMV rate."""
+
+    def __init__(self, threads: int = 1, kv_len: int = PROMPT_LEN + 1):
+        import concurrent.futures as cf
+
+        import numpy as np
+
+        import oracle as O
+
+        self.O = O
+        self._orig = O.motif_oracle.quantized_matmul
+        self.threads = threads
+        self.kv_len = kv_len
+        args = O.OracleArgs(num_hidden_layers=1, vocab_size=1000)
+        rng = np.random.default_rng(0)
+        self.w = O.make_synthetic_weights(args, seed=0)
+        self.L = self.w["layers"][0]
+        self.orc = O.GroupedDecodeOracle(args, self.w)
+        d = args.head_dim
+        self.hist = [(rng.standard_normal((1, 8, kv_len - 1, d)) * 0.5).astype(np.float16) for _ in range(4)]
+        self.h = (rng.standard_normal((1, args.hidden_size)) * 0.5).astype(np.float16)
+        self.x = rng.standard_normal((1, args.hidden_size)).astype(np.float16)
+        self.pool = cf.ThreadPoolExecutor(threads) if threads > 1 else None
+        self.layer_weights = sum(self.L[k][0].size * 8 for k in ("qkv", "o", "gate", "up", "down"))
+
+    def _qmm(self, x, data, scales, biases, group_size=64, bits=4):
+        g, b = group_size, bits
+        import numpy as np
+
+        if self.pool is None:
+            return self._orig(x, data, scales, biases, g, b)
+        n = data.shape[0]
+        cuts = np.linspace(0, n, self.threads + 1).astype(int)
+        parts = self.pool.map(lambda ab: self._orig(
+            x, data[ab[0]:ab[1]], scales[ab[0]:ab[1]], biases[ab[0]:ab[1]], g, b), list(zip(cuts[:-1], cuts[1:])))
+        return np.concatenate(list(parts), axis=-1)
+
+    def seconds_per_token(self) -> float:
+        import oracle.motif_oracle as M
+
+        cache = self.orc.caches[0]
+        cache.k1 = cache.k2 = cache.v1 = cache.v2 = None
+        cache.offset = 0
+        cache.update_and_fetch_4(*self.hist)
+        orig = M.quantized_matmul
+        M.quantized_matmul = self._qmm  # the layer's GEMVs run on the thread pool
+        try:
+            t0 = time.perf_counter()
+            self.orc.layer(0, self.h)
+            t_layer = time.perf_counter() - t0
+            t0 = time.perf_counter()
+            self._qmm(self.x, *self.L["gate"])
+            t_gate = time.perf_counter() - t0
+        finally:
+            M.quantized_matmul = orig
+        per_weight = t_gate / (self.L["gate"][0].size * 8)
+        self.t_layer = t_layer
+        return 48 * t_layer + 219520 * 4096 * per_weight
+
+    def describe(self) -> str:
+        return (f"numpy oracle decode of 1 of 48 full-size layers at kv_len {self.kv_len} "
+                f"({self.layer_weights / 1e6:.0f}M q4 weights, {self.t_layer:.2f} s) scaled x48, plus lm_head "
+                f"(219520x4096) at the layer's measured GEMV rate; {self.threads} thread(s)")
+
+    def close(self):
+        if self.pool:
+            self.pool.shutdown()
+
+
+def cpu_baseline(threads: int = 1) -> dict:
+    s = CpuOracleSample(threads)
+    t = s.seconds_per_token()
+    out = {"value": 1.0 / t, "unit": "tok/s", "cores": threads, "kind": "port", "sample": s.describe()}
+    s.close()
+    return out
+
+
+# --------------------------------------------------------------------------- #
+# B200 arm
+# --------------------------------------------------------------------------- #
+def time_gemvs(model, reps: int = 3) -> dict:
+    """CUDA-event time of one step's GEMV launches (every layer's qkv, o, gate|up, down + lm_head)."""
+    import torch
+
+    lins = [(L[k], inp) for L in model.layers for k, inp in
+            (("qkv", model.x), ("o", model.attn), ("gate_up", model.x), ("down", model.act))]
+    lins.append((model.lm_head, model.x))
+    outs = {id(q): torch.empty(q.out_dim, dtype=torch.float16, device=model.device) for q, _ in lins}
+    alg = 0
+    for q, _ in lins:
+        alg += q.nbytes() + 2 * q.in_dim + 2 * q.out_dim
+    for q, inp in lins:  # warm
+        q(inp[: q.in_dim], out=outs[id(q)], workspace=model.lin_ws)
+    torch.cuda.synchronize()
+    st = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    best = math.inf
+    for _ in range(reps):
+        e0.record(st)
+        for q, inp in lins:
+            q(inp[: q.in_dim], out=outs[id(q)], workspace=model.lin_ws)
+        e1.record(st)
+        e1.synchronize()
+        best = min(best, e0.elapsed_time(e1))
+    n = len(lins)
+    return {"launches": n, "ms_total": best, "ms_per_launch": best / n, "bytes_total": alg,
+            "bytes_per_launch": alg / n, "gbs": alg / (best / 1e3) / 1e9}
+
+
+def time_attention(model, reps: int = 5) -> dict:
+    """CUDA-event time of the 48 layers' fused attention (2 kernels each) at the current kv_len."""
+    import torch
+
+    from mlx_motif._native import check, lib, ptr, stream
+
+    kv_len = int(model.pos_len[1].item())
+    st = stream(model.device)
+    kvl_p = model.pos_len.data_ptr() + 4
+
+    def run():
+        for li, L in enumerate(model.layers):
+            check(lib.motif_gda_decode_attention(ptr(model.q), model._slots[li], model.scale, model.q_groups, model.gr,
+                                                 0, kvl_p, ptr(L["subln"]), ptr(L["lambda_full"]),
+                                                 L["lambda_full"].numel(), L["lambda_init"], 1e-5, ptr(model.attn),
+                                                 ptr(model.attn_ws), model.attn_ws_bytes, st))
+
+    run()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    best = math.inf
+    for _ in range(reps):
+        e0.record()
+        run()
+        e1.record()
+        e1.synchronize()
+        best = min(best, e0.elapsed_time(e1))
+    kv_bytes = model.kv_bytes_per_token(kv_len)
+    return {"kv_len": kv_len, "ms_48_layers": best, "bytes": kv_bytes, "gbs": kv_bytes / (best / 1e3) / 1e9}
+
+
+def read_traffic() -> float | None:
+    """ncu DRAM bytes per q4-GEMV launch, from the committed profile summary (None if absent)."""
+    p = ROOT / "profiles" / "q4_gemv_decode_step.txt"
+    if not p.exists():
+        return None
+    for line in p.read_text().splitlines():
+        if line.startswith("traffic_bytes_per_launch:"):
+            try:
+                return float(line.split(":", 1)[1].split()[0])
+            except ValueError:
+                return None
+    return None
+
+
+def peaks() -> tuple[float, str]:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        return float(json.loads(p.read_text())["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def run_b200(a) -> None:
+    import numpy as np
+    import torch
+
+    from mlx_motif.model import ModelArgs, MotifDecoder
+
+    rank, world, local, group = dist_setup(a.gpus)
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    margin = a.warmup * 2 + a.steps * 2 + 16
+    args = ModelArgs(num_hidden_layers=a.layers)
+    t_init = time.time()
+    model = MotifDecoder.random(args, seed=0, cache=a.cache, max_seq=PROMPT_LEN + margin + 8, device=dev,
+                                tp_group=group, rank=rank, world=world)
+    torch.cuda.synchronize()
+    t_init = time.time() - t_init
+    prompt = np.random.default_rng(0).integers(0, args.vocab_size, PROMPT_LEN).tolist()
+    model.prefill(prompt)
+    for _ in range(a.warmup):
+        model.step_device()
+    torch.cuda.synchronize()
+    barrier(world)
+
+    sampler = ClockSampler(local) if rank == 0 else None
+    if sampler:
+        sampler.start()
+    st = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier(world)
+    torch.cuda.synchronize()
+    if sampler:
+        sampler.mark("t0")
+    e0.record(st)
+    for _ in range(a.steps):
+        model.step_device()
+    e1.record(st)
+    torch.cuda.synchronize()
+    if sampler:
+        sampler.mark("t1")
+    barrier(world)
+    ms = max_over_ranks(e0.elapsed_time(e1), world)
+    clocks = sampler.stop() if sampler else None
+    value = a.steps / (ms / 1e3)
+    kv_mid = PROMPT_LEN + a.warmup + a.steps // 2
+    bytes_per_step = model.weight_bytes * world + model.kv_bytes_per_token(kv_mid) * world
+
+    # ---- e2e through the public per-token API (host buffers) ----
+    tok = int(model.token.item())
+    for _ in range(a.warmup):
+        tok = model.decode_host(tok)
+    barrier(world)
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for _ in range(a.steps):
+        tok = model.decode_host(tok)
+    e2e_s = max_over_ranks(time.perf_counter() - t0, world)
+    e2e = {"value": a.steps / e2e_s, "unit": "tok/s", "h2d_bytes_per_step": 4, "d2h_bytes_per_step": 4}
+
+    # ---- dominant kernel roofline (q4 GEMV), measured live ----
+    gem = time_gemvs(model)
+    peak, peak_kind = peaks()
+    traffic = read_traffic()
+    roofline = {"bound": "hbm", "kernel": "motif_quantized_linear (q4 GEMV, all 193 launches of a step)",
+                "achieved": round(gem["gbs"], 1), "peak": peak, "peak_kind": peak_kind, "unit": "GB/s",
+                "frac": round(gem["gbs"] / peak, 4), "traffic": traffic,
+                "bytes_per_launch": round(gem["bytes_per_launch"]), "ms_per_launch": round(gem["ms_per_launch"], 5)}
+    attn_p164 = time_attention(model)
+    step_frac = bytes_per_step / world / (ms / a.steps / 1e3) / 1e9 / peak
+
+    extra = {"weights_gb": round(model.weight_bytes * world / 1e9, 3), "init_s": round(t_init, 1),
+             "step_hbm_gbs_per_gpu": round(bytes_per_step / world / (ms / a.steps / 1e3) / 1e9, 1),
+             "step_frac_of_peak": round(step_frac, 4), "attention_p164": attn_p164,
+             "gemv": {k: (round(v, 4) if isinstance(v, float) else v) for k, v in gem.items()}}
+
+    # ---- config[2]: p16k with q4 and fp16 caches ----
+    if not a.no_long:
+        weights = model.weights_dict()
+        del model
+        torch.cuda.empty_cache()
+        for kind in ("q4", "fp16"):
+            m = MotifDecoder(args, weights, cache=kind, max_seq=16000 + a.warmup + a.steps + 8, device=dev,
+                             tp_group=group)
+            m.fill_cache_synthetic(16000, seed=1)
+            m.token.fill_(1)
+            for _ in range(a.warmup):
+                m.step_device()
+            torch.cuda.synchronize()
+            barrier(world)
+            e0.record(st)
+            for _ in range(a.steps):
+                m.step_device()
+            e1.record(st)
+            torch.cuda.synchronize()
+            barrier(world)
+            lms = max_over_ranks(e0.elapsed_time(e1), world)
+            att = time_attention(m)
+            extra[f"p16k_{kind}"] = {
+                "tok_s": round(a.steps / (lms / 1e3), 2), "ms_per_step": round(lms / a.steps, 4),
+                "attention_gbs": round(att["gbs"], 1), "attention_frac": round(att["gbs"] / peak, 4),
+                "attention_ms_per_step": round(att["ms_48_layers"], 4),
+                "peak_hbm_bytes": int(torch.cuda.max_memory_allocated(dev)),
+            }
+            del m
+            torch.cuda.empty_cache()
+
+    cpu = None
+    if rank == 0 and world == 1 and not a.no_cpu_baseline:
+        cpu = cpu_baseline(threads=1)
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": "tok/s", "n_gpus": world, "steps": a.steps,
+            "warmup": a.warmup, "ms_per_step": round(ms / a.steps, 4), "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "fp16 activations, q4 g64 weights, fp32 accumulate",
+            "data": "synthetic: random-init weights (std 0.02) and random prompt ids",
+            "config": {"workload": f"config[1]: 12.7B-class GDA q4, p{PROMPT_LEN} prompt then greedy decode, "
+                                   f"{a.cache} 4-slot cache, batch 1",
+                       "model": "motif-12.7B-class (48L, H4096, 24+8 q heads, 8 kv/slot, I14336, V219520)",
+                       "global_batch": 1, "seq_len": PROMPT_LEN, "parallelism": f"tp{world}" if world > 1 else "single",
+                       "l2": "inputs larger than L2: 6.85 GB of weights stream from HBM every step"},
+            "e2e": e2e, "gpu_launches": model_launches(args, world) * a.steps,
+            "roofline": roofline, "cpu_baseline": cpu, "clocks": clocks, "extra": extra,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+
+
+def model_launches(args, world: int) -> int:
+    """Kernels of this library per decode step (torch's one-element position increment excluded)."""
+    from mlx_motif._native import lib
+
+    H, d = args.hidden_size, args.d
+    qkv_n = (args.q_heads * d + 4 * args.k_noise_heads * d) // world
+    shapes = [(qkv_n, H), (H, args.q_origin * 2 * d // world), (2 * args.intermediate_size // world, H),
+              (H, args.intermediate_size // world)]
+    per_layer = 0
+    for n, k in shapes:
+        per_layer += 1 + (1 if lib.motif_quantized_linear_workspace_bytes(1, n, k, 4, 64) > 0 else 0)
+    per_layer += 1 + 2 + 1 + 1 + 1  # rope+append, attention (2), add_rms, polynorm_mul, add_rms
+    head = 1 + (1 if lib.motif_quantized_linear_workspace_bytes(1, args.vocab_size, H, 4, 64) > 0 else 0) + 2
+    return 1 + args.num_hidden_layers * per_layer + head
+
+
+# --------------------------------------------------------------------------- #
+# reference arm: the CPU oracle port
+# --------------------------------------------------------------------------- #
+def run_reference(a) -> None:
+    """Reference arm: the oracle port on all host cores; each step is one full-size layer
+    sample scaled to a token. Stops early (reporting the steps done) after ~150 s."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    threads = os.cpu_count() or 1
+    sampler = CpuOracleSample(threads)
+    for _ in range(min(a.warmup, 1)):
+        sampler.seconds_per_token()
+    secs = []
+    t_start = time.perf_counter()
+    for _ in range(a.steps):
+        secs.append(sampler.seconds_per_token())
+        if time.perf_counter() - t_start > 150:
+            break
+    value = len(secs) / sum(secs)
+    line = {
+        "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": a.gpus, "steps": len(secs),
+        "warmup": a.warmup, "ms_per_step": 1e3 / value, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "fp16 storage, float64 compute", "data": "synthetic",
+        "impl": "reference",
+        "config": {"workload": f"config[1]: 12.7B-class GDA q4, p{PROMPT_LEN}, fp16 4-slot cache, batch 1",
+                   "model": "motif-12.7B-class", "global_batch": 1, "seq_len": PROMPT_LEN,
+                   "parallelism": "host cores"},
+        "cpu_baseline": {"value": value, "unit": "tok/s", "cores": threads, "kind": "port",
+                         "sample": sampler.describe() + " (MLX, the reference's own runtime, is not installable "
+                                                        "in this image; the oracle port stands in)"},
+        "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    sampler.close()
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    a = parse_args()
+    if a.impl == "reference":
+        run_reference(a)
+    else:
+        run_b200(a)
+
+
+if __name__ == "__main__":
+    main()

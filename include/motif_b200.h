@@ -1,0 +1,220 @@
+/*
+ * motif_b200.h — C ABI of the B200 (sm_100a) Motif decode hot path.
+ *
+ * Plain extern "C" entry points: raw device pointers, element counts, a
+ * cudaStream_t passed as void*, and an int status return (MOTIF_OK on
+ * success). No C++ or framework types cross this boundary, so the Python
+ * package (ctypes), a Swift MotifKit layer or any C caller binds it the same
+ * way. All kernels are asynchronous on the given stream; inputs are read-only
+ * unless a parameter says otherwise.
+ *
+ * Each declaration cites the reference interface it replaces (paths relative
+ * to the junhoyeo/mlx-motif project root). The reference's operator layer is
+ * src/mlx_motif/kernels/__init__.py:21-50; its cache API is
+ * src/mlx_motif/cache.py.
+ *
+ * Runtime lengths: every KV length / cache offset can be given either as a
+ * host integer or as a device int32 pointer (non-NULL pointer wins). The
+ * device form keeps the value out of the launch, so a captured CUDA graph
+ * replays at every length (the reference passes the length as a runtime
+ * kernel input for the same reason, attention.py:42-51).
+ */
+#ifndef MOTIF_B200_H
+#define MOTIF_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define MOTIF_API __attribute__((visibility("default")))
+#else
+#define MOTIF_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes ------------------------------------------------------ */
+#define MOTIF_OK 0
+#define MOTIF_ERR_NULL 1          /* a required pointer is NULL            */
+#define MOTIF_ERR_BAD_SHAPE 2     /* shapes inconsistent / out of range    */
+#define MOTIF_ERR_BAD_CONTRACT 3  /* shape outside the kernel contract     */
+#define MOTIF_ERR_DTYPE 4         /* dtype / bits not supported            */
+#define MOTIF_ERR_CUDA 5          /* a CUDA runtime call failed            */
+#define MOTIF_ERR_WORKSPACE 6     /* workspace missing or too small        */
+
+/* ---- element types ----------------------------------------------------- */
+#define MOTIF_F16 0
+#define MOTIF_BF16 1
+#define MOTIF_F32 2
+
+/* Human-readable name of a status code. */
+MOTIF_API const char* motif_status_string(int status);
+/* Detail message of the last failed call on this host thread ("" if none). */
+MOTIF_API const char* motif_last_error(void);
+/* ABI version (bumped on any signature change). */
+MOTIF_API int motif_abi_version(void);
+
+/* ---- 4-slot KV cache view ------------------------------------------------
+ * The four slots k1, k2, v1, v2 of one layer (cache.py:303-545), each
+ * (batch, heads, capacity, head_dim) row-contiguous. bits == 16: data[i] are
+ * fp16/bf16 rows. bits == 4 or 8: data[i] are packed uint32
+ * (…, head_dim*bits/32) and scales[i]/biases[i] are (…, head_dim/group_size)
+ * in the activation dtype (the MLX affine triple, cache.py:430-436). */
+typedef struct motif_kv4_slots {
+  void* data[4];
+  void* scales[4];
+  void* biases[4];
+  int32_t bits;
+  int32_t group_size;
+  int64_t batch;
+  int64_t heads;
+  int64_t capacity;
+  int64_t head_dim;
+} motif_kv4_slots;
+
+/* ---- PolyNorm -------------------------------------------------------------
+ * y = w0*x^3/rms(x^3) + w1*x^2/rms(x^2) + w2*x/rms(x) + b over the last axis.
+ * Replaces mlx_motif.kernels.polynorm (src/mlx_motif/kernels/mlp.py:119-157).
+ * x, y: (rows, dim); weight (3,), bias (1,) in dtype. */
+MOTIF_API int motif_polynorm(int dtype, const void* x, const void* weight, const void* bias, float eps,
+                   int64_t rows, int64_t dim, void* y, void* stream);
+
+/* act = polynorm(gate) * up, the MLP activation of MotifMLP.__call__
+ * (src/mlx_motif/model.py:267-268). gate/up rows are `in_stride` elements
+ * apart (so a fused [gate | up] GEMV output can be passed as two views). */
+MOTIF_API int motif_polynorm_mul(int dtype, const void* gate, const void* up, int64_t in_stride,
+                       const void* weight, const void* bias, float eps, int64_t rows, int64_t dim,
+                       void* y, void* stream);
+
+/* ---- GDA post reduction -----------------------------------------------------
+ * y = (o − λ·n[h/gr]) · rsqrt(mean(d²) + eps) · subln_w · (1 − λ_init).
+ * Replaces gda_post_split (src/mlx_motif/kernels/gda.py:223-282).
+ * attn_o (B, q_groups*gr, S, C), attn_n (B, q_groups, S, C), subln_w (C,) in
+ * dtype; lambda_full fp32 device array of lambda_len ∈ {1, q_groups,
+ * q_groups*gr} values (1 = the reference's per-layer scalar). */
+MOTIF_API int motif_gda_post_split(int dtype, const void* attn_o, const void* attn_n, const void* subln_w,
+                         const float* lambda_full, int64_t lambda_len, float lambda_init,
+                         int64_t batch, int64_t q_groups, int64_t gr, int64_t seq, int64_t channels,
+                         float eps, void* y, void* stream);
+
+/* Same on the concatenated (origin | noise) input merged (B, q_groups*(gr+1), S, C).
+ * Replaces gda_post (src/mlx_motif/kernels/gda.py:285-341). */
+MOTIF_API int motif_gda_post(int dtype, const void* merged, const void* subln_w, const float* lambda_full,
+                   int64_t lambda_len, float lambda_init, int64_t batch, int64_t q_groups,
+                   int64_t gr, int64_t seq, int64_t channels, float eps, void* y, void* stream);
+
+/* ---- shared-QK dual-V decode attention ------------------------------------
+ * y = cat[softmax(q kᵀ·scale)·v1, softmax(q kᵀ·scale)·v2] with GQA broadcast
+ * (q head h reads kv head h / (h_q/h_kv)); rows ≥ kv_len are never read.
+ * Replaces sdpa_dual_v (src/mlx_motif/kernels/attention.py:190-260).
+ * q (B, h_q, 1, D); k, v1, v2 (B, h_kv, kv_cap, D); y (B, h_q, 1, 2D).
+ * Split-KV: the workspace holds per-split partials; pass workspace_bytes = 0
+ * for a single split (no workspace). */
+MOTIF_API size_t motif_sdpa_dual_v_workspace_bytes(int64_t batch, int64_t h_q, int64_t head_dim,
+                                         int64_t max_splits);
+MOTIF_API int motif_sdpa_dual_v(int dtype, const void* q, const void* k, const void* v1, const void* v2,
+                      float scale, int64_t batch, int64_t h_q, int64_t h_kv, int64_t kv_cap,
+                      int64_t head_dim, int64_t kv_len, const int32_t* kv_len_dev, void* y,
+                      void* workspace, size_t workspace_bytes, void* stream);
+
+/* Same attention reading MLX affine-quantized K, V1, V2 triples directly
+ * (bits 4 or 8). Replaces sdpa_dual_v_q4 (attention.py:510-645) with the same
+ * shape contract (attention.py:556-608): D % 32 == 0, D % group_size == 0,
+ * (32/bits) % (D/32) == 0 and group_size % (D/32) == 0. */
+MOTIF_API int motif_sdpa_dual_v_q(int dtype, int bits, int group_size, const void* q,
+                        const uint32_t* k_data, const void* k_scales, const void* k_biases,
+                        const uint32_t* v1_data, const void* v1_scales, const void* v1_biases,
+                        const uint32_t* v2_data, const void* v2_scales, const void* v2_biases,
+                        float scale, int64_t batch, int64_t h_q, int64_t h_kv, int64_t kv_cap,
+                        int64_t head_dim, int64_t kv_len, const int32_t* kv_len_dev, void* y,
+                        void* workspace, size_t workspace_bytes, void* stream);
+
+/* One GDA decode layer's attention block in one pass over the 4-slot cache:
+ * both sdpa_dual_v calls of MotifAttention._forward_grouped (model.py:716-768;
+ * origin heads with k1, noise heads with k2, shared v1/v2) plus
+ * gda_post_split, reading every cache row once. fp16 only, batch 1.
+ * q: (q_groups*(gr+1), D) origin-first; out: (q_groups*gr, 2D) — the o_proj
+ * input. cache->bits selects fp16 rows (16) or packed q4/q8. */
+MOTIF_API size_t motif_gda_decode_attention_workspace_bytes(int64_t q_heads, int64_t head_dim,
+                                                  int64_t max_splits);
+MOTIF_API int motif_gda_decode_attention(const void* q, const motif_kv4_slots* cache, float scale,
+                               int64_t q_groups, int64_t gr, int64_t kv_len,
+                               const int32_t* kv_len_dev, const void* subln_w,
+                               const float* lambda_full, int64_t lambda_len, float lambda_init,
+                               float eps, void* out, void* workspace, size_t workspace_bytes,
+                               void* stream);
+
+/* ---- affine quantization ---------------------------------------------------
+ * MLX-layout affine group quantization along the last axis (bits 4 or 8):
+ * data (rows, dim*bits/32) uint32 little-endian, scales/biases
+ * (rows, dim/group_size) in dtype. Replaces the mx.quantize call sites of the
+ * cache (cache.py:399-402, 498). */
+MOTIF_API int motif_quantize(int dtype, int bits, int group_size, const void* x, int64_t rows, int64_t dim,
+                   uint32_t* data, void* scales, void* biases, void* stream);
+/* Inverse, element ch = scale[g]*((data[ch/EL] >> (ch%EL)*bits) & mask) + bias[g].
+ * Replaces _dequant_probe / mx.dequantize (src/mlx_motif/kernels/mlp.py:213-255). */
+MOTIF_API int motif_dequantize(int dtype, int bits, int group_size, const uint32_t* data,
+                     const void* scales, const void* biases, int64_t rows, int64_t dim, void* y,
+                     void* stream);
+
+/* ---- 4-slot cache writes ---------------------------------------------------
+ * Write k1, k2, v1, v2 (B, heads, seq, D) at rows [offset, offset+seq) of the
+ * slots (fp16 copy, or one batched quantize for bits 4/8). Replaces
+ * MotifGroupedKVCache.update_and_fetch_4 (cache.py:337-360) and
+ * MotifGroupedQuantizedKVCache._update_4 (cache.py:485-512); the caller owns
+ * capacity and the offset bookkeeping. */
+MOTIF_API int motif_kv4_append(int dtype, const motif_kv4_slots* cache, const void* k1, const void* k2,
+                     const void* v1, const void* v2, int64_t seq, int64_t offset,
+                     const int32_t* offset_dev, void* stream);
+
+/* Decode prologue of _forward_grouped (model.py:580-657) for batch 1, S = 1:
+ * split the fused qkv row (q_heads + 2*kv2 + 2*kv2 heads of D, Q origin-first,
+ * k/v heads interleaved slot-1/slot-2), apply non-traditional RoPE at position
+ * *pos_dev to q and k, write q to q_out (q_heads, D) and append k1, k2, v1,
+ * v2 at row *pos_dev of the cache. inv_freq: fp32 (D/2,). fp16 only. */
+MOTIF_API int motif_rope_qkv_append(const void* qkv, const float* inv_freq, int64_t q_heads,
+                          const motif_kv4_slots* cache, const int32_t* pos_dev, void* q_out,
+                          void* stream);
+
+/* Non-traditional RoPE on x (B, H, S, D) at positions offset + s (mlx-lm
+ * initialize_rope, traditional=False, as used at model.py:414-420,589-594). */
+MOTIF_API int motif_rope(int dtype, const void* x, int64_t batch, int64_t heads, int64_t seq, int64_t dim,
+               int64_t offset, const int32_t* offset_dev, const float* inv_freq, void* y,
+               void* stream);
+
+/* ---- quantized linear ------------------------------------------------------
+ * y (m, n) = x (m, k) · dequant(W)ᵀ with W in the nn.QuantizedLinear layout:
+ * w (n, k*bits/32) uint32, scales/biases (n, k/group_size) in dtype. Replaces
+ * mx.quantized_matmul behind nn.QuantizedLinear (every linear of the decoder,
+ * model.py:437-442, 262-264, 894; fused qkv 1017-1079). bits 4, group 64;
+ * fp16; m ≤ 8 (decode / verify rows). */
+MOTIF_API size_t motif_quantized_linear_workspace_bytes(int64_t m, int64_t n, int64_t k, int bits,
+                                              int group_size);
+MOTIF_API int motif_quantized_linear(int dtype, int bits, int group_size, const void* x, int64_t m,
+                           int64_t k, const uint32_t* w, const void* scales, const void* biases,
+                           int64_t n, void* y, void* workspace, size_t workspace_bytes,
+                           void* stream);
+
+/* ---- decoder glue (model.py:845-905) ---------------------------------------- */
+/* y = rms_norm(x) * w (nn.RMSNorm, model.py:850-851, 864). */
+MOTIF_API int motif_rms_norm(int dtype, const void* x, const void* w, float eps, int64_t rows, int64_t dim,
+                   void* y, void* stream);
+/* h += delta (residual, model.py:854-855), then y = rms_norm(h) * w. h is in/out. */
+MOTIF_API int motif_add_rms_norm(int dtype, void* h, const void* delta, const void* w, float eps,
+                       int64_t rows, int64_t dim, void* y, void* stream);
+/* h = table[*token_dev] (nn.Embedding, model.py:862/872), y = rms_norm(h) * w. */
+MOTIF_API int motif_embed_rms_norm(int dtype, const int32_t* token_dev, const void* table, int64_t vocab,
+                         int64_t dim, const void* w, float eps, void* h, void* y, void* stream);
+/* Greedy sampler: first index of the maximum of logits (n,) -> *out_index
+ * (argmax at temperature 0 in mlx_lm generate_step). */
+MOTIF_API size_t motif_argmax_workspace_bytes(int64_t n);
+MOTIF_API int motif_argmax(int dtype, const void* logits, int64_t n, int32_t* out_index, void* workspace,
+                 size_t workspace_bytes, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MOTIF_B200_H */

@@ -1,0 +1,585 @@
+// Shared-QK dual-V decode attention, split-KV ("flash-decode") on B200.
+//
+// One CTA owns one (batch, kv head) and one contiguous chunk of KV positions,
+// and serves every query head that reads that kv head: the GQA heads of the
+// generic op, or — in the fused GDA layer path — the gr origin heads (slot
+// k1) plus the noise head (slot k2) of one group. Each cache row (k1, k2, v1,
+// v2) is therefore read from HBM exactly once per layer.
+//
+// Inside a CTA, 8 warps each take 4 consecutive positions per round (16
+// independent loads per lane in flight), a lane owns D/32 channels, scores
+// are warp all-reduced, and the online softmax (base-2, scale·log2e folded
+// into q) updates two V accumulators with one weight. Warps merge through
+// shared memory; splits merge in a second kernel (plain, or fused with the
+// GDA post reduction).
+//
+// Packed caches (bits 4/8, MLX affine triples) are dequantized in registers:
+// a lane's D/32 channels sit in one uint32 and one scale/bias group, the same
+// lane→word contract the reference enforces (attention.py:565-608).
+#include <cmath>
+
+#include "common.cuh"
+
+namespace motif {
+namespace {
+
+constexpr int kAttnThreads = 256;
+constexpr int kAttnWarps = kAttnThreads / 32;
+constexpr int kPosPerWarp = 4;
+constexpr int kRoundPositions = kAttnWarps * kPosPerWarp;  // 32
+constexpr int kMinChunk = 32;
+constexpr float kLog2e = 1.4426950408889634f;
+
+struct AttnArgs {
+  const void* q;
+  int64_t q_bstride;  // elements between batches of q
+  int na;             // A heads per kv head (runtime, <= MAXA)
+  int nb_base;        // head index of the B head of kv head 0
+  int h_out;          // heads per batch in y / workspace indexing
+  const void* kA;
+  const void* kB;
+  const void* v1;
+  const void* v2;
+  const void* kA_s;
+  const void* kA_b;
+  const void* kB_s;
+  const void* kB_b;
+  const void* v1_s;
+  const void* v1_b;
+  const void* v2_s;
+  const void* v2_b;
+  int h_kv;
+  int64_t cap;
+  int gs;
+  int kv_len;
+  const int32_t* kv_len_dev;
+  float scale_log2;
+  int force_partials;
+  void* y;
+  float* ws;
+};
+
+__device__ __forceinline__ void split_range(int kv_len, int nsplit, int split, int& p0, int& p1,
+                                            int& n_active) {
+  int chunk = (kv_len + nsplit - 1) / nsplit;
+  if (chunk < kMinChunk) chunk = kMinChunk;
+  n_active = (kv_len + chunk - 1) / chunk;
+  p0 = split * chunk;
+  p1 = min(kv_len, p0 + chunk);
+}
+
+template <typename T, int D, int BITS>
+__device__ __forceinline__ void load_kv(const void* data, const void* sc, const void* bi, int64_t row,
+                                        int lane, int gs, float (&out)[D / 32]) {
+  constexpr int CPL = D / 32;
+  if constexpr (BITS == 16) {
+    load_vec<T, CPL>(static_cast<const T*>(data) + row * D + lane * CPL, out);
+  } else {
+    constexpr int EL = 32 / BITS;
+    constexpr int WPR = D / EL;
+    constexpr uint32_t MASK = (1u << BITS) - 1u;
+    const int ch0 = lane * CPL;
+    const uint32_t w = __ldg(static_cast<const uint32_t*>(data) + row * WPR + ch0 / EL);
+    const int shift = (ch0 % EL) * BITS;
+    const int64_t g = row * (D / gs) + ch0 / gs;
+    const float s = to_f<T>(static_cast<const T*>(sc)[g]);
+    const float b = to_f<T>(static_cast<const T*>(bi)[g]);
+#pragma unroll
+    for (int j = 0; j < CPL; ++j) out[j] = s * (float)((w >> (shift + j * BITS)) & MASK) + b;
+  }
+}
+
+template <typename T, int D, int BITS, int MAXA, int NB>
+__global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(AttnArgs a) {
+  constexpr int CPL = D / 32;
+  constexpr int NH = MAXA + NB;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int split = blockIdx.x, nsplit = gridDim.x;
+  const int b = blockIdx.y / a.h_kv, hk = blockIdx.y % a.h_kv;
+  const int kv_len = a.kv_len_dev ? *a.kv_len_dev : a.kv_len;
+  int p0, p1, n_active;
+  split_range(kv_len, nsplit, split, p0, p1, n_active);
+  if (nsplit > 1 && split >= n_active) return;
+
+  int head[NH];
+  bool valid[NH];
+#pragma unroll
+  for (int h = 0; h < MAXA; ++h) {
+    head[h] = hk * a.na + h;
+    valid[h] = h < a.na;
+  }
+  if constexpr (NB > 0) {
+    head[MAXA] = a.nb_base + hk;
+    valid[MAXA] = true;
+  }
+
+  float q[NH][CPL];
+  const T* qb = static_cast<const T*>(a.q) + (int64_t)b * a.q_bstride;
+#pragma unroll
+  for (int h = 0; h < NH; ++h) {
+    if (valid[h]) {
+      load_vec<T, CPL>(qb + (int64_t)head[h] * D + lane * CPL, q[h]);
+#pragma unroll
+      for (int c = 0; c < CPL; ++c) q[h][c] *= a.scale_log2;
+    } else {
+#pragma unroll
+      for (int c = 0; c < CPL; ++c) q[h][c] = 0.f;
+    }
+  }
+
+  float m[NH], l[NH], o1[NH][CPL], o2[NH][CPL];
+#pragma unroll
+  for (int h = 0; h < NH; ++h) {
+    m[h] = -INFINITY;
+    l[h] = 0.f;
+#pragma unroll
+    for (int c = 0; c < CPL; ++c) o1[h][c] = o2[h][c] = 0.f;
+  }
+
+  const int64_t row0 = ((int64_t)b * a.h_kv + hk) * a.cap;
+  for (int base = p0 + warp * kPosPerWarp; base < p1; base += kRoundPositions) {
+    float ka[kPosPerWarp][CPL], kb[kPosPerWarp][CPL], x1[kPosPerWarp][CPL], x2[kPosPerWarp][CPL];
+#pragma unroll
+    for (int u = 0; u < kPosPerWarp; ++u) {
+      if (base + u < p1) {
+        const int64_t r = row0 + base + u;
+        load_kv<T, D, BITS>(a.kA, a.kA_s, a.kA_b, r, lane, a.gs, ka[u]);
+        if constexpr (NB > 0) load_kv<T, D, BITS>(a.kB, a.kB_s, a.kB_b, r, lane, a.gs, kb[u]);
+        load_kv<T, D, BITS>(a.v1, a.v1_s, a.v1_b, r, lane, a.gs, x1[u]);
+        load_kv<T, D, BITS>(a.v2, a.v2_s, a.v2_b, r, lane, a.gs, x2[u]);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < kPosPerWarp; ++u) {
+      if (base + u >= p1) break;
+      float s[NH];
+#pragma unroll
+      for (int h = 0; h < MAXA; ++h) {
+        float t = 0.f;
+#pragma unroll
+        for (int c = 0; c < CPL; ++c) t += q[h][c] * ka[u][c];
+        s[h] = t;
+      }
+      if constexpr (NB > 0) {
+        float t = 0.f;
+#pragma unroll
+        for (int c = 0; c < CPL; ++c) t += q[MAXA][c] * kb[u][c];
+        s[MAXA] = t;
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+#pragma unroll
+        for (int h = 0; h < NH; ++h) s[h] += __shfl_xor_sync(0xffffffffu, s[h], o);
+      }
+#pragma unroll
+      for (int h = 0; h < NH; ++h) {
+        const float mn = fmaxf(m[h], s[h]);
+        const float fac = exp2f(m[h] - mn);
+        const float e = exp2f(s[h] - mn);
+        m[h] = mn;
+        l[h] = l[h] * fac + e;
+#pragma unroll
+        for (int c = 0; c < CPL; ++c) {
+          o1[h][c] = o1[h][c] * fac + e * x1[u][c];
+          o2[h][c] = o2[h][c] * fac + e * x2[u][c];
+        }
+      }
+    }
+  }
+
+  // ---- merge the warps' partial softmax states through shared memory ----
+  extern __shared__ float smem[];
+  float* sm_ml = smem;                          // [warp][h][2]
+  float* sm_o = smem + kAttnWarps * NH * 2;     // [warp][h][2D]
+#pragma unroll
+  for (int h = 0; h < NH; ++h) {
+    if (lane == 0) {
+      sm_ml[(warp * NH + h) * 2 + 0] = m[h];
+      sm_ml[(warp * NH + h) * 2 + 1] = l[h];
+    }
+    float* dst = sm_o + (int64_t)(warp * NH + h) * 2 * D + lane * CPL;
+#pragma unroll
+    for (int c = 0; c < CPL; ++c) {
+      dst[c] = o1[h][c];
+      dst[D + c] = o2[h][c];
+    }
+  }
+  __syncthreads();
+  const bool partial = nsplit > 1 || a.force_partials;
+  for (int it = threadIdx.x; it < NH * 2 * D; it += kAttnThreads) {
+    const int h = it / (2 * D);
+    const int ch = it - h * 2 * D;
+    if (h < MAXA && h >= a.na) continue;
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < kAttnWarps; ++w) M = fmaxf(M, sm_ml[(w * NH + h) * 2]);
+    float L = 0.f, O = 0.f;
+    if (M != -INFINITY) {
+#pragma unroll
+      for (int w = 0; w < kAttnWarps; ++w) {
+        const float mw = sm_ml[(w * NH + h) * 2];
+        if (mw == -INFINITY) continue;
+        const float f = exp2f(mw - M);
+        L += sm_ml[(w * NH + h) * 2 + 1] * f;
+        O += sm_o[(int64_t)(w * NH + h) * 2 * D + ch] * f;
+      }
+    }
+    int hh;
+    if constexpr (NB > 0) hh = (h == MAXA) ? a.nb_base + hk : hk * a.na + h;
+    else hh = hk * a.na + h;
+    const int64_t bh = (int64_t)b * a.h_out + hh;
+    if (partial) {
+      float* p = a.ws + (bh * nsplit + split) * (2 * D + 2);
+      p[2 + ch] = O;
+      if (ch == 0) {
+        p[0] = M;
+        p[1] = L;
+      }
+    } else {
+      static_cast<T*>(a.y)[bh * 2 * D + ch] = from_f<T>(L > 0.f ? O / L : 0.f);
+    }
+  }
+}
+
+// Merge split partials into the final (B, h_out, 2D) output.
+template <typename T, int D>
+__global__ void attn_combine_kernel(const float* __restrict__ ws, int nsplit, int kv_len_host,
+                                    const int32_t* __restrict__ kv_len_dev, T* __restrict__ y) {
+  const int64_t bh = blockIdx.x;
+  const int ch = threadIdx.x;
+  const int kv_len = kv_len_dev ? *kv_len_dev : kv_len_host;
+  int p0, p1, n_active;
+  split_range(kv_len, nsplit, 0, p0, p1, n_active);
+  const float* base = ws + bh * nsplit * (2 * D + 2);
+  float M = -INFINITY;
+  for (int s = 0; s < n_active; ++s) M = fmaxf(M, base[s * (2 * D + 2)]);
+  float L = 0.f, O = 0.f;
+  for (int s = 0; s < n_active; ++s) {
+    const float* p = base + s * (2 * D + 2);
+    if (p[0] == -INFINITY) continue;
+    const float f = exp2f(p[0] - M);
+    L += p[1] * f;
+    O += p[2 + ch] * f;
+  }
+  y[bh * 2 * D + ch] = from_f<T>(L > 0.f ? O / L : 0.f);
+}
+
+// Merge split partials of one GDA group and apply gda_post_split:
+// out[h_o] = (o − λ·n) · rsqrt(mean d² + eps) · w · (1 − λ_init), with the
+// attention outputs rounded through fp16 first (the reference materialises
+// them as fp16 arrays between the two kernels).
+template <int D, int GR>
+__global__ void gda_combine_kernel(const float* __restrict__ ws, int nsplit, int kv_len_host,
+                                   const int32_t* __restrict__ kv_len_dev, int q_origin,
+                                   const __half* __restrict__ subln_w,
+                                   const float* __restrict__ lam, int lam_mode, float out_scale,
+                                   float eps, __half* __restrict__ out) {
+  __shared__ float scratch[32 * GR];
+  const int g = blockIdx.x;
+  const int ch = threadIdx.x;  // 0 .. 2D-1
+  const int kv_len = kv_len_dev ? *kv_len_dev : kv_len_host;
+  int p0, p1, n_active;
+  split_range(kv_len, nsplit, 0, p0, p1, n_active);
+  float val[GR + 1];
+#pragma unroll
+  for (int j = 0; j <= GR; ++j) {
+    const int head = j < GR ? g * GR + j : q_origin + g;
+    const float* base = ws + (int64_t)head * nsplit * (2 * D + 2);
+    float M = -INFINITY;
+    for (int s = 0; s < n_active; ++s) M = fmaxf(M, base[s * (2 * D + 2)]);
+    float L = 0.f, O = 0.f;
+    for (int s = 0; s < n_active; ++s) {
+      const float* p = base + s * (2 * D + 2);
+      if (p[0] == -INFINITY) continue;
+      const float f = exp2f(p[0] - M);
+      L += p[1] * f;
+      O += p[2 + ch] * f;
+    }
+    val[j] = round_through<__half>(L > 0.f ? O / L : 0.f);
+  }
+  float d[GR], ssq[GR];
+#pragma unroll
+  for (int j = 0; j < GR; ++j) {
+    const int h_o = g * GR + j;
+    const float l = lam[lam_mode == 0 ? 0 : (lam_mode == 1 ? g : h_o)];
+    d[j] = val[j] - l * val[GR];
+    ssq[j] = d[j] * d[j];
+  }
+  block_sum<GR>(ssq, scratch);
+  const float w = __half2float(subln_w[ch]);
+#pragma unroll
+  for (int j = 0; j < GR; ++j) {
+    const float inv = rsqrtf(ssq[j] / (float)(2 * D) + eps);
+    out[(int64_t)(g * GR + j) * 2 * D + ch] = __float2half_rn(d[j] * inv * w * out_scale);
+  }
+}
+
+template <typename T, int D, int BITS, int MAXA, int NB>
+int launch_split(const AttnArgs& a, int nsplit, int batch, cudaStream_t st) {
+  constexpr int NH = MAXA + NB;
+  const size_t smem = sizeof(float) * (size_t)kAttnWarps * NH * (2 + 2 * D);
+  auto kern = attn_split_kernel<T, D, BITS, MAXA, NB>;
+  static bool configured = false;  // one attribute call per instantiation
+  if (!configured) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return fail(MOTIF_ERR_CUDA, "attention: smem attribute: %s", cudaGetErrorString(e));
+    configured = true;
+  }
+  dim3 grid(nsplit, batch * a.h_kv);
+  kern<<<grid, kAttnThreads, smem, st>>>(a);
+  return check_launch("attention split");
+}
+
+template <typename T, int D, int BITS>
+int dispatch_generic(AttnArgs& a, int G, int nsplit, int batch, cudaStream_t st) {
+  if (G == 1) return launch_split<T, D, BITS, 1, 0>(a, nsplit, batch, st);
+  if (G <= 4) return launch_split<T, D, BITS, 4, 0>(a, nsplit, batch, st);
+  return launch_split<T, D, BITS, 8, 0>(a, nsplit, batch, st);
+}
+
+int choose_splits(int64_t groups, int64_t len_bound, int64_t max_splits) {
+  // Aim for ~2 CTAs per SM across 148 SMs, never below kMinChunk positions per split.
+  int64_t want = ceil_div(296, groups < 1 ? 1 : groups);
+  int64_t by_len = ceil_div(len_bound < 1 ? 1 : len_bound, kMinChunk);
+  int64_t n = want < by_len ? want : by_len;
+  if (n > max_splits) n = max_splits;
+  if (n < 1) n = 1;
+  return (int)n;
+}
+
+size_t partial_bytes(int64_t rows, int64_t D, int64_t nsplit) {
+  return sizeof(float) * (size_t)rows * (size_t)nsplit * (size_t)(2 * D + 2);
+}
+
+template <typename T>
+int run_generic(int bits, AttnArgs& a, int64_t batch, int64_t h_q, int64_t h_kv, int64_t cap,
+                int64_t D, int64_t kv_len, void* workspace, size_t ws_bytes, cudaStream_t st) {
+  const int G = (int)(h_q / h_kv);
+  const int64_t len_bound = a.kv_len_dev ? cap : kv_len;
+  const int64_t max_splits_ws = ws_bytes / partial_bytes(batch * h_q, D, 1);
+  int nsplit = choose_splits(batch * h_kv, len_bound, max_splits_ws);
+  if (!workspace || ws_bytes == 0) nsplit = 1;
+  a.ws = static_cast<float*>(workspace);
+  a.force_partials = 0;
+  int rc;
+#define MOTIF_RUN_D(DD)                                                                  \
+  if (bits == 16) rc = dispatch_generic<T, DD, 16>(a, G, nsplit, (int)batch, st);        \
+  else if (bits == 4) rc = dispatch_generic<T, DD, 4>(a, G, nsplit, (int)batch, st);     \
+  else rc = dispatch_generic<T, DD, 8>(a, G, nsplit, (int)batch, st);
+  if (D == 64) {
+    MOTIF_RUN_D(64)
+  } else {
+    MOTIF_RUN_D(128)
+  }
+#undef MOTIF_RUN_D
+  if (rc != MOTIF_OK || nsplit == 1) return rc;
+  if (D == 64)
+    attn_combine_kernel<T, 64><<<batch * h_q, 128, 0, st>>>(a.ws, nsplit, (int)kv_len, a.kv_len_dev, static_cast<T*>(a.y));
+  else
+    attn_combine_kernel<T, 128><<<batch * h_q, 256, 0, st>>>(a.ws, nsplit, (int)kv_len, a.kv_len_dev, static_cast<T*>(a.y));
+  return check_launch("attention combine");
+}
+
+int check_common(int64_t batch, int64_t h_q, int64_t h_kv, int64_t cap, int64_t D, int64_t kv_len,
+                 const int32_t* kv_len_dev) {
+  MOTIF_REQUIRE(batch > 0 && h_q > 0 && h_kv > 0 && cap >= 0, MOTIF_ERR_BAD_SHAPE,
+                "sdpa_dual_v: bad shape B=%lld H_q=%lld H_kv=%lld cap=%lld", (long long)batch,
+                (long long)h_q, (long long)h_kv, (long long)cap);
+  MOTIF_REQUIRE(D % 32 == 0, MOTIF_ERR_BAD_CONTRACT, "sdpa_dual_v: D=%lld must be a multiple of 32", (long long)D);
+  MOTIF_REQUIRE(D == 64 || D == 128, MOTIF_ERR_BAD_CONTRACT,
+                "sdpa_dual_v: head_dim %lld not built (64 and 128 are)", (long long)D);
+  MOTIF_REQUIRE(h_q % h_kv == 0, MOTIF_ERR_BAD_CONTRACT, "sdpa_dual_v: H_q=%lld must be a multiple of H_kv=%lld",
+                (long long)h_q, (long long)h_kv);
+  MOTIF_REQUIRE(h_q / h_kv <= 8, MOTIF_ERR_BAD_CONTRACT, "sdpa_dual_v: GQA factor %lld > 8 not built",
+                (long long)(h_q / h_kv));
+  MOTIF_REQUIRE(kv_len_dev || (kv_len >= 0 && kv_len <= cap), MOTIF_ERR_BAD_SHAPE,
+                "sdpa_dual_v: kv_len=%lld must be in [0, %lld]", (long long)kv_len, (long long)cap);
+  MOTIF_REQUIRE(cap < (1ll << 31), MOTIF_ERR_BAD_SHAPE, "sdpa_dual_v: capacity too large");
+  return MOTIF_OK;
+}
+
+bool al(const void* p, int n) { return (reinterpret_cast<uintptr_t>(p) % n) == 0; }
+
+}  // namespace
+}  // namespace motif
+
+using namespace motif;
+
+extern "C" {
+
+size_t motif_sdpa_dual_v_workspace_bytes(int64_t batch, int64_t h_q, int64_t head_dim,
+                                         int64_t max_splits) {
+  return partial_bytes(batch * h_q, head_dim, max_splits < 1 ? 1 : max_splits);
+}
+
+int motif_sdpa_dual_v(int dtype, const void* q, const void* k, const void* v1, const void* v2,
+                      float scale, int64_t batch, int64_t h_q, int64_t h_kv, int64_t kv_cap,
+                      int64_t head_dim, int64_t kv_len, const int32_t* kv_len_dev, void* y,
+                      void* workspace, size_t workspace_bytes, void* stream) {
+  MOTIF_REQUIRE(q && k && v1 && v2 && y, MOTIF_ERR_NULL, "sdpa_dual_v: null pointer");
+  int rc = check_common(batch, h_q, h_kv, kv_cap, head_dim, kv_len, kv_len_dev);
+  if (rc) return rc;
+  const int esz = dtype == MOTIF_F32 ? 4 : 2;
+  for (const void* p : {q, k, v1, v2})
+    MOTIF_REQUIRE(al(p, esz * (int)(head_dim / 32)), MOTIF_ERR_BAD_SHAPE, "sdpa_dual_v: misaligned input");
+  AttnArgs a{};
+  a.q = q;
+  a.q_bstride = h_q * head_dim;
+  a.na = (int)(h_q / h_kv);
+  a.nb_base = 0;
+  a.h_out = (int)h_q;
+  a.kA = k;
+  a.v1 = v1;
+  a.v2 = v2;
+  a.h_kv = (int)h_kv;
+  a.cap = kv_cap;
+  a.gs = 64;
+  a.kv_len = (int)kv_len;
+  a.kv_len_dev = kv_len_dev;
+  a.scale_log2 = scale * kLog2e;
+  a.y = y;
+  cudaStream_t st = as_stream(stream);
+  MOTIF_DISPATCH_FLOAT(dtype, T, return run_generic<T>(16, a, batch, h_q, h_kv, kv_cap, head_dim, kv_len, workspace, workspace_bytes, st));
+  return MOTIF_OK;
+}
+
+int motif_sdpa_dual_v_q(int dtype, int bits, int group_size, const void* q,
+                        const uint32_t* k_data, const void* k_scales, const void* k_biases,
+                        const uint32_t* v1_data, const void* v1_scales, const void* v1_biases,
+                        const uint32_t* v2_data, const void* v2_scales, const void* v2_biases,
+                        float scale, int64_t batch, int64_t h_q, int64_t h_kv, int64_t kv_cap,
+                        int64_t head_dim, int64_t kv_len, const int32_t* kv_len_dev, void* y,
+                        void* workspace, size_t workspace_bytes, void* stream) {
+  MOTIF_REQUIRE(q && k_data && k_scales && k_biases && v1_data && v1_scales && v1_biases &&
+                    v2_data && v2_scales && v2_biases && y,
+                MOTIF_ERR_NULL, "sdpa_dual_v_q: null pointer");
+  MOTIF_REQUIRE(bits == 4 || bits == 8, MOTIF_ERR_BAD_CONTRACT, "sdpa_dual_v_q: bits=%d not in (4, 8)", bits);
+  const int64_t D = head_dim;
+  MOTIF_REQUIRE(D % 32 == 0 && group_size > 0 && D % group_size == 0, MOTIF_ERR_BAD_CONTRACT,
+                "sdpa_dual_v_q: need D %% 32 == 0 and D %% group_size == 0 (D=%lld, group_size=%d)",
+                (long long)D, group_size);
+  const int64_t cpl = D / 32;
+  MOTIF_REQUIRE((32 / bits) % cpl == 0, MOTIF_ERR_BAD_CONTRACT,
+                "sdpa_dual_v_q: each lane's qk_per_thread = D/32 channels must come from one packed "
+                "uint32, i.e. qk_per_thread | EL_PER_INT (which implies D/32 <= 32/bits); got D=%lld, "
+                "bits=%d -> qk_per_thread=%lld, EL_PER_INT=%d",
+                (long long)D, bits, (long long)cpl, 32 / bits);
+  MOTIF_REQUIRE(group_size % cpl == 0, MOTIF_ERR_BAD_CONTRACT,
+                "sdpa_dual_v_q: qk_per_thread | group_size required so a lane's D/32 channels share one "
+                "scale/bias group; got D=%lld, group_size=%d -> qk_per_thread=%lld",
+                (long long)D, group_size, (long long)cpl);
+  int rc = check_common(batch, h_q, h_kv, kv_cap, D, kv_len, kv_len_dev);
+  if (rc) return rc;
+  AttnArgs a{};
+  a.q = q;
+  a.q_bstride = h_q * D;
+  a.na = (int)(h_q / h_kv);
+  a.nb_base = 0;
+  a.h_out = (int)h_q;
+  a.kA = k_data;
+  a.v1 = v1_data;
+  a.v2 = v2_data;
+  a.kA_s = k_scales;
+  a.kA_b = k_biases;
+  a.v1_s = v1_scales;
+  a.v1_b = v1_biases;
+  a.v2_s = v2_scales;
+  a.v2_b = v2_biases;
+  a.h_kv = (int)h_kv;
+  a.cap = kv_cap;
+  a.gs = group_size;
+  a.kv_len = (int)kv_len;
+  a.kv_len_dev = kv_len_dev;
+  a.scale_log2 = scale * kLog2e;
+  a.y = y;
+  cudaStream_t st = as_stream(stream);
+  MOTIF_DISPATCH_FLOAT(dtype, T, return run_generic<T>(bits, a, batch, h_q, h_kv, kv_cap, D, kv_len, workspace, workspace_bytes, st));
+  return MOTIF_OK;
+}
+
+size_t motif_gda_decode_attention_workspace_bytes(int64_t q_heads, int64_t head_dim,
+                                                  int64_t max_splits) {
+  return partial_bytes(q_heads, head_dim, max_splits < 1 ? 1 : max_splits);
+}
+
+int motif_gda_decode_attention(const void* q, const motif_kv4_slots* cache, float scale,
+                               int64_t q_groups, int64_t gr, int64_t kv_len,
+                               const int32_t* kv_len_dev, const void* subln_w,
+                               const float* lambda_full, int64_t lambda_len, float lambda_init,
+                               float eps, void* out, void* workspace, size_t workspace_bytes,
+                               void* stream) {
+  MOTIF_REQUIRE(q && cache && subln_w && lambda_full && out && workspace, MOTIF_ERR_NULL,
+                "gda_decode_attention: null pointer");
+  const motif_kv4_slots& c = *cache;
+  for (int i = 0; i < 4; ++i) MOTIF_REQUIRE(c.data[i], MOTIF_ERR_NULL, "gda_decode_attention: slot %d null", i);
+  MOTIF_REQUIRE(c.batch == 1 && c.head_dim == 128, MOTIF_ERR_BAD_CONTRACT,
+                "gda_decode_attention: batch 1, head_dim 128 only");
+  MOTIF_REQUIRE(c.heads == q_groups, MOTIF_ERR_BAD_CONTRACT,
+                "gda_decode_attention: kv heads per slot (%lld) must equal q_groups (%lld)",
+                (long long)c.heads, (long long)q_groups);
+  MOTIF_REQUIRE(gr == 3 || gr == 4, MOTIF_ERR_BAD_CONTRACT, "gda_decode_attention: gr=%lld not built (3, 4)", (long long)gr);
+  MOTIF_REQUIRE(kv_len_dev || (kv_len >= 0 && kv_len <= c.capacity), MOTIF_ERR_BAD_SHAPE,
+                "gda_decode_attention: kv_len out of range");
+  const int64_t q_origin = q_groups * gr;
+  const int64_t q_heads = q_origin + q_groups;
+  int lam_mode;
+  if (lambda_len == 1) lam_mode = 0;
+  else if (lambda_len == q_groups) lam_mode = 1;
+  else if (lambda_len == q_origin) lam_mode = 2;
+  else return fail(MOTIF_ERR_BAD_SHAPE, "gda_decode_attention: lambda_len %lld", (long long)lambda_len);
+  const int bits = c.bits;
+  MOTIF_REQUIRE(bits == 16 || ((bits == 4 || bits == 8) && c.scales[0] && c.biases[0] &&
+                               (c.group_size == 32 || c.group_size == 64 || c.group_size == 128)),
+                MOTIF_ERR_BAD_CONTRACT, "gda_decode_attention: cache bits/group_size");
+  const int64_t len_bound = kv_len_dev ? c.capacity : kv_len;
+  const int64_t max_splits_ws = workspace_bytes / partial_bytes(q_heads, 128, 1);
+  MOTIF_REQUIRE(max_splits_ws >= 1, MOTIF_ERR_WORKSPACE, "gda_decode_attention: workspace too small");
+  const int nsplit = choose_splits(q_groups, len_bound, max_splits_ws);
+
+  AttnArgs a{};
+  a.q = q;
+  a.q_bstride = 0;
+  a.na = (int)gr;
+  a.nb_base = (int)q_origin;
+  a.h_out = (int)q_heads;
+  a.kA = c.data[0];
+  a.kB = c.data[1];
+  a.v1 = c.data[2];
+  a.v2 = c.data[3];
+  a.kA_s = c.scales[0];
+  a.kA_b = c.biases[0];
+  a.kB_s = c.scales[1];
+  a.kB_b = c.biases[1];
+  a.v1_s = c.scales[2];
+  a.v1_b = c.biases[2];
+  a.v2_s = c.scales[3];
+  a.v2_b = c.biases[3];
+  a.h_kv = (int)c.heads;
+  a.cap = c.capacity;
+  a.gs = c.group_size;
+  a.kv_len = (int)kv_len;
+  a.kv_len_dev = kv_len_dev;
+  a.scale_log2 = scale * kLog2e;
+  a.force_partials = 1;
+  a.ws = static_cast<float*>(workspace);
+  cudaStream_t st = as_stream(stream);
+  int rc;
+#define MOTIF_FUSED(GR)                                                                    \
+  if (bits == 16) rc = launch_split<__half, 128, 16, GR, 1>(a, nsplit, 1, st);            \
+  else if (bits == 4) rc = launch_split<__half, 128, 4, GR, 1>(a, nsplit, 1, st);         \
+  else rc = launch_split<__half, 128, 8, GR, 1>(a, nsplit, 1, st);                        \
+  if (rc) return rc;                                                                      \
+  gda_combine_kernel<128, GR><<<q_groups, 256, 0, st>>>(                                  \
+      a.ws, nsplit, (int)kv_len, kv_len_dev, (int)q_origin,                               \
+      static_cast<const __half*>(subln_w), lambda_full, lam_mode, 1.0f - lambda_init, eps, \
+      static_cast<__half*>(out));
+  if (gr == 3) {
+    MOTIF_FUSED(3)
+  } else {
+    MOTIF_FUSED(4)
+  }
+#undef MOTIF_FUSED
+  return check_launch("gda decode attention");
+}
+
+}  // extern "C"

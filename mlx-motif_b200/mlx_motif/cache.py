@@ -1,0 +1,279 @@
+"""4-slot KV caches for grouped differential attention (k1, k2, v1, v2) on the GPU.
+
+API of ``src/mlx_motif/cache.py``: ``MotifGroupedKVCache`` (303-404) and
+``MotifGroupedQuantizedKVCache`` (407-545) with ``update_and_fetch_4``,
+``update_and_fetch_4_quantized``, ``offset``, ``step``, ``trim``,
+``is_trimmable``, ``state`` / ``meta_state``, ``make_mask`` and
+``to_quantized``. Fetches return the FULL row-contiguous capacity buffers;
+consumers bound reads by ``offset`` (the attention kernels take it as
+``kv_len``).
+
+Writes go through ``motif_kv4_append``: a copy for the fp16 cache, or one
+batched affine quantize of all four slots for the quantized cache (codes,
+scales and biases bit-identical to quantizing each slot separately, since
+groups never cross the head axis).
+
+Capacity: by default slots grow in ``step``-row increments like the reference
+(``cache.py:245-265``). Passing ``max_size`` preallocates the whole capacity
+once, so the buffers never move — the form a captured CUDA graph needs.
+"""
+
+from __future__ import annotations
+
+import torch
+
+from ._native import check, dtype_code, lib, motif_kv4_slots, ptr, stream
+
+
+def create_causal_mask(N: int, offset: int = 0, window_size: int | None = None) -> torch.Tensor:
+    """Boolean (N, offset+N) causal mask (True = attend), mlx-lm's convention."""
+    rinds = torch.arange(offset + N)
+    linds = torch.arange(offset, offset + N)
+    mask = linds[:, None] >= rinds[None]
+    if window_size is not None:
+        mask = mask & (linds[:, None] < rinds[None] + window_size)
+    return mask
+
+
+def create_attention_mask(N: int, offset: int = 0, return_array: bool = False, window_size: int | None = None):
+    """mlx-lm cache-module contract: None for one query row, "causal" or an explicit array otherwise."""
+    if N == 1:
+        return None
+    if return_array:
+        return create_causal_mask(N, offset, window_size)
+    return "causal"
+
+
+def _slots_struct(slots, bits: int, group_size: int, B: int, H: int, cap: int, D: int) -> motif_kv4_slots:
+    s = motif_kv4_slots()
+    for i, slot in enumerate(slots):
+        if bits == 16:
+            s.data[i] = ptr(slot)
+            s.scales[i] = None
+            s.biases[i] = None
+        else:
+            s.data[i] = ptr(slot[0])
+            s.scales[i] = ptr(slot[1])
+            s.biases[i] = ptr(slot[2])
+    s.bits = bits
+    s.group_size = group_size
+    s.batch = B
+    s.heads = H
+    s.capacity = cap
+    s.head_dim = D
+    return s
+
+
+class MotifGroupedKVCacheBase:
+    """Offset bookkeeping and storage growth shared by both 4-slot caches (``cache.py:178-300``)."""
+
+    step = 256
+
+    def update_and_fetch(self, keys, values):
+        raise NotImplementedError(
+            "MotifGroupedKVCacheBase subclasses require the model to call "
+            "update_and_fetch_4 directly — the 1-slot path is intentionally unsupported."
+        )
+
+    def is_trimmable(self):
+        return True
+
+    def trim(self, n):
+        n = min(self.offset, n)
+        self.offset -= n
+        return n
+
+    def make_mask(self, N, return_array: bool = False, window_size=None):
+        return create_attention_mask(N, offset=self.offset, return_array=return_array, window_size=window_size)
+
+    @staticmethod
+    def _assert_uniform_heads(k1, k2, v1, v2) -> None:
+        h1 = k1.shape[1]
+        if not (k2.shape[1] == v1.shape[1] == v2.shape[1] == h1):
+            raise ValueError(
+                "4-slot grouped KV cache requires k1/k2/v1/v2 to share a head "
+                f"count; got k1={h1}, k2={k2.shape[1]}, v1={v1.shape[1]}, "
+                f"v2={v2.shape[1]}. This happens with k_ratio > 1, which the "
+                "4-slot cache does not support."
+            )
+
+    def _grow(self, B: int, H: int, S: int, D: int, dtype, device) -> None:
+        prev = self.offset
+        if self.k1 is not None and prev + S <= self._slot_capacity(self.k1):
+            return
+        if self.max_size is not None:
+            if self.k1 is None and prev + S <= self.max_size:
+                self.k1, self.k2, self.v1, self.v2 = (
+                    self._init_storage(B, H, self.max_size, D, dtype, device) for _ in range(4)
+                )
+                return
+            raise ValueError(f"cache capacity {self.max_size} exceeded (offset {prev} + {S} rows)")
+        new_len = ((self.step + S - 1) // self.step) * self.step
+        if self.k1 is None:
+            self.k1, self.k2, self.v1, self.v2 = (
+                self._init_storage(B, H, new_len, D, dtype, device) for _ in range(4)
+            )
+            return
+        slots = [self.k1, self.k2, self.v1, self.v2]
+        if prev % self.step != 0:
+            slots = [self._trim_slot(s, prev) for s in slots]
+        fresh = self._init_storage(B, H, new_len, D, dtype, device)
+        self.k1, self.k2, self.v1, self.v2 = (self._expand_slot(s, fresh) for s in slots)
+
+    def slots_struct(self) -> motif_kv4_slots:
+        """C-ABI view of the four slots (valid until the next growth)."""
+        return self._struct()
+
+
+class MotifGroupedKVCache(MotifGroupedKVCacheBase):
+    """fp16/bf16 4-slot cache; each slot (B, H, capacity, D)."""
+
+    def __init__(self, max_size: int | None = None):
+        self.k1 = self.k2 = self.v1 = self.v2 = None
+        self.offset = 0
+        self.max_size = max_size
+
+    def _slot_capacity(self, slot) -> int:
+        return slot.shape[2]
+
+    def _init_storage(self, B, H, n, D, dtype, device):
+        return torch.zeros((B, H, n, D), dtype=dtype, device=device)
+
+    def _trim_slot(self, slot, prev):
+        return slot[..., :prev, :].contiguous()
+
+    def _expand_slot(self, slot, fresh):
+        return torch.cat([slot, fresh], dim=2)
+
+    def _struct(self):
+        B, H, cap, D = self.k1.shape
+        return _slots_struct((self.k1, self.k2, self.v1, self.v2), 16, 64, B, H, cap, D)
+
+    def update_and_fetch_4(self, k1, k2, v1, v2):
+        """Append the 4 incoming slices; return the FULL capacity buffers (``cache.py:337-360``)."""
+        self._assert_uniform_heads(k1, k2, v1, v2)
+        B, H, S, D = k1.shape
+        prev = self.offset
+        self._grow(B, H, S, D, k1.dtype, k1.device)
+        ins = [t.to(self.k1.dtype).contiguous() for t in (k1, k2, v1, v2)]
+        s = self._struct()
+        check(lib.motif_kv4_append(dtype_code(self.k1), s, *(ptr(t) for t in ins), S, prev, None,
+                                   stream(k1.device)), "kv4_append")
+        self.offset += S
+        return self.k1, self.k2, self.v1, self.v2
+
+    @property
+    def state(self):
+        if self.offset == 0 or self.k1 is None:
+            return self.k1, self.k2, self.v1, self.v2
+        o = self.offset
+        return tuple(t[..., :o, :] for t in (self.k1, self.k2, self.v1, self.v2))
+
+    @state.setter
+    def state(self, v):
+        self.k1, self.k2, self.v1, self.v2 = (t.contiguous() if t is not None else None for t in v)
+
+    @property
+    def meta_state(self):
+        return (str(self.offset),)
+
+    @meta_state.setter
+    def meta_state(self, v):
+        self.offset = int(v[0])
+
+    def to_quantized(self, group_size: int = 64, bits: int = 8) -> "MotifGroupedQuantizedKVCache":
+        """Switch to the quantized variant (``cache.py:394-404``)."""
+        from .quantization import quantize
+
+        new = MotifGroupedQuantizedKVCache(group_size=group_size, bits=bits)
+        if self.offset > 0:
+            o = self.offset
+            new.k1, new.k2, new.v1, new.v2 = (
+                quantize(t[..., :o, :].contiguous(), group_size, bits) for t in (self.k1, self.k2, self.v1, self.v2)
+            )
+            new.offset = self.offset
+        return new
+
+
+class MotifGroupedQuantizedKVCache(MotifGroupedKVCacheBase):
+    """4-slot quantized cache: each slot a (data uint32, scales, biases) triple."""
+
+    def __init__(self, group_size: int = 64, bits: int = 8, max_size: int | None = None):
+        self.k1 = self.k2 = self.v1 = self.v2 = None
+        self.offset = 0
+        self.group_size = group_size
+        self.bits = bits
+        self.max_size = max_size
+
+    def _slot_capacity(self, slot) -> int:
+        return slot[0].shape[2]
+
+    def _init_storage(self, B, H, n, D, dtype, device):
+        el = 32 // self.bits
+        return (
+            torch.zeros((B, H, n, D // el), dtype=torch.uint32, device=device),
+            torch.zeros((B, H, n, D // self.group_size), dtype=dtype, device=device),
+            torch.zeros((B, H, n, D // self.group_size), dtype=dtype, device=device),
+        )
+
+    def _trim_slot(self, slot, prev):
+        return tuple(x[..., :prev, :].contiguous() for x in slot)
+
+    def _expand_slot(self, slot, fresh):
+        return tuple(torch.cat([slot[i], fresh[i]], dim=-2) for i in range(3))
+
+    def _struct(self):
+        B, H, cap, _ = self.k1[0].shape
+        D = self.k1[1].shape[-1] * self.group_size
+        return _slots_struct((self.k1, self.k2, self.v1, self.v2), self.bits, self.group_size, B, H, cap, D)
+
+    def _update_4(self, k1, k2, v1, v2):
+        """One batched quantize of all four slots written at [offset, offset+S) (``cache.py:485-512``)."""
+        self._assert_uniform_heads(k1, k2, v1, v2)
+        B, H, S, D = k1.shape
+        prev = self.offset
+        self._grow(B, H, S, D, k1.dtype, k1.device)
+        ins = [t.to(self.k1[1].dtype).contiguous() for t in (k1, k2, v1, v2)]
+        s = self._struct()
+        check(lib.motif_kv4_append(dtype_code(self.k1[1]), s, *(ptr(t) for t in ins), S, prev, None,
+                                   stream(k1.device)), "kv4_append")
+        self.offset += S
+
+    def update_and_fetch_4(self, k1, k2, v1, v2):
+        """Quantize and append; return dequantized live slices (``cache.py:448-465``)."""
+        from .quantization import dequantize
+
+        self._update_4(k1, k2, v1, v2)
+        o = self.offset
+
+        def _deq(slot):
+            return dequantize(*(x[..., :o, :].contiguous() for x in slot), group_size=self.group_size,
+                              bits=self.bits)
+
+        return _deq(self.k1), _deq(self.k2), _deq(self.v1), _deq(self.v2)
+
+    def update_and_fetch_4_quantized(self, k1, k2, v1, v2):
+        """Quantize and append; return each slot's FULL capacity triple (``cache.py:467-483``)."""
+        self._update_4(k1, k2, v1, v2)
+        return self.k1, self.k2, self.v1, self.v2
+
+    @property
+    def state(self):
+        if self.offset == 0 or self.k1 is None:
+            return self.k1, self.k2, self.v1, self.v2
+        o = self.offset
+        return tuple(tuple(x[..., :o, :] for x in slot) for slot in (self.k1, self.k2, self.v1, self.v2))
+
+    @state.setter
+    def state(self, v):
+        self.k1, self.k2, self.v1, self.v2 = (
+            tuple(x.contiguous() for x in slot) if slot is not None else None for slot in v
+        )
+
+    @property
+    def meta_state(self):
+        return tuple(map(str, (self.offset, self.group_size, self.bits)))
+
+    @meta_state.setter
+    def meta_state(self, v):
+        self.offset, self.group_size, self.bits = map(int, v)

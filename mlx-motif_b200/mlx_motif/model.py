@@ -1,0 +1,610 @@
+"""Motif GDA decoder on B200: config, path resolution and the CUDA-graph decode engine.
+
+Host-side mirror of ``src/mlx_motif/model.py``:
+  * ``ModelArgs`` with the reference's validation rules (``model.py:48-204``).
+  * ``AttnPath`` / ``_resolve_attention_path`` (``model.py:288-344``), same
+    truth table and env flags (``MLX_MOTIF_QUANT_SDPA``, ``MLX_MOTIF_DUAL_V``).
+  * λ helpers (``model.py:389, 462-470``) and the origin-first Q permutation
+    of ``fuse_qkv`` (``model.py:994-1015``).
+  * ``MotifDecoder``: batch-1 decode of the grouped (12.7B-class) model
+    through the DUAL_V / QUANT_SDPA path of ``_forward_grouped``
+    (``model.py:563-837``) and ``MotifDecoderLayer`` (845-855). One decode
+    step is a fixed sequence of C-ABI kernels captured once into a CUDA graph;
+    the position and KV length live in device memory, so the graph replays at
+    every length and the greedy token never leaves the GPU.
+
+Per layer the step launches: fused-qkv GEMV, RoPE+4-slot append, fused
+dual-V attention + GDA post (2 kernels), o_proj GEMV, residual+RMSNorm,
+fused gate|up GEMV, PolyNorm·up, down GEMV, residual+RMSNorm.
+"""
+
+from __future__ import annotations
+
+import enum
+import math
+import os
+from dataclasses import dataclass
+
+import torch
+
+from ._native import check, lib, ptr, stream
+from .cache import MotifGroupedKVCache, MotifGroupedQuantizedKVCache
+from .linear import QuantizedLinear
+from .quantization import quantize
+
+# --------------------------------------------------------------------------- #
+# Config (model.py:48-204)
+# --------------------------------------------------------------------------- #
+
+
+@dataclass
+class ModelArgs:
+    model_type: str = "motif"
+    hidden_size: int = 4096
+    num_hidden_layers: int = 48
+    intermediate_size: int = 14336
+    num_attention_heads: int = 32
+    num_key_value_heads: int = 16
+    vocab_size: int = 219520
+    rms_norm_eps: float = 1e-6
+    rope_theta: float = 10000.0
+    max_position_embeddings: int = 32768
+    head_dim: int | None = 128
+    num_noise_heads: int | None = 8
+    k_ratio: int = 1
+    attn_rms_norm_eps: float = 1e-5
+    tie_word_embeddings: bool = False
+    fused_rope: bool = False
+
+    def __post_init__(self) -> None:
+        for name in ("hidden_size", "num_hidden_layers", "intermediate_size", "num_attention_heads",
+                     "num_key_value_heads", "vocab_size", "max_position_embeddings"):
+            v = getattr(self, name)
+            if type(v) is not int:
+                raise ValueError(f"{name} must be an integer; got {v!r}")
+            if v <= 0:
+                raise ValueError(f"{name} must be greater than zero; got {v}")
+        if self.head_dim is not None:
+            if type(self.head_dim) is not int:
+                raise ValueError(f"head_dim must be an integer; got {self.head_dim!r}")
+            if self.head_dim <= 0:
+                raise ValueError(f"head_dim must be greater than zero; got {self.head_dim}")
+        elif self.hidden_size < self.num_attention_heads:
+            raise ValueError("derived head_dim must be greater than zero")
+        elif self.hidden_size % self.num_attention_heads:
+            raise ValueError("hidden_size must be divisible by num_attention_heads when head_dim is omitted")
+        if self.is_grouped:
+            self._validate_grouped()
+        else:
+            self._validate_vanilla()
+
+    def _validate_vanilla(self) -> None:
+        if self.num_attention_heads % 2:
+            raise ValueError("num_attention_heads must be even for vanilla differential attention")
+        if self.num_key_value_heads % 2:
+            raise ValueError("num_key_value_heads must be even for vanilla differential attention")
+        if self.num_attention_heads % self.num_key_value_heads:
+            raise ValueError("num_attention_heads must be divisible by num_key_value_heads")
+        if self.head_dim is not None and self.head_dim * self.num_attention_heads != self.hidden_size:
+            raise ValueError("head_dim * num_attention_heads must equal hidden_size for vanilla attention")
+
+    def _validate_grouped(self) -> None:
+        if type(self.num_noise_heads) is not int:
+            raise ValueError(f"num_noise_heads must be an integer when provided; got {self.num_noise_heads!r}")
+        if self.num_noise_heads <= 0:
+            raise ValueError("num_noise_heads must be greater than zero")
+        if type(self.k_ratio) is not int or self.k_ratio < 1:
+            raise ValueError(f"k_ratio must be an integer >= 1 for grouped attention; got {self.k_ratio!r}")
+        if self.num_attention_heads <= self.num_noise_heads:
+            raise ValueError("num_attention_heads must be greater than num_noise_heads for grouped attention")
+        if self.num_attention_heads % self.num_noise_heads:
+            raise ValueError("num_attention_heads must be divisible by num_noise_heads")
+        width = self.k_ratio + 1
+        if self.num_key_value_heads < width or self.num_key_value_heads % width:
+            raise ValueError("num_key_value_heads must be a positive multiple of k_ratio + 1")
+        k_noise = self.num_key_value_heads // width
+        if self.num_noise_heads % k_noise:
+            raise ValueError("num_noise_heads must be divisible by num_key_value_heads / (k_ratio + 1)")
+        if (self.num_attention_heads // self.num_noise_heads - 1) % self.k_ratio:
+            raise ValueError("the grouped attention ratio must be divisible by k_ratio")
+
+    @property
+    def is_grouped(self) -> bool:
+        return self.num_noise_heads is not None
+
+    # Derived grouped-attention dims (MotifAttention._init_grouped, model.py:424-447).
+    @property
+    def d(self) -> int:
+        return self.head_dim or self.hidden_size // self.num_attention_heads
+
+    @property
+    def grouped_ratio(self) -> int:
+        return (self.num_attention_heads - self.num_noise_heads) // self.num_noise_heads
+
+    @property
+    def q_heads(self) -> int:
+        return (self.grouped_ratio + 1) * self.num_noise_heads
+
+    @property
+    def q_origin(self) -> int:
+        return self.grouped_ratio * self.num_noise_heads
+
+    @property
+    def k_noise_heads(self) -> int:
+        return self.num_key_value_heads // (self.k_ratio + 1)
+
+    @property
+    def kv_repeat(self) -> int:
+        return self.num_noise_heads // self.k_noise_heads
+
+    @property
+    def qkv_out(self) -> int:
+        return self.q_heads * self.d + self.num_key_value_heads * self.d + 2 * self.k_noise_heads * self.d
+
+
+# --------------------------------------------------------------------------- #
+# Path resolution (model.py:288-344)
+# --------------------------------------------------------------------------- #
+
+
+class AttnPath(enum.Enum):
+    QUANT_SDPA = "sdpa_dual_v_q4"
+    DUAL_V = "sdpa_dual_v"
+    FALLBACK = "stacked_sdpa"
+
+
+def _resolve_attention_path(cache, S: int, kv_repeat: int, kr: int, fused_rope: bool, env=os.environ) -> AttnPath:
+    """First match wins: QUANT_SDPA (quantized 4-slot cache), DUAL_V, else FALLBACK."""
+    falsy = ("0", "", "false", "False")
+    decode_ok = S == 1 and kv_repeat == 1 and kr == 1
+    if (decode_ok and not fused_rope and isinstance(cache, MotifGroupedQuantizedKVCache)
+            and env.get("MLX_MOTIF_QUANT_SDPA", "1") not in falsy):
+        return AttnPath.QUANT_SDPA
+    if decode_ok and not fused_rope and env.get("MLX_MOTIF_DUAL_V", "1") not in falsy:
+        return AttnPath.DUAL_V
+    return AttnPath.FALLBACK
+
+
+# --------------------------------------------------------------------------- #
+# λ and the origin-first permutation
+# --------------------------------------------------------------------------- #
+
+
+def lambda_init_for_layer(layer_idx: int) -> float:
+    """λ_init = 0.8 − 0.6·exp(−0.3·(layer_idx − 1)) (``model.py:389``)."""
+    return 0.8 - 0.6 * math.exp(-0.3 * (layer_idx - 1))
+
+
+def lambda_full(lq1, lk1, lq2, lk2, lam_init: float) -> torch.Tensor:
+    """exp(Σ lq1·lk1) − exp(Σ lq2·lk2) + λ_init in fp32 (``model.py:462-470``)."""
+    l1 = torch.exp(torch.sum(lq1.float() * lk1.float(), dim=-1))
+    l2 = torch.exp(torch.sum(lq2.float() * lk2.float(), dim=-1))
+    return (l1 - l2 + lam_init).reshape(1).float()
+
+
+def origin_first_perm(q_groups: int, gr: int, d: int) -> torch.Tensor:
+    """Row permutation HF head stripes -> [origin heads | noise heads] (``model.py:994-1015``)."""
+    heads = [g * (gr + 1) + p for g in range(q_groups) for p in range(gr)]
+    heads += [g * (gr + 1) + gr for g in range(q_groups)]
+    return torch.cat([torch.arange(h * d, (h + 1) * d) for h in heads])
+
+
+def rope_inv_freq(dims: int, base: float, device) -> torch.Tensor:
+    """fp32 inverse frequencies 2^(−(i/(dims/2))·log2 base), i < dims/2 (non-traditional RoPE).
+
+    Formed in float64 and rounded once to fp32, so every caller gets the same table.
+    """
+    half = dims // 2
+    vals = [2.0 ** (-(i / half) * math.log2(base)) for i in range(half)]
+    return torch.tensor(vals, dtype=torch.float64).to(torch.float32).to(device)
+
+
+# --------------------------------------------------------------------------- #
+# Tensor-parallel shard plan (no reference counterpart: the reference is single-device)
+# --------------------------------------------------------------------------- #
+
+
+def tp_shard_plan(args: ModelArgs, rank: int, world: int) -> dict:
+    """Which rows/columns of each global weight rank `rank` of `world` keeps.
+
+    Attention is split by GDA group (each group's gr origin heads, its noise
+    head and its kv head of every slot stay on one rank, so attention and
+    gda_post need no exchange); o_proj keeps the matching input columns;
+    gate/up keep rows [r·I/w, (r+1)·I/w) and down the matching columns. The
+    two row-parallel outputs (o_proj, down_proj) are summed across ranks.
+    """
+    G, gr, d, Hk, I = args.num_noise_heads, args.grouped_ratio, args.d, args.k_noise_heads, args.intermediate_size
+    if G % world or Hk % world or I % world or G != Hk:
+        raise ValueError(f"TP {world}: q_groups {G}, kv heads {Hk} and intermediate {I} must split evenly")
+    gpr, kpr, ipr = G // world, Hk // world, I // world
+    qo0 = rank * gpr * gr
+    qkv_rows = torch.cat([
+        torch.arange(qo0 * d, (qo0 + gpr * gr) * d),  # origin heads of my groups
+        G * gr * d + torch.arange(rank * gpr * d, (rank + 1) * gpr * d),  # my noise heads
+        G * (gr + 1) * d + torch.arange(2 * rank * kpr * d, 2 * (rank + 1) * kpr * d),  # (k1,k2) pairs
+        G * (gr + 1) * d + 2 * Hk * d + torch.arange(2 * rank * kpr * d, 2 * (rank + 1) * kpr * d),  # (v1,v2)
+    ])
+    return dict(
+        qkv_rows=qkv_rows,
+        o_cols=(rank * gpr * gr * 2 * d, (rank + 1) * gpr * gr * 2 * d),
+        mlp_rows=(rank * ipr, (rank + 1) * ipr),
+    )
+
+
+# --------------------------------------------------------------------------- #
+# Decode engine
+# --------------------------------------------------------------------------- #
+
+
+def _ql(triple, device) -> QuantizedLinear:
+    import numpy as np
+
+    d, s, b = triple
+    if isinstance(d, np.ndarray):
+        d = torch.from_numpy(d.view(np.int32)).view(torch.uint32)
+        s = torch.from_numpy(s)
+        b = torch.from_numpy(b)
+    return QuantizedLinear(d.to(device), s.to(device), b.to(device))
+
+
+def _t(a, device, dtype=None) -> torch.Tensor:
+    import numpy as np
+
+    if isinstance(a, np.ndarray):
+        a = torch.from_numpy(np.ascontiguousarray(a))
+    a = torch.as_tensor(a)
+    return a.to(device=device, dtype=dtype or a.dtype).contiguous()
+
+
+class MotifDecoder:
+    """Batch-1 greedy decoder of the grouped Motif model on one GPU (or one TP rank).
+
+    ``cache``: "fp16" (4-slot fp16 rows) or "q4"/"q8" (packed 4-slot cache,
+    group 64). ``max_seq`` is the preallocated KV capacity. With a process
+    group ``tp_group`` the weights passed in must already be this rank's shard
+    (q groups and MLP columns); the engine all-reduces the o_proj and
+    down_proj outputs and the PolyNorm statistics.
+    """
+
+    def __init__(self, args: ModelArgs, weights: dict, cache: str = "fp16", max_seq: int = 4096,
+                 device="cuda", tp_group=None):
+        if not args.is_grouped or args.k_ratio != 1 or args.kv_repeat != 1:
+            raise ValueError("MotifDecoder runs the grouped DUAL_V/QUANT_SDPA decode path "
+                             "(num_noise_heads set, k_ratio == 1, kv_repeat == 1)")
+        self.args = args
+        self.device = torch.device(device)
+        self.tp_group = tp_group
+        self.tp = 1 if tp_group is None else torch.distributed.get_world_size(tp_group)
+        a = args
+        self.q_groups = a.num_noise_heads // self.tp
+        self.gr = a.grouped_ratio
+        self.d = a.d
+        self.kv_heads = a.k_noise_heads // self.tp
+        self.q_heads = self.q_groups * (self.gr + 1)
+        self.q_origin = self.q_groups * self.gr
+        self.inter = a.intermediate_size // self.tp
+        self.H = a.hidden_size
+        self.V = a.vocab_size
+        self.max_seq = max_seq
+        self.cache_kind = cache
+        dev = self.device
+
+        self.embed = _t(weights["embed"], dev, torch.float16)
+        self.final_norm = _t(weights["final_norm"], dev, torch.float16)
+        self.lm_head = weights["lm_head"] if isinstance(weights["lm_head"], QuantizedLinear) else _ql(weights["lm_head"], dev)
+        self.layers = []
+        for L in weights["layers"]:
+            if "gate_up" in L:
+                gate_up = L["gate_up"]
+            else:
+                g, u = _ql(L["gate"], dev), _ql(L["up"], dev)
+                gate_up = QuantizedLinear(torch.cat([g.weight, u.weight]), torch.cat([g.scales, u.scales]),
+                                          torch.cat([g.biases, u.biases]))
+            self.layers.append(dict(
+                input_norm=_t(L["input_norm"], dev, torch.float16),
+                post_norm=_t(L["post_norm"], dev, torch.float16),
+                qkv=L["qkv"] if isinstance(L["qkv"], QuantizedLinear) else _ql(L["qkv"], dev),
+                o=L["o"] if isinstance(L["o"], QuantizedLinear) else _ql(L["o"], dev),
+                gate_up=gate_up,
+                down=L["down"] if isinstance(L["down"], QuantizedLinear) else _ql(L["down"], dev),
+                subln=_t(L["subln"], dev, torch.float16),
+                lambda_full=_t(L["lambda_full"], dev, torch.float32).reshape(-1),
+                lambda_init=float(L["lambda_init"]),
+                polynorm_w=_t(L.get("polynorm_w", [1 / 3, 1 / 3, 1 / 3]), dev, torch.float16),
+                polynorm_b=_t(L.get("polynorm_b", [0.0]), dev, torch.float16),
+            ))
+        self._check_shapes()
+
+        # KV caches: preallocated capacity (buffers never move; graph-safe).
+        if cache == "fp16":
+            self.caches = [MotifGroupedKVCache(max_size=max_seq) for _ in self.layers]
+        elif cache in ("q4", "q8"):
+            bits = 4 if cache == "q4" else 8
+            self.caches = [MotifGroupedQuantizedKVCache(64, bits, max_size=max_seq) for _ in self.layers]
+        else:
+            raise ValueError(f"cache must be fp16, q4 or q8; got {cache!r}")
+        for c in self.caches:
+            c._grow(1, self.kv_heads, 1, self.d, torch.float16, dev)
+        self._slots = [c.slots_struct() for c in self.caches]
+
+        f16 = torch.float16
+        H, d = self.H, self.d
+        self.h = torch.zeros(H, dtype=f16, device=dev)
+        self.x = torch.zeros(H, dtype=f16, device=dev)
+        self.qkv = torch.zeros(self.layers[0]["qkv"].out_dim, dtype=f16, device=dev)
+        self.q = torch.zeros(self.q_heads * d, dtype=f16, device=dev)
+        self.attn = torch.zeros(self.q_origin * 2 * d, dtype=f16, device=dev)
+        self.o = torch.zeros(H, dtype=f16, device=dev)
+        self.gu = torch.zeros(2 * self.inter, dtype=f16, device=dev)
+        self.act = torch.zeros(self.inter, dtype=f16, device=dev)
+        self.dn = torch.zeros(H, dtype=f16, device=dev)
+        self.logits = torch.zeros(self.V, dtype=f16, device=dev)
+        self.token = torch.zeros(1, dtype=torch.int32, device=dev)
+        # pos_len[0] = position of the token being decoded, pos_len[1] = kv_len after its append.
+        self.pos_len = torch.tensor([0, 1], dtype=torch.int32, device=dev)
+        self._one_one = torch.ones(2, dtype=torch.int32, device=dev)
+        self.inv_freq = rope_inv_freq(d, a.rope_theta, dev)
+        self.scale = d ** -0.5
+        lin_ws = max(lib.motif_quantized_linear_workspace_bytes(1, ql.out_dim, ql.in_dim, 4, 64)
+                     for L in self.layers for ql in (L["qkv"], L["o"], L["gate_up"], L["down"]))
+        lin_ws = max(lin_ws, lib.motif_quantized_linear_workspace_bytes(1, self.V, H, 4, 64))
+        self.lin_ws = torch.zeros(max(lin_ws, 16), dtype=torch.uint8, device=dev)
+        self.attn_ws_bytes = lib.motif_gda_decode_attention_workspace_bytes(self.q_heads, d, 64)
+        self.attn_ws = torch.zeros(self.attn_ws_bytes, dtype=torch.uint8, device=dev)
+        self.argmax_ws_bytes = lib.motif_argmax_workspace_bytes(self.V)
+        self.argmax_ws = torch.zeros(self.argmax_ws_bytes, dtype=torch.uint8, device=dev)
+        self.offset = 0  # host mirror of pos_len[0]
+        self._graphs: dict[bool, torch.cuda.CUDAGraph] = {}
+        self.pinned_in = torch.zeros(1, dtype=torch.int32).pin_memory()
+        self.pinned_out = torch.zeros(1, dtype=torch.int32).pin_memory()
+
+    # ------------------------------------------------------------------ #
+    def _check_shapes(self) -> None:
+        L0 = self.layers[0]
+        d = self.d
+        exp_qkv = self.q_heads * d + 4 * self.kv_heads * d
+        if L0["qkv"].out_dim != exp_qkv or L0["qkv"].in_dim != self.H:
+            raise ValueError(f"qkv weight ({L0['qkv'].out_dim}, {L0['qkv'].in_dim}) != ({exp_qkv}, {self.H})")
+        if L0["o"].in_dim != self.q_origin * 2 * d or L0["o"].out_dim != self.H:
+            raise ValueError("o_proj shape mismatch")
+        if L0["gate_up"].out_dim != 2 * self.inter or L0["down"].in_dim != self.inter:
+            raise ValueError("MLP shape mismatch")
+
+    @property
+    def weight_bytes(self) -> int:
+        """Packed weight bytes streamed per token (every linear + lm_head)."""
+        n = self.lm_head.nbytes()
+        for L in self.layers:
+            n += sum(L[k].nbytes() for k in ("qkv", "o", "gate_up", "down"))
+        return n
+
+    def weights_dict(self) -> dict:
+        """The device weights in the constructor's format (share them with another cache kind)."""
+        return dict(embed=self.embed, final_norm=self.final_norm, lm_head=self.lm_head,
+                    layers=[dict(L) for L in self.layers])
+
+    def kv_bytes_per_token(self, kv_len: int) -> int:
+        """KV-cache bytes the attention reads at one step (4 slots, all layers)."""
+        d = self.d
+        per_row = 2 * d if self.cache_kind == "fp16" else (d * (4 if self.cache_kind == "q4" else 8) // 8 + 4 * d // 64)
+        return len(self.layers) * 4 * self.kv_heads * kv_len * per_row
+
+    # ------------------------------------------------------------------ #
+    def _allreduce(self, t: torch.Tensor) -> None:
+        if self.tp_group is not None:
+            torch.distributed.all_reduce(t, group=self.tp_group)
+
+    def _launch_step(self, with_head: bool) -> None:
+        """Enqueue one decode step on the current stream (no host sync, no allocation)."""
+        st = stream(self.device)
+        H, d = self.H, self.d
+        eps = self.args.rms_norm_eps
+        pos_p = self.pos_len.data_ptr()
+        kvl_p = pos_p + 4
+        L0 = self.layers[0]
+        check(lib.motif_embed_rms_norm(0, ptr(self.token), ptr(self.embed), self.V, H, ptr(L0["input_norm"]), eps,
+                                       ptr(self.h), ptr(self.x), st), "embed")
+        for li, L in enumerate(self.layers):
+            L["qkv"](self.x, out=self.qkv, workspace=self.lin_ws)
+            check(lib.motif_rope_qkv_append(ptr(self.qkv), ptr(self.inv_freq), self.q_heads, self._slots[li], pos_p,
+                                            ptr(self.q), st), "rope_qkv_append")
+            check(lib.motif_gda_decode_attention(ptr(self.q), self._slots[li], self.scale, self.q_groups, self.gr, 0,
+                                                 kvl_p, ptr(L["subln"]), ptr(L["lambda_full"]),
+                                                 L["lambda_full"].numel(), L["lambda_init"],
+                                                 self.args.attn_rms_norm_eps, ptr(self.attn), ptr(self.attn_ws),
+                                                 self.attn_ws_bytes, st), "gda_decode_attention")
+            L["o"](self.attn, out=self.o, workspace=self.lin_ws)
+            self._allreduce(self.o)
+            check(lib.motif_add_rms_norm(0, ptr(self.h), ptr(self.o), ptr(L["post_norm"]), eps, 1, H, ptr(self.x), st),
+                  "add_rms_norm")
+            L["gate_up"](self.x, out=self.gu, workspace=self.lin_ws)
+            self._polynorm_mul(L, st)
+            L["down"](self.act, out=self.dn, workspace=self.lin_ws)
+            self._allreduce(self.dn)
+            nxt = self.layers[li + 1]["input_norm"] if li + 1 < len(self.layers) else self.final_norm
+            check(lib.motif_add_rms_norm(0, ptr(self.h), ptr(self.dn), ptr(nxt), eps, 1, H, ptr(self.x), st),
+                  "add_rms_norm")
+        if with_head:
+            self.lm_head(self.x, out=self.logits, workspace=self.lin_ws)
+            check(lib.motif_argmax(0, ptr(self.logits), self.V, ptr(self.token), ptr(self.argmax_ws),
+                                   self.argmax_ws_bytes, st), "argmax")
+        self.pos_len.add_(self._one_one)
+
+    def _polynorm_mul(self, L, st) -> None:
+        if self.tp_group is not None:
+            self._polynorm_mul_tp(L)
+            return
+        I = self.inter
+        gp = self.gu.data_ptr()
+        check(lib.motif_polynorm_mul(0, gp, gp + 2 * I, 2 * I, ptr(L["polynorm_w"]), ptr(L["polynorm_b"]), 1e-6, 1, I,
+                                     ptr(self.act), st), "polynorm_mul")
+
+    def _polynorm_mul_tp(self, L) -> None:
+        # Full-row PolyNorm statistics over the sharded intermediate axis: all-reduce
+        # (Σx², Σx⁴, Σx⁶) then apply locally (torch glue; NCCL carries 12 bytes).
+        I = self.inter
+        g = self.gu[:I].float()
+        u = self.gu[I:].float()
+        g2 = g * g
+        stats = torch.stack([g2.sum(), (g2 * g2).sum(), (g2 * g2 * g2).sum()])
+        self._allreduce(stats)
+        n = float(self.args.intermediate_size)
+        eps = 1e-6
+        r2, r4, r6 = (torch.rsqrt(stats / n + eps)).unbind(0)
+        w = L["polynorm_w"].float()
+        b = L["polynorm_b"].float()
+        act = w[0] * (g2 * g * r6) + w[1] * (g2 * r4) + w[2] * (g * r2) + b[0]
+        self.act.copy_((act.half().float() * u).half())
+
+    # ------------------------------------------------------------------ #
+    def _graph(self, with_head: bool) -> torch.cuda.CUDAGraph:
+        g = self._graphs.get(with_head)
+        if g is None:
+            # Warm up once outside capture (function attributes, NCCL comm init), then restore state.
+            saved = (self.pos_len.clone(), self.token.clone(), self.h.clone())
+            self._launch_step(with_head)
+            self.pos_len.copy_(saved[0])
+            self.token.copy_(saved[1])
+            torch.cuda.synchronize(self.device)
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                self._launch_step(with_head)
+            self._graphs[with_head] = g
+        return g
+
+    def reset(self) -> None:
+        self.pos_len.copy_(torch.tensor([0, 1], dtype=torch.int32))
+        self.offset = 0
+        for c in self.caches:
+            c.offset = 0
+
+    def _bump_host(self, n: int = 1) -> None:
+        self.offset += n
+        for c in self.caches:
+            c.offset = self.offset
+
+    def step_device(self, with_head: bool = True) -> None:
+        """One decode step from ``self.token`` (device); the argmax lands back in ``self.token``."""
+        if self.offset >= self.max_seq:
+            raise ValueError(f"KV capacity {self.max_seq} exhausted")
+        self._graph(with_head).replay()
+        self._bump_host()
+
+    def step_eager(self, with_head: bool = True) -> None:
+        """Same step launched kernel by kernel (no graph) — for debugging and tests."""
+        if self.offset >= self.max_seq:
+            raise ValueError(f"KV capacity {self.max_seq} exhausted")
+        self._launch_step(with_head)
+        self._bump_host()
+
+    def prefill(self, ids) -> None:
+        """Feed prompt tokens through the decode path (causal, one position at a time)."""
+        ids_d = torch.as_tensor(ids, dtype=torch.int32).reshape(-1).to(self.device)
+        for i in range(ids_d.numel()):
+            self.token.copy_(ids_d[i : i + 1])
+            self.step_device(with_head=(i == ids_d.numel() - 1))
+
+    def decode_host(self, token: int) -> int:
+        """Public per-token API with host buffers: H2D token, one graph replay, D2H argmax, sync."""
+        self.pinned_in[0] = int(token)
+        self.token.copy_(self.pinned_in, non_blocking=True)
+        self.step_device(with_head=True)
+        self.pinned_out.copy_(self.token, non_blocking=True)
+        torch.cuda.current_stream(self.device).synchronize()
+        return int(self.pinned_out[0])
+
+    def generate(self, prompt_ids, n_tokens: int) -> list[int]:
+        """Greedy generation: prefill the prompt, then n_tokens argmax steps (device-resident)."""
+        self.prefill(prompt_ids)
+        out = [int(self.token.item())]
+        toks = []
+        for _ in range(n_tokens - 1):
+            self.step_device(with_head=True)
+            toks.append(self.token.clone())
+        out += [int(t.item()) for t in toks]
+        return out
+
+    def fill_cache_synthetic(self, n: int, seed: int = 0, std: float = 0.5) -> None:
+        """Fill the first n cache rows of every layer with N(0,1)·std keys/values (a stand-in
+        for a long prompt's KV; decode cost does not depend on the values) and set the position."""
+        if n >= self.max_seq:
+            raise ValueError("synthetic fill must leave room to decode")
+        gen = torch.Generator(device=self.device)
+        gen.manual_seed(seed)
+        for c in self.caches:
+            for slot_name in ("k1", "k2", "v1", "v2"):
+                rows = torch.randn((1, self.kv_heads, n, self.d), generator=gen, device=self.device) * std
+                rows = rows.half()
+                slot = getattr(c, slot_name)
+                if self.cache_kind == "fp16":
+                    slot[:, :, :n].copy_(rows)
+                else:
+                    dq, sc, bi = quantize(rows, 64, c.bits)
+                    slot[0][:, :, :n].copy_(dq)
+                    slot[1][:, :, :n].copy_(sc)
+                    slot[2][:, :, :n].copy_(bi)
+        self.pos_len[0] = n
+        self.pos_len[1] = n + 1
+        self.offset = n
+        for c in self.caches:
+            c.offset = n
+
+    # ------------------------------------------------------------------ #
+    @classmethod
+    def random(cls, args: ModelArgs, seed: int = 0, std: float = 0.02, cache: str = "fp16", max_seq: int = 4096,
+               device="cuda", tp_group=None, rank: int = 0, world: int = 1) -> "MotifDecoder":
+        """Random-init weights (std 0.02) generated and quantized (q4, g64) on the GPU.
+
+        With TP, every rank draws the same global tensors layer by layer (same seed)
+        and keeps its shard, so the sharded model equals the unsharded one.
+        """
+        dev = torch.device(device)
+        gen = torch.Generator(device=dev)
+        gen.manual_seed(seed)
+        f16 = torch.float16
+        a = args
+        H, I, d = a.hidden_size, a.intermediate_size, a.d
+        G, gr, Hk = a.num_noise_heads, a.grouped_ratio, a.k_noise_heads
+
+        def randn(*shape):
+            return (torch.randn(shape, generator=gen, device=dev, dtype=torch.float32) * std).to(f16)
+
+        def qlin(w):
+            return QuantizedLinear(*quantize(w, 64, 4))
+
+        def norm_w(n):
+            return (1.0 + 0.02 * torch.randn(n, generator=gen, device=dev)).to(f16)
+
+        plan = tp_shard_plan(args, rank, world)
+        layers = []
+        for li in range(a.num_hidden_layers):
+            qkv = randn(a.qkv_out, H)
+            o = randn(H, a.q_origin * 2 * d)
+            gate = randn(I, H)
+            up = randn(I, H)
+            down = randn(H, I)
+            if world > 1:
+                qkv = qkv.index_select(0, plan["qkv_rows"].to(dev))
+                o = o[:, plan["o_cols"][0]:plan["o_cols"][1]].contiguous()
+                r0, r1 = plan["mlp_rows"]
+                gate = gate[r0:r1].contiguous()
+                up = up[r0:r1].contiguous()
+                down = down[:, r0:r1].contiguous()
+            lam_init = lambda_init_for_layer(li)
+            lp = [torch.randn(d, generator=gen, device=dev) * 0.1 for _ in range(4)]
+            layers.append(dict(
+                input_norm=norm_w(H), post_norm=norm_w(H),
+                qkv=qlin(qkv), o=qlin(o), gate_up=qlin(torch.cat([gate, up])), down=qlin(down),
+                subln=norm_w(2 * d), lambda_init=lam_init, lambda_full=lambda_full(*lp, lam_init),
+                polynorm_w=torch.full((3,), 1 / 3, dtype=f16, device=dev),
+                polynorm_b=torch.zeros(1, dtype=f16, device=dev),
+            ))
+            del qkv, o, gate, up, down
+        weights = dict(embed=randn(a.vocab_size, H), final_norm=norm_w(H), lm_head=qlin(randn(a.vocab_size, H)),
+                       layers=layers)
+        return cls(args, weights, cache=cache, max_seq=max_seq, device=dev, tp_group=tp_group)
+
+
+def motif_12_7b_args(**overrides) -> ModelArgs:
+    """12.7B-class grouped config of the bench (8 KV heads per slot; see ModelArgs defaults)."""
+    return ModelArgs(**overrides)

@@ -1,0 +1,171 @@
+"""Host-side logic on CPU: ModelArgs validation, the attention-path truth table,
+λ helpers, the tensor-parallel shard plan, and a world-size-2 gloo run of the
+TP decode algorithm (oracle math, real torch.distributed collectives)."""
+
+from __future__ import annotations
+
+import os
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+import oracle as O
+
+
+def test_model_args_validation():
+    from mlx_motif.model import ModelArgs
+
+    a = ModelArgs()
+    assert (a.grouped_ratio, a.q_heads, a.q_origin, a.k_noise_heads, a.kv_repeat, a.qkv_out) == (3, 32, 24, 8, 1,
+                                                                                                   8192)
+    with pytest.raises(ValueError, match="hidden_size must be greater than zero"):
+        ModelArgs(hidden_size=0)
+    with pytest.raises(ValueError, match="must be an integer"):
+        ModelArgs(num_hidden_layers=2.0)
+    with pytest.raises(ValueError, match="greater than num_noise_heads"):
+        ModelArgs(num_attention_heads=8, num_noise_heads=8)
+    with pytest.raises(ValueError, match="divisible by num_noise_heads"):
+        ModelArgs(num_attention_heads=30, num_noise_heads=8)
+    with pytest.raises(ValueError, match="k_ratio"):
+        ModelArgs(k_ratio=0)
+    with pytest.raises(ValueError, match="multiple of k_ratio"):
+        ModelArgs(num_key_value_heads=15)
+    with pytest.raises(ValueError, match="even"):
+        ModelArgs(num_noise_heads=None, num_attention_heads=15, num_key_value_heads=15, head_dim=None,
+                  hidden_size=30)
+    lit = ModelArgs(num_key_value_heads=8)  # BASELINE's literal "8 KV heads" reading
+    assert lit.kv_repeat == 2
+
+
+def test_resolve_attention_path_truth_table():
+    from mlx_motif.cache import MotifGroupedKVCache, MotifGroupedQuantizedKVCache
+    from mlx_motif.model import AttnPath, _resolve_attention_path
+
+    q, f = MotifGroupedQuantizedKVCache(64, 4), MotifGroupedKVCache()
+    R = _resolve_attention_path
+    assert R(q, 1, 1, 1, False, env={}) is AttnPath.QUANT_SDPA
+    assert R(q, 1, 1, 1, False, env={"MLX_MOTIF_QUANT_SDPA": "0"}) is AttnPath.DUAL_V
+    assert R(q, 1, 1, 1, False, env={"MLX_MOTIF_QUANT_SDPA": "0", "MLX_MOTIF_DUAL_V": "false"}) is AttnPath.FALLBACK
+    assert R(f, 1, 1, 1, False, env={}) is AttnPath.DUAL_V
+    assert R(f, 5, 1, 1, False, env={}) is AttnPath.FALLBACK
+    assert R(f, 1, 2, 1, False, env={}) is AttnPath.FALLBACK
+    assert R(q, 1, 1, 2, False, env={}) is AttnPath.FALLBACK
+    assert R(q, 1, 1, 1, True, env={}) is AttnPath.FALLBACK
+    assert R(None, 1, 1, 1, False, env={}) is AttnPath.DUAL_V
+
+
+def test_lambda_helpers_match_oracle():
+    from mlx_motif.model import lambda_full, lambda_init_for_layer, origin_first_perm
+
+    for li in (0, 1, 7, 47):
+        assert lambda_init_for_layer(li) == O.lambda_init_for_layer(li)
+    rng = np.random.default_rng(0)
+    lp = [rng.standard_normal(128).astype(np.float32) * 0.1 for _ in range(4)]
+    got = lambda_full(*(torch.from_numpy(x) for x in lp), 0.65)
+    np.testing.assert_allclose(got.numpy(), O.lambda_full(*lp, 0.65), rtol=1e-6)
+    np.testing.assert_array_equal(origin_first_perm(8, 3, 128).numpy(), O.origin_first_perm(8, 3, 128))
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_tp_shard_plan_matches_oracle_sharding(world):
+    from mlx_motif.model import ModelArgs, tp_shard_plan
+
+    oa = O.OracleArgs(hidden_size=128, num_hidden_layers=1, intermediate_size=512, vocab_size=50)
+    ma = ModelArgs(hidden_size=128, num_hidden_layers=1, intermediate_size=512, vocab_size=50)
+    w = O.make_synthetic_weights(oa, seed=0)
+    for rank in range(world):
+        sh = O.shard_weights_tp(oa, w, rank, world)["layers"][0]
+        plan = tp_shard_plan(ma, rank, world)
+        L = w["layers"][0]
+        np.testing.assert_array_equal(L["qkv"][0][plan["qkv_rows"].numpy()], sh["qkv"][0])
+        c0, c1 = plan["o_cols"]
+        np.testing.assert_array_equal(L["o"][0][:, c0 // 8:c1 // 8], sh["o"][0])
+        r0, r1 = plan["mlp_rows"]
+        np.testing.assert_array_equal(L["gate"][0][r0:r1], sh["gate"][0])
+        np.testing.assert_array_equal(L["down"][1][:, r0 // 64:r1 // 64], sh["down"][1])
+
+
+# ---------------------------------------------------------------- gloo TP decode
+def _tp_layer(args, L, h, cache, rank, world, inv_freq):
+    """One decode layer on this rank's shard; all-reduces where the engine does."""
+    f16 = np.float16
+    d, gr = args.head_dim, args.grouped_ratio
+    G = args.num_noise_heads // world
+    Hk = args.kv_heads_per_slot // world
+    lin = lambda x, t: O.quantized_matmul(x, *t, 64, 4).astype(f16)  # noqa: E731
+    x = O.rms_norm(h, L["input_norm"]).astype(f16)
+    qkv = lin(x, L["qkv"])
+    qd, kd = G * (gr + 1) * d, 2 * Hk * d
+    q = qkv[..., :qd].reshape(1, 1, -1, d).transpose(0, 2, 1, 3)
+    k = qkv[..., qd:qd + kd].reshape(1, 1, -1, d).transpose(0, 2, 1, 3)
+    v = qkv[..., qd + kd:].reshape(1, 1, -1, d).transpose(0, 2, 1, 3)
+    off = cache.offset
+    q = O.rope(q, off, inv_freq=inv_freq).astype(f16)
+    k = O.rope(k, off, inv_freq=inv_freq).astype(f16)
+    K1, K2, V1, V2 = cache.update_and_fetch_4(k[:, 0::2], k[:, 1::2], v[:, 0::2], v[:, 1::2])
+    n = cache.offset
+    ao = O.sdpa_dual_v_reference(q[:, :G * gr], K1, V1, V2, d ** -0.5, n).astype(f16)
+    an = O.sdpa_dual_v_reference(q[:, G * gr:], K2, V1, V2, d ** -0.5, n).astype(f16)
+    out = O.gda_post_split_reference(ao, an, L["subln"], L["lambda_full"], L["lambda_init"], gr).astype(f16)
+    o = torch.from_numpy(O.quantized_matmul(out.transpose(0, 2, 1, 3).reshape(1, -1), *L["o"], 64, 4))
+    dist.all_reduce(o)  # row-parallel o_proj
+    h = (h.astype(np.float32) + o.numpy().astype(f16).astype(np.float32)).astype(f16)
+    x2 = O.rms_norm(h, L["post_norm"]).astype(f16)
+    g = lin(x2, L["gate"]).astype(np.float64)
+    u = lin(x2, L["up"])
+    g2 = g * g
+    stats = torch.tensor([g2.sum(), (g2 * g2).sum(), (g2 ** 3).sum()], dtype=torch.float64)
+    dist.all_reduce(stats)  # PolyNorm statistics over the full intermediate row
+    r2, r4, r6 = (1.0 / np.sqrt(stats.numpy() / args.intermediate_size + 1e-6))
+    w = L["polynorm_w"].astype(np.float64)
+    act = (w[0] * g2 * g * r6 + w[1] * g2 * r4 + w[2] * g * r2).astype(f16)
+    act = (act.astype(np.float64) * u.astype(np.float64)).astype(f16)
+    dn = torch.from_numpy(O.quantized_matmul(act, *L["down"], 64, 4))
+    dist.all_reduce(dn)  # row-parallel down_proj
+    return (h.astype(np.float32) + dn.numpy().astype(f16).astype(np.float32)).astype(f16)
+
+
+def _tp_worker(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        args = O.OracleArgs(hidden_size=128, num_hidden_layers=2, intermediate_size=256, num_noise_heads=8,
+                            grouped_ratio=3, kv_heads_per_slot=8, head_dim=128, vocab_size=64)
+        w = O.shard_weights_tp(args, O.make_synthetic_weights(args, seed=3, std=0.05), rank, world)
+        caches = [O.OracleGroupedKVCache() for _ in range(args.num_hidden_layers)]
+        inv = O.rope_inv_freq(128)
+        logits_seq = []
+        for tok in (1, 7, 9):
+            h = w["embed"][tok][None, :].astype(np.float16)
+            for li, L in enumerate(w["layers"]):
+                h = _tp_layer(args, L, h, caches[li], rank, world, inv)
+            hn = O.rms_norm(h, w["final_norm"]).astype(np.float16)
+            logits_seq.append(O.quantized_matmul(hn, *w["lm_head"], 64, 4).astype(np.float16)[0])
+        if rank == 0:
+            q.put(np.stack(logits_seq))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_tp2_gloo_decode_equals_single_rank():
+    """Sharded decode over 2 gloo ranks (all-reduce after o_proj, down_proj and of the
+    PolyNorm statistics) reproduces the unsharded oracle decode."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = 29500 + (os.getpid() % 1000)
+    procs = [ctx.Process(target=_tp_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    tp_logits = q.get(timeout=240)
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    args = O.OracleArgs(hidden_size=128, num_hidden_layers=2, intermediate_size=256, num_noise_heads=8,
+                        grouped_ratio=3, kv_heads_per_slot=8, head_dim=128, vocab_size=64)
+    ref = O.GroupedDecodeOracle(args, O.make_synthetic_weights(args, seed=3, std=0.05))
+    for i, tok in enumerate((1, 7, 9)):
+        logits, _ = ref.step(tok)
+        np.testing.assert_allclose(tp_logits[i].astype(np.float32), logits.astype(np.float32), atol=2e-2, rtol=2e-2)
