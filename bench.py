@@ -63,6 +63,10 @@ def parse_args():
     ap.add_argument("--no-long", action="store_true", help="skip the p16k extras")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--layers", type=int, default=48, help="(debug) model depth; 48 is the benchmark")
+    ap.add_argument("--prompt", type=int, default=164, help="prompt length (164 = config[1])")
+    ap.add_argument("--profile", action="store_true",
+                    help="profiler window only: cudaProfilerStart/Stop around the timed steps, then exit "
+                         "(for `ncu --profile-from-start off`)")
     return ap.parse_args()
 
 
@@ -251,62 +255,67 @@ def cpu_baseline(threads: int = 1) -> dict:
 # --------------------------------------------------------------------------- #
 # B200 arm
 # --------------------------------------------------------------------------- #
-def time_gemvs(model, reps: int = 3) -> dict:
-    """CUDA-event time of one step's GEMV launches (every layer's qkv, o, gate|up, down + lm_head)."""
+def _graph_time(fn, reps: int = 5) -> float:
+    """Best CUDA-event time (ms) of replaying a graph that captured fn() once."""
     import torch
 
-    lins = [(L[k], inp) for L in model.layers for k, inp in
-            (("qkv", model.x), ("o", model.attn), ("gate_up", model.x), ("down", model.act))]
-    lins.append((model.lm_head, model.x))
-    outs = {id(q): torch.empty(q.out_dim, dtype=torch.float16, device=model.device) for q, _ in lins}
-    alg = 0
-    for q, _ in lins:
-        alg += q.nbytes() + 2 * q.in_dim + 2 * q.out_dim
-    for q, inp in lins:  # warm
-        q(inp[: q.in_dim], out=outs[id(q)], workspace=model.lin_ws)
+    fn()
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        fn()
+    g.replay()
     torch.cuda.synchronize()
     st = torch.cuda.current_stream()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     best = math.inf
     for _ in range(reps):
         e0.record(st)
-        for q, inp in lins:
-            q(inp[: q.in_dim], out=outs[id(q)], workspace=model.lin_ws)
+        g.replay()
         e1.record(st)
         e1.synchronize()
         best = min(best, e0.elapsed_time(e1))
+    del g
+    return best
+
+
+def time_gemvs(model) -> dict:
+    """CUDA-event time of one step's GEMV launches (every layer's qkv, o, gate|up, down + lm_head),
+    replayed from a CUDA graph so host launch cost is excluded."""
+    import torch
+
+    lins = [(L[k], inp) for L in model.layers for k, inp in
+            (("qkv", model.x), ("o", model.attn), ("gate_up", model.x), ("down", model.act))]
+    lins.append((model.lm_head, model.x))
+    outs = {id(q): torch.empty(q.out_dim, dtype=torch.float16, device=model.device) for q, _ in lins}
+    alg = sum(q.nbytes() + 2 * q.in_dim + 2 * q.out_dim for q, _ in lins)
+
+    def run():
+        for q, inp in lins:
+            q(inp[: q.in_dim], out=outs[id(q)], workspace=model.lin_ws)
+
+    best = _graph_time(run)
     n = len(lins)
     return {"launches": n, "ms_total": best, "ms_per_launch": best / n, "bytes_total": alg,
             "bytes_per_launch": alg / n, "gbs": alg / (best / 1e3) / 1e9}
 
 
-def time_attention(model, reps: int = 5) -> dict:
-    """CUDA-event time of the 48 layers' fused attention (2 kernels each) at the current kv_len."""
-    import torch
-
+def time_attention(model) -> dict:
+    """CUDA-event time (graph replay) of the 48 layers' fused attention at the current kv_len."""
     from mlx_motif._native import check, lib, ptr, stream
 
     kv_len = int(model.pos_len[1].item())
-    st = stream(model.device)
     kvl_p = model.pos_len.data_ptr() + 4
 
     def run():
+        st = stream(model.device)
         for li, L in enumerate(model.layers):
             check(lib.motif_gda_decode_attention(ptr(model.q), model._slots[li], model.scale, model.q_groups, model.gr,
                                                  0, kvl_p, ptr(L["subln"]), ptr(L["lambda_full"]),
                                                  L["lambda_full"].numel(), L["lambda_init"], 1e-5, ptr(model.attn),
                                                  ptr(model.attn_ws), model.attn_ws_bytes, st))
 
-    run()
-    torch.cuda.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    best = math.inf
-    for _ in range(reps):
-        e0.record()
-        run()
-        e1.record()
-        e1.synchronize()
-        best = min(best, e0.elapsed_time(e1))
+    best = _graph_time(run)
     kv_bytes = model.kv_bytes_per_token(kv_len)
     return {"kv_len": kv_len, "ms_48_layers": best, "bytes": kv_bytes, "gbs": kv_bytes / (best / 1e3) / 1e9}
 
@@ -341,6 +350,8 @@ def run_b200(a) -> None:
     rank, world, local, group = dist_setup(a.gpus)
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
+    global PROMPT_LEN
+    PROMPT_LEN = a.prompt
     margin = a.warmup * 2 + a.steps * 2 + 16
     args = ModelArgs(num_hidden_layers=a.layers)
     t_init = time.time()
@@ -354,6 +365,16 @@ def run_b200(a) -> None:
         model.step_device()
     torch.cuda.synchronize()
     barrier(world)
+
+    if a.profile:
+        torch.cuda.cudart().cudaProfilerStart()
+        for _ in range(a.steps):
+            model.step_device()
+        torch.cuda.synchronize()
+        torch.cuda.cudart().cudaProfilerStop()
+        if rank == 0:
+            print(json.dumps({"profile_steps": a.steps, "kernels_per_step": model_launches(args, world)}))
+        return
 
     sampler = ClockSampler(local) if rank == 0 else None
     if sampler:

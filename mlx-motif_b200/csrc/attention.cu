@@ -583,3 +583,4 @@ int motif_gda_decode_attention(const void* q, const motif_kv4_slots* cache, floa
 }
 
 }  // extern "C"
+
