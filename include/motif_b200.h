@@ -119,6 +119,27 @@ MOTIF_API int motif_sdpa_dual_v(int dtype, const void* q, const void* k, const v
                       int64_t head_dim, int64_t kv_len, const int32_t* kv_len_dev, void* y,
                       void* workspace, size_t workspace_bytes, void* stream);
 
+/* Allocation-free variant of motif_sdpa_dual_v, for callers that cannot call
+ * cudaMalloc (a plugin whose device memory belongs to its host framework's
+ * allocator, code running during someone else's stream capture, hot paths
+ * that must not take cudaMalloc's device-wide synchronisation). It has no
+ * counterpart in the reference. Its split-KV partials live in one
+ * file-scope __device__ array of motif_sdpa_dual_v_static_scratch_bytes()
+ * (4 MiB) that each GPU loading the library keeps until exit. The first
+ * call on a device resolves the array's device address (call it once
+ * before any stream capture). Shapes whose two-split partials
+ * (batch*h_q*(2*head_dim+2)*4*2 bytes) exceed the array are rejected with
+ * MOTIF_ERR_WORKSPACE. Nothing in the array needs to start at zero (every
+ * split writes its partial before the merge reads it), but all calls share
+ * it: calls that overlap on the GPU (different streams, or devices sharing
+ * nothing else) race and must be serialised by the caller. Otherwise the
+ * same arguments and results as motif_sdpa_dual_v. */
+MOTIF_API size_t motif_sdpa_dual_v_static_scratch_bytes(void);
+MOTIF_API int motif_sdpa_dual_v_static(int dtype, const void* q, const void* k, const void* v1,
+                                       const void* v2, float scale, int64_t batch, int64_t h_q,
+                                       int64_t h_kv, int64_t kv_cap, int64_t head_dim, int64_t kv_len,
+                                       const int32_t* kv_len_dev, void* y, void* stream);
+
 /* Same attention reading MLX affine-quantized K, V1, V2 triples directly
  * (bits 4 or 8). Replaces sdpa_dual_v_q4 (attention.py:510-645) with the same
  * shape contract (attention.py:556-608): D % 32 == 0, D % group_size == 0,

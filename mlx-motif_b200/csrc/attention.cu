@@ -584,3 +584,70 @@ int motif_gda_decode_attention(const void* q, const motif_kv4_slots* cache, floa
 
 }  // extern "C"
 
+// ---------------------------------------------------------------------------
+// Allocation-free variant of motif_sdpa_dual_v.
+//
+// Some callers cannot call cudaMalloc at all: a plugin whose device memory
+// belongs to the host framework's own allocator, code that runs while
+// someone else's stream is being captured into a CUDA graph (an allocation
+// there breaks or escapes the capture), and hot paths that must not take
+// cudaMalloc's implicit device synchronisation. For them the split-KV
+// partials live in this file-scope device array instead of a caller
+// workspace. It is sized once for the library (kStaticScratchBytes) and
+// every GPU that loads the library holds it until the process exits.
+// ---------------------------------------------------------------------------
+namespace motif {
+namespace {
+
+constexpr size_t kStaticScratchBytes = 4u << 20;  // 4 MiB of split partials
+static __device__ __align__(256) float g_attn_scratch[kStaticScratchBytes / sizeof(float)];
+
+constexpr int kMaxDevices = 64;
+static void* g_scratch_ptr[kMaxDevices] = {};
+
+// Host code may not use g_attn_scratch as a device address: it names the
+// host-side stand-in. Resolve the device address once per device, with that
+// device current (this first call must not sit inside a stream capture).
+int static_scratch(void** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return fail(MOTIF_ERR_CUDA, "sdpa_dual_v_static: cudaGetDevice: %s", cudaGetErrorString(e));
+  if (dev < 0 || dev >= kMaxDevices) return fail(MOTIF_ERR_CUDA, "sdpa_dual_v_static: device %d out of range", dev);
+  if (!g_scratch_ptr[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_attn_scratch);
+    if (e != cudaSuccess || !p)
+      return fail(MOTIF_ERR_CUDA, "sdpa_dual_v_static: cudaGetSymbolAddress: %s", cudaGetErrorString(e));
+    g_scratch_ptr[dev] = p;
+  }
+  *out = g_scratch_ptr[dev];
+  return MOTIF_OK;
+}
+
+}  // namespace
+}  // namespace motif
+
+extern "C" {
+
+size_t motif_sdpa_dual_v_static_scratch_bytes(void) { return motif::kStaticScratchBytes; }
+
+int motif_sdpa_dual_v_static(int dtype, const void* q, const void* k, const void* v1, const void* v2,
+                             float scale, int64_t batch, int64_t h_q, int64_t h_kv, int64_t kv_cap,
+                             int64_t head_dim, int64_t kv_len, const int32_t* kv_len_dev, void* y,
+                             void* stream) {
+  MOTIF_REQUIRE(q && k && v1 && v2 && y, MOTIF_ERR_NULL, "sdpa_dual_v_static: null pointer");
+  int rc = check_common(batch, h_q, h_kv, kv_cap, head_dim, kv_len, kv_len_dev);
+  if (rc) return rc;
+  const size_t two_splits = partial_bytes(batch * h_q, head_dim, 2);
+  MOTIF_REQUIRE(two_splits <= kStaticScratchBytes, MOTIF_ERR_WORKSPACE,
+                "sdpa_dual_v_static: batch*h_q=%lld rows at head_dim %lld need %zu bytes of split "
+                "scratch, more than the %zu-byte static array; call motif_sdpa_dual_v with a workspace",
+                (long long)(batch * h_q), (long long)head_dim, two_splits, kStaticScratchBytes);
+  void* scratch = nullptr;
+  rc = static_scratch(&scratch);
+  if (rc) return rc;
+  return motif_sdpa_dual_v(dtype, q, k, v1, v2, scale, batch, h_q, h_kv, kv_cap, head_dim, kv_len,
+                           kv_len_dev, y, scratch, kStaticScratchBytes, stream);
+}
+
+}  // extern "C"

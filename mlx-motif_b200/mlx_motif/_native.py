@@ -54,6 +54,8 @@ SIGNATURES = {
     "motif_gda_post": (_I, [_I, _P, _P, _P, _L, _F, _L, _L, _L, _L, _L, _F, _P, _P]),
     "motif_sdpa_dual_v_workspace_bytes": (_S, [_L, _L, _L, _L]),
     "motif_sdpa_dual_v": (_I, [_I, _P, _P, _P, _P, _F, _L, _L, _L, _L, _L, _L, _P, _P, _P, _S, _P]),
+    "motif_sdpa_dual_v_static_scratch_bytes": (_S, []),
+    "motif_sdpa_dual_v_static": (_I, [_I, _P, _P, _P, _P, _F, _L, _L, _L, _L, _L, _L, _P, _P, _P]),
     "motif_sdpa_dual_v_q": (
         _I,
         [_I, _I, _I, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _F, _L, _L, _L, _L, _L, _L, _P, _P, _P, _S, _P],
