@@ -64,6 +64,7 @@ def parse_args():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--layers", type=int, default=48, help="(debug) model depth; 48 is the benchmark")
     ap.add_argument("--prompt", type=int, default=164, help="prompt length (164 = config[1])")
+    ap.add_argument("--vocab", type=int, default=219520, help="(profiling) vocabulary size; 219520 is the benchmark")
     ap.add_argument("--profile", action="store_true",
                     help="profiler window only: cudaProfilerStart/Stop around the timed steps, then exit "
                          "(for `ncu --profile-from-start off`)")
@@ -353,7 +354,7 @@ def run_b200(a) -> None:
     global PROMPT_LEN
     PROMPT_LEN = a.prompt
     margin = a.warmup * 2 + a.steps * 2 + 16
-    args = ModelArgs(num_hidden_layers=a.layers)
+    args = ModelArgs(num_hidden_layers=a.layers, vocab_size=a.vocab)
     t_init = time.time()
     model = MotifDecoder.random(args, seed=0, cache=a.cache, max_seq=PROMPT_LEN + margin + 8, device=dev,
                                 tp_group=group, rank=rank, world=world)

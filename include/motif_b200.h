@@ -209,14 +209,68 @@ MOTIF_API int motif_rope(int dtype, const void* x, int64_t batch, int64_t heads,
  * y (m, n) = x (m, k) · dequant(W)ᵀ with W in the nn.QuantizedLinear layout:
  * w (n, k*bits/32) uint32, scales/biases (n, k/group_size) in dtype. Replaces
  * mx.quantized_matmul behind nn.QuantizedLinear (every linear of the decoder,
- * model.py:437-442, 262-264, 894; fused qkv 1017-1079). bits 4, group 64;
- * fp16; m ≤ 8 (decode / verify rows). */
+ * model.py:437-442, 262-264, 894; fused qkv 1017-1079). Fast path: bits 4,
+ * group 64, fp16, k % 128 == 0 (persistent stream-K GEMV; rows of x run one
+ * after another); other bits/groups/dtypes take a CUDA-core path. The
+ * workspace (motif_quantized_linear_workspace_bytes) must be zero-filled
+ * before its first use; the kernel leaves it zeroed. */
 MOTIF_API size_t motif_quantized_linear_workspace_bytes(int64_t m, int64_t n, int64_t k, int bits,
                                               int group_size);
 MOTIF_API int motif_quantized_linear(int dtype, int bits, int group_size, const void* x, int64_t m,
                            int64_t k, const uint32_t* w, const void* scales, const void* biases,
                            int64_t n, void* y, void* workspace, size_t workspace_bytes,
                            void* stream);
+
+/* Fused decode linear: the q4 GEMV of motif_quantized_linear (bits 4, group 64,
+ * fp16, one input row) with the input vector built in its prologue and an
+ * optional statistics epilogue, so the decoder's norms and activations need no
+ * kernels of their own. Replaces, per layer of MotifDecoderLayer
+ * (model.py:845-855): input_layernorm + qkv_proj (mode 1), o_proj (mode 0),
+ * residual + post_attention_layernorm + gate/up (mode 1 + stats), PolyNorm·up
+ * + down_proj (mode 2, model.py:267-268); final norm + lm_head (mode 1,
+ * model.py:879, 905).
+ *   mode 0: x given.
+ *   mode 1: v = (token ? embed[*token] : h_in) + delta (delta may be NULL, the
+ *           sum rounded to fp16 as the reference's residual add); x =
+ *           rms_norm(v)·norm_w (eps); v is written to h_out when non-NULL
+ *           (h_out must not alias h_in).
+ *   mode 2: x = fp16(polynorm(gate))·up, PolyNorm statistics = the sum of
+ *           stats_count (Σg², Σg⁴, Σg⁶) triplets at `stats`, mean over poly_dim.
+ * stats_out (optional): for output rows [0, stats_rows) (a multiple of 16),
+ * one (Σy², Σy⁴, Σy⁶) triplet per 16-row tile of the fp16-rounded outputs.
+ * workspace: motif_linear_fused_workspace_bytes(n, k) bytes, zero-filled
+ * before first use (the kernel leaves its counters zeroed). Its first 64 KiB
+ * hold per-tile counters at a fixed place, so one workspace sized for the
+ * largest shape serves GEMVs of every shape in turn; launched with programmatic
+ * stream serialization, it starts streaming weights while the previous kernel
+ * finishes. */
+typedef struct motif_linear_io {
+  int32_t mode;
+  const void* x;
+  const void* h_in;
+  const int32_t* token;
+  const void* embed;
+  int64_t vocab;
+  const void* delta;
+  void* h_out;
+  const void* norm_w;
+  float eps;
+  const void* gate;
+  const void* up;
+  const float* stats;
+  int64_t stats_count;
+  const void* poly_w;
+  const void* poly_b;
+  float poly_eps;
+  int64_t poly_dim;
+  float* stats_out;
+  int64_t stats_rows;
+} motif_linear_io;
+
+MOTIF_API size_t motif_linear_fused_workspace_bytes(int64_t n, int64_t k);
+MOTIF_API int motif_linear_fused(const motif_linear_io* io, const uint32_t* w, const void* scales,
+                                 const void* biases, int64_t n, int64_t k, void* y, void* workspace,
+                                 size_t workspace_bytes, void* stream);
 
 /* ---- decoder glue (model.py:845-905) ---------------------------------------- */
 /* y = rms_norm(x) * w (nn.RMSNorm, model.py:850-851, 864). */

@@ -93,6 +93,7 @@ template <typename T, int D, int BITS, int MAXA, int NB>
 __global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(AttnArgs a) {
   constexpr int CPL = D / 32;
   constexpr int NH = MAXA + NB;
+  pdl_trigger();
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int split = blockIdx.x, nsplit = gridDim.x;
   const int b = blockIdx.y / a.h_kv, hk = blockIdx.y % a.h_kv;
@@ -241,27 +242,58 @@ __global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(AttnArgs a) {
   }
 }
 
-// Merge split partials into the final (B, h_out, 2D) output.
+constexpr int kMaxSplits = 64;
+
+// Split weights of one head: f[s] = 2^(m_s − M), M = max_s m_s, and L = Σ l_s f[s],
+// computed by one warp (two splits per lane) into shared memory.
+__device__ __forceinline__ void split_weights(const float* __restrict__ base, int n_active, int stride,
+                                              float* f_out, float* L_out, int lane) {
+  const float m0 = lane < n_active ? base[lane * stride] : -INFINITY;
+  const float m1 = lane + 32 < n_active ? base[(lane + 32) * stride] : -INFINITY;
+  const float l0 = lane < n_active ? base[lane * stride + 1] : 0.f;
+  const float l1 = lane + 32 < n_active ? base[(lane + 32) * stride + 1] : 0.f;
+  const float M = warp_max(fmaxf(m0, m1));
+  const float f0 = (M != -INFINITY && m0 != -INFINITY) ? exp2f(m0 - M) : 0.f;
+  const float f1 = (M != -INFINITY && m1 != -INFINITY) ? exp2f(m1 - M) : 0.f;
+  const float L = warp_sum(l0 * f0 + l1 * f1);
+  f_out[lane] = f0;
+  f_out[lane + 32] = f1;
+  if (lane == 0) *L_out = L;
+}
+
+// Σ_s f[s] · o_s[ch] with independent loads (4 splits in flight per step).
+__device__ __forceinline__ float merge_channel(const float* __restrict__ base, const float* f, int n_active,
+                                              int stride, int ch) {
+  float o0 = 0.f, o1 = 0.f, o2 = 0.f, o3 = 0.f;
+  int s = 0;
+  for (; s + 4 <= n_active; s += 4) {
+    o0 += f[s] * base[s * stride + 2 + ch];
+    o1 += f[s + 1] * base[(s + 1) * stride + 2 + ch];
+    o2 += f[s + 2] * base[(s + 2) * stride + 2 + ch];
+    o3 += f[s + 3] * base[(s + 3) * stride + 2 + ch];
+  }
+  for (; s < n_active; ++s) o0 += f[s] * base[s * stride + 2 + ch];
+  return (o0 + o1) + (o2 + o3);
+}
+
+// Merge split partials into the final (B, h_out, 2D) output; one CTA of 2D threads per row.
 template <typename T, int D>
 __global__ void attn_combine_kernel(const float* __restrict__ ws, int nsplit, int kv_len_host,
                                     const int32_t* __restrict__ kv_len_dev, T* __restrict__ y) {
+  __shared__ float f_s[kMaxSplits];
+  __shared__ float L_s;
+  pdl_trigger();
   const int64_t bh = blockIdx.x;
   const int ch = threadIdx.x;
   const int kv_len = kv_len_dev ? *kv_len_dev : kv_len_host;
   int p0, p1, n_active;
   split_range(kv_len, nsplit, 0, p0, p1, n_active);
-  const float* base = ws + bh * nsplit * (2 * D + 2);
-  float M = -INFINITY;
-  for (int s = 0; s < n_active; ++s) M = fmaxf(M, base[s * (2 * D + 2)]);
-  float L = 0.f, O = 0.f;
-  for (int s = 0; s < n_active; ++s) {
-    const float* p = base + s * (2 * D + 2);
-    if (p[0] == -INFINITY) continue;
-    const float f = exp2f(p[0] - M);
-    L += p[1] * f;
-    O += p[2 + ch] * f;
-  }
-  y[bh * 2 * D + ch] = from_f<T>(L > 0.f ? O / L : 0.f);
+  constexpr int stride = 2 * D + 2;
+  const float* base = ws + bh * nsplit * stride;
+  if (threadIdx.x < 32) split_weights(base, n_active, stride, f_s, &L_s, threadIdx.x);
+  __syncthreads();
+  const float O = merge_channel(base, f_s, n_active, stride, ch);
+  y[bh * 2 * D + ch] = from_f<T>(L_s > 0.f ? O / L_s : 0.f);
 }
 
 // Merge split partials of one GDA group and apply gda_post_split:
@@ -275,27 +307,27 @@ __global__ void gda_combine_kernel(const float* __restrict__ ws, int nsplit, int
                                    const float* __restrict__ lam, int lam_mode, float out_scale,
                                    float eps, __half* __restrict__ out) {
   __shared__ float scratch[32 * GR];
+  __shared__ float f_s[GR + 1][kMaxSplits];
+  __shared__ float L_s[GR + 1];
+  pdl_trigger();
   const int g = blockIdx.x;
   const int ch = threadIdx.x;  // 0 .. 2D-1
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int kv_len = kv_len_dev ? *kv_len_dev : kv_len_host;
   int p0, p1, n_active;
   split_range(kv_len, nsplit, 0, p0, p1, n_active);
+  constexpr int stride = 2 * D + 2;
+  if (warp <= GR) {
+    const int head = warp < GR ? g * GR + warp : q_origin + g;
+    split_weights(ws + (int64_t)head * nsplit * stride, n_active, stride, f_s[warp], &L_s[warp], lane);
+  }
+  __syncthreads();
   float val[GR + 1];
 #pragma unroll
   for (int j = 0; j <= GR; ++j) {
     const int head = j < GR ? g * GR + j : q_origin + g;
-    const float* base = ws + (int64_t)head * nsplit * (2 * D + 2);
-    float M = -INFINITY;
-    for (int s = 0; s < n_active; ++s) M = fmaxf(M, base[s * (2 * D + 2)]);
-    float L = 0.f, O = 0.f;
-    for (int s = 0; s < n_active; ++s) {
-      const float* p = base + s * (2 * D + 2);
-      if (p[0] == -INFINITY) continue;
-      const float f = exp2f(p[0] - M);
-      L += p[1] * f;
-      O += p[2 + ch] * f;
-    }
-    val[j] = round_through<__half>(L > 0.f ? O / L : 0.f);
+    const float O = merge_channel(ws + (int64_t)head * nsplit * stride, f_s[j], n_active, stride, ch);
+    val[j] = round_through<__half>(L_s[j] > 0.f ? O / L_s[j] : 0.f);
   }
   float d[GR], ssq[GR];
 #pragma unroll
@@ -343,6 +375,7 @@ int choose_splits(int64_t groups, int64_t len_bound, int64_t max_splits) {
   int64_t by_len = ceil_div(len_bound < 1 ? 1 : len_bound, kMinChunk);
   int64_t n = want < by_len ? want : by_len;
   if (n > max_splits) n = max_splits;
+  if (n > kMaxSplits) n = kMaxSplits;
   if (n < 1) n = 1;
   return (int)n;
 }

@@ -99,6 +99,12 @@ __device__ __forceinline__ void store_vec(T* p, const float (&in)[N]) {
   }
 }
 
+// Programmatic dependent launch: let the next kernel in the stream (if it was
+// launched with programmatic stream serialization) start its independent
+// prologue — the quantized GEMV streams its weights — while this one runs. The
+// dependent still waits for this grid's completion before reading its outputs.
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;\n"); }
+
 // ---- reductions ----------------------------------------------------------------
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll

@@ -232,6 +232,7 @@ __device__ __forceinline__ Best warp_best(Best x) {
 template <typename T>
 __global__ void argmax_partial_kernel(const T* __restrict__ x, int64_t n, Best* __restrict__ part) {
   __shared__ Best sm[32];
+  pdl_trigger();
   Best best{-INFINITY, 0x7fffffff};
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
        i += (int64_t)gridDim.x * blockDim.x) {

@@ -1,29 +1,42 @@
 // Affine-quantized linear y = x · dequant(W)ᵀ in the nn.QuantizedLinear
 // layout (W (N, K·bits/32) uint32, scales/biases (N, K/g)).
 //
-// Decode fast path (bits 4, group 64, K % 128 == 0, fp16): HBM-streaming GEMV.
-//   * A warp owns 16 output rows and a range of 512-wide K blocks. Each lane
-//     streams 16-byte chunks of two rows (r, r+8) straight into registers,
-//     double-buffered one block ahead.
-//   * Nibbles become exact fp16 integers with the 0x6400 magic-exponent trick
-//     (one LOP3 per nibble pair, one HSUB2/HFMA2 to remove the offset) and feed
-//     mma.sync.m16n8k16 (fp16 × fp16 → fp32). The MMA is only a wide FMA here:
-//     the kernel stays bound by HBM, and without it the per-nibble
-//     convert+FMA work would make it issue-bound.
-//   * The B operand's 8 columns are the 8 quantization groups of the block: a
-//     lane feeds x only into the column of the group its k values belong to,
-//     so column n accumulates Σ_{k∈g} x_k q_k for group g = 8·blk + n exactly
-//     in fp32. Scales and biases are then applied per group in fp32:
-//        y_n = Σ_g s_ng · dot_ng + b_ng · Σ_{k∈g} x_k
-//     which is the affine quantized matmul formula (MLX qmv), not a
-//     dequantize-to-fp16 approximation.
+// Decode fast path (bits 4, group 64, K % 128 == 0, fp16): a persistent
+// HBM-streaming GEMV.
+//   * Work unit = (16-row tile, 512-wide K block). Units are ordered tile-major
+//     and every warp of the grid takes one contiguous run of them (stream-K),
+//     so all warps stream the same number of bytes whatever N and K are.
+//   * A lane streams 16-byte chunks of its two rows (r, r+8) straight into
+//     registers, one unit ahead of the one it computes. The first unit's loads
+//     are issued before `griddepcontrol.wait`: launched with programmatic
+//     stream serialization, the kernel's weight stream starts while the
+//     previous kernel is still finishing, and only reading x waits for it.
+//   * Nibbles become exact fp16 integers with the 0x6400 magic exponent (one
+//     LOP3 per nibble pair, one HSUB2/HFMA2 to drop the offset) and feed
+//     mma.sync.m16n8k16 (fp16 × fp16 → fp32). The MMA is a wide FMA: without
+//     it the per-nibble convert+FMA work would make the kernel issue-bound.
+//   * The B operand's 8 columns are the 8 quantization groups of a K block:
+//     a lane feeds x only into the column of the group its k values belong
+//     to, so column n accumulates Σ_{k∈g} x_k q_k for group g = 8·blk + n
+//     exactly in fp32, and the affine epilogue y = Σ_g s·dot + b·Σx runs in
+//     fp32 (the MLX quantized-matmul formula).
+//   * A tile split across warps is finished by the last contributing warp:
+//     partials go to the workspace, an atomic counter per tile elects the
+//     last warp (no waiting), which sums the partials in slot order
+//     (deterministic), writes fp16 and resets the counter to zero.
 //   * x is staged once per CTA in shared memory, permuted to the nibble order
-//     the dequant produces, with per-group sums of x.
-//   * Split-K writes fp32 partials that a small kernel (or the consumer) sums.
+//     the dequant produces, with per-group sums. Optional prologues build x
+//     in place: rms_norm(h + delta)·w (residual + norm, optionally gathering
+//     h from the embedding table), or polynorm(gate)·up from per-tile
+//     (Σg², Σg⁴, Σg⁶) statistics. An optional epilogue writes those
+//     statistics for output rows [0, stats_rows) (the gate half of a fused
+//     gate|up projection).
 //
 // General path (bits 4/8, group 32/64/128, any K % 32 == 0): CUDA-core GEMV,
 // one warp per output row, exact fp32 per-nibble MACs. Used for shapes the
 // fast path does not cover.
+#include <cuda.h>
+
 #include "common.cuh"
 
 namespace motif {
@@ -62,37 +75,92 @@ __device__ __forceinline__ void mma16816(float (&c)[4], uint32_t a0, uint32_t a1
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
-constexpr int kGemvWarps = 4;
-constexpr int kGemvThreads = kGemvWarps * 32;
-constexpr int kRowsPerWarp = 16;
-constexpr int kRowsPerCta = kGemvWarps * kRowsPerWarp;  // 64
-constexpr int kBlockK = 512;
+__device__ __forceinline__ void grid_dep_wait() { asm volatile("griddepcontrol.wait;\n" ::: "memory"); }
+__device__ __forceinline__ void grid_dep_launch() { asm volatile("griddepcontrol.launch_dependents;\n"); }
 
-struct BlockRegs {
-  uint4 wr[4];   // row r:   chunk q (32 nibbles) of this block
-  uint4 wr8[4];  // row r+8
-  uint32_t s, s8, b, b8;  // half2 scales / biases of groups (g0, g0+1), rows r and r+8
+constexpr int kWarps = 8;
+constexpr int kThreads = kWarps * 32;
+constexpr int kBlockK = 512;
+constexpr int kTileRows = 16;
+// Workspace layout: [tile counters: kCounterTiles int32][split-K partials]. The
+// counter region has a fixed size so that GEMVs of different shapes can share
+// one workspace: partials of one shape never land on another shape's counters.
+constexpr int64_t kCounterTiles = 16384;  // N up to 262144 rows
+constexpr size_t kCounterBytes = sizeof(int) * kCounterTiles;
+
+enum : int { kModeX = 0, kModeAddRms = 1, kModePoly = 2 };
+
+struct LinArgs {
+  // TMA descriptors of the weight codes, scales and biases (TMA kernel only).
+  alignas(64) CUtensorMap tm_w;
+  alignas(64) CUtensorMap tm_s;
+  alignas(64) CUtensorMap tm_b;
+  int* err;  // set non-zero if a TMA wait ran out (the kernel then stops early)
+  const uint32_t* w;
+  const __half* sc;
+  const __half* bi;
+  int64_t N, K;
+  int nblk, ntiles;
+  int64_t units;
+  int total_warps;
+  __half* y;
+  float* partial;  // [ntiles][maxc][16]
+  int* counters;   // [ntiles], zero between calls
+  int maxc;
+  // prologue
+  int mode;
+  const __half* x;
+  const __half* h_in;
+  const int32_t* token;
+  const __half* embed;
+  int64_t vocab;
+  const __half* delta;
+  __half* h_out;
+  const __half* norm_w;
+  float eps;
+  const __half* gate;
+  const __half* up;
+  const float* stats;
+  int stats_count;
+  const __half* poly_w;
+  const __half* poly_b;
+  float poly_eps;
+  float poly_inv_dim;
+  // epilogue
+  float* stats_out;
+  int64_t stats_rows;
 };
 
-__device__ __forceinline__ void load_block(BlockRegs& R, const uint32_t* __restrict__ w,
-                                           const __half* __restrict__ sc,
-                                           const __half* __restrict__ bi, int64_t row_r,
-                                           int64_t row_r8, int64_t wpr, int64_t gpr, int blk,
-                                           int quarters, int c) {
+struct UnitRegs {
+  uint4 wr[4];
+  uint4 wr8[4];
+  uint32_t s, s8, b, b8;
+};
+
+__device__ __forceinline__ int quarters_of(const LinArgs& a, int blk) {
+  const int64_t rem = a.K - (int64_t)blk * kBlockK;
+  return rem >= kBlockK ? 4 : (int)(rem / 128);
+}
+
+__device__ __forceinline__ void load_unit(UnitRegs& R, const LinArgs& a, int tile, int blk, int r, int c) {
+  const int64_t row_r = min((int64_t)tile * kTileRows + r, a.N - 1);
+  const int64_t row_r8 = min((int64_t)tile * kTileRows + r + 8, a.N - 1);
+  const int64_t wpr = a.K / 8, gpr = a.K / 64;
+  const int quarters = quarters_of(a, blk);
 #pragma unroll
   for (int q = 0; q < 4; ++q) {
     if (q < quarters) {
       const int64_t word = (int64_t)blk * 64 + q * 16 + c * 4;
-      R.wr[q] = __ldg(reinterpret_cast<const uint4*>(w + row_r * wpr + word));
-      R.wr8[q] = __ldg(reinterpret_cast<const uint4*>(w + row_r8 * wpr + word));
+      R.wr[q] = __ldg(reinterpret_cast<const uint4*>(a.w + row_r * wpr + word));
+      R.wr8[q] = __ldg(reinterpret_cast<const uint4*>(a.w + row_r8 * wpr + word));
     }
   }
   const int64_t g0 = (int64_t)blk * 8 + 2 * c;
   if (g0 < gpr) {
-    R.s = __ldg(reinterpret_cast<const uint32_t*>(sc + row_r * gpr + g0));
-    R.s8 = __ldg(reinterpret_cast<const uint32_t*>(sc + row_r8 * gpr + g0));
-    R.b = __ldg(reinterpret_cast<const uint32_t*>(bi + row_r * gpr + g0));
-    R.b8 = __ldg(reinterpret_cast<const uint32_t*>(bi + row_r8 * gpr + g0));
+    R.s = __ldg(reinterpret_cast<const uint32_t*>(a.sc + row_r * gpr + g0));
+    R.s8 = __ldg(reinterpret_cast<const uint32_t*>(a.sc + row_r8 * gpr + g0));
+    R.b = __ldg(reinterpret_cast<const uint32_t*>(a.bi + row_r * gpr + g0));
+    R.b8 = __ldg(reinterpret_cast<const uint32_t*>(a.bi + row_r8 * gpr + g0));
   }
 }
 
@@ -101,18 +169,18 @@ __device__ __forceinline__ float2 h2f(uint32_t v) {
   return __half22float2(h);
 }
 
-// One 512-wide K block of one warp: 32 MMAs, then the per-group affine epilogue.
-__device__ __forceinline__ void compute_block(const BlockRegs& R, const __half* __restrict__ xp_s,
-                                              const float* __restrict__ xsum_s, int blk, int blk0,
-                                              int quarters, int64_t gpr, int c, int q_lane,
-                                              float& acc_r, float& acc_r8) {
-  // This lane's x chunk (permuted fp16): only needed by lanes whose quarter exists.
+// One unit: 32 MMAs over a 512-wide K block, then the per-group affine epilogue.
+__device__ __forceinline__ void compute_unit(const UnitRegs& R, const LinArgs& a, int blk,
+                                             const __half* __restrict__ xp_s,
+                                             const float* __restrict__ xsum_s, int c, int q_lane,
+                                             float& acc_r, float& acc_r8) {
+  const int quarters = quarters_of(a, blk);
   uint32_t xr[16];
   if (q_lane >= 0 && q_lane < quarters) {
-    const uint4* src = reinterpret_cast<const uint4*>(xp_s + (blk - blk0) * kBlockK + q_lane * 128 + c * 32);
+    const uint4* src = reinterpret_cast<const uint4*>(xp_s + (int64_t)blk * kBlockK + q_lane * 128 + c * 32);
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-      uint4 v = src[i];
+      const uint4 v = src[i];
       xr[4 * i + 0] = v.x;
       xr[4 * i + 1] = v.y;
       xr[4 * i + 2] = v.z;
@@ -143,108 +211,520 @@ __device__ __forceinline__ void compute_block(const BlockRegs& R, const __half* 
     }
   }
   const int64_t g0 = (int64_t)blk * 8 + 2 * c;
-  if (g0 < gpr) {
-    const int lg = (int)(g0 - (int64_t)blk0 * 8);
-    const float xs0 = xsum_s[lg], xs1 = xsum_s[lg + 1];
+  if (g0 < a.K / 64) {
+    const float xs0 = xsum_s[g0], xs1 = xsum_s[g0 + 1];
     const float2 s = h2f(R.s), s8 = h2f(R.s8), b = h2f(R.b), b8 = h2f(R.b8);
     acc_r += s.x * C[0] + s.y * C[1] + b.x * xs0 + b.y * xs1;
     acc_r8 += s8.x * C[2] + s8.y * C[3] + b8.x * xs0 + b8.y * xs1;
   }
 }
 
-// grid (ceil(N / 64), ksplit); dynamic smem: permuted x of the CTA's K range + group sums.
-__global__ void __launch_bounds__(kGemvThreads) q4_gemv_mma_kernel(
-    const __half* __restrict__ x, int64_t K, const uint32_t* __restrict__ w,
-    const __half* __restrict__ sc, const __half* __restrict__ bi, int64_t N, int blocks_per_split,
-    __half* __restrict__ y, float* __restrict__ partial) {
-  extern __shared__ __align__(16) unsigned char smem_raw[];
-  const int nblk = (int)((K + kBlockK - 1) / kBlockK);
-  const int blk0 = blockIdx.y * blocks_per_split;
-  const int blk1 = min(nblk, blk0 + blocks_per_split);
-  const int64_t k0 = (int64_t)blk0 * kBlockK;
-  const int64_t k1 = min(K, (int64_t)blk1 * kBlockK);
-  const int64_t klen = k1 - k0;  // multiple of 128
-  __half* xp_s = reinterpret_cast<__half*>(smem_raw);
-  float* xsum_s = reinterpret_cast<float*>(smem_raw + (size_t)blocks_per_split * kBlockK * sizeof(__half));
+// The warp whose unit range [u·W/U, (u+1)·W/U) contains unit u (32-bit: the host
+// guarantees units · total_warps < 2^32).
+__device__ __forceinline__ int warp_of_unit(uint32_t u, uint32_t units, uint32_t tw) {
+  return (int)(((u + 1) * tw - 1) / units);
+}
 
-  // ---- stage x: permute each 8-value word to (x0,x4,x1,x5,x2,x6,x3,x7); group sums ----
-  for (int64_t wi = threadIdx.x; wi < klen / 8; wi += kGemvThreads) {
-    const uint4 v = *reinterpret_cast<const uint4*>(x + k0 + wi * 8);
-    const __half* e = reinterpret_cast<const __half*>(&v);
-    uint4 o;
-    __half* oe = reinterpret_cast<__half*>(&o);
-    oe[0] = e[0]; oe[1] = e[4]; oe[2] = e[1]; oe[3] = e[5];
-    oe[4] = e[2]; oe[5] = e[6]; oe[6] = e[3]; oe[7] = e[7];
-    *reinterpret_cast<uint4*>(xp_s + wi * 8) = o;
-  }
-  for (int64_t g = threadIdx.x; g < klen / 64; g += kGemvThreads) {
-    const uint4* src = reinterpret_cast<const uint4*>(x + k0 + g * 64);
-    float s = 0.f;
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const uint4 v = src[i];
-      const __half2* h = reinterpret_cast<const __half2*>(&v);
-#pragma unroll
-      for (int t = 0; t < 4; ++t) {
-        const float2 f = __half22float2(h[t]);
-        s += f.x + f.y;
-      }
-    }
-    xsum_s[g] = s;
-  }
-  __syncthreads();
-
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+// Finish this warp's share of a tile: write it, or publish a partial and let the last
+// contributing warp reduce. Also emits the tile's PolyNorm statistics when asked.
+__device__ void tile_epilogue(const LinArgs& a, int tile, int gw, float acc_r, float acc_r8, int lane) {
   const int r = lane >> 2, c = lane & 3;
-  const int64_t tile_row = (int64_t)blockIdx.x * kRowsPerCta + warp * kRowsPerWarp;
-  if (tile_row >= N) return;
-  const int64_t row_r = min(tile_row + r, N - 1);
-  const int64_t row_r8 = min(tile_row + r + 8, N - 1);
-  const int64_t wpr = K / 8, gpr = K / 64;
-  // The quarter whose group feeds this lane's B column (column r = group 2q + c/2).
-  const int diff = r - (c >> 1);
-  const int q_lane = (diff >= 0 && (diff & 1) == 0) ? diff >> 1 : -1;
-
-  float acc_r = 0.f, acc_r8 = 0.f;
-  auto quarters_of = [&](int blk) -> int {
-    const int64_t rem = K - (int64_t)blk * kBlockK;
-    return rem >= kBlockK ? 4 : (int)(rem / 128);
-  };
-  BlockRegs A, B;
-  if (blk0 < blk1) load_block(A, w, sc, bi, row_r, row_r8, wpr, gpr, blk0, quarters_of(blk0), c);
-  for (int blk = blk0; blk < blk1; blk += 2) {
-    const bool has1 = blk + 1 < blk1;
-    if (has1) load_block(B, w, sc, bi, row_r, row_r8, wpr, gpr, blk + 1, quarters_of(blk + 1), c);
-    compute_block(A, xp_s, xsum_s, blk, blk0, quarters_of(blk), gpr, c, q_lane, acc_r, acc_r8);
-    if (has1) {
-      if (blk + 2 < blk1) load_block(A, w, sc, bi, row_r, row_r8, wpr, gpr, blk + 2, quarters_of(blk + 2), c);
-      compute_block(B, xp_s, xsum_s, blk + 1, blk0, quarters_of(blk + 1), gpr, c, q_lane, acc_r, acc_r8);
-    }
-  }
   acc_r += __shfl_xor_sync(0xffffffffu, acc_r, 1);
   acc_r += __shfl_xor_sync(0xffffffffu, acc_r, 2);
   acc_r8 += __shfl_xor_sync(0xffffffffu, acc_r8, 1);
   acc_r8 += __shfl_xor_sync(0xffffffffu, acc_r8, 2);
-  if (c == 0) {
-    const int64_t n_r = tile_row + r, n_r8 = tile_row + r + 8;
-    if (partial) {
-      float* p = partial + (int64_t)blockIdx.y * N;
-      if (n_r < N) p[n_r] = acc_r;
-      if (n_r8 < N) p[n_r8] = acc_r8;
-    } else {
-      if (n_r < N) y[n_r] = __float2half_rn(acc_r);
-      if (n_r8 < N) y[n_r8] = __float2half_rn(acc_r8);
+  const uint32_t u_first = (uint32_t)tile * (uint32_t)a.nblk;
+  const int w_first = warp_of_unit(u_first, (uint32_t)a.units, (uint32_t)a.total_warps);
+  const int w_last = warp_of_unit(u_first + a.nblk - 1, (uint32_t)a.units, (uint32_t)a.total_warps);
+  const int nc = w_last - w_first + 1;
+  const int64_t row0 = (int64_t)tile * kTileRows;
+  // Final fp16 values of this tile's rows, held by lanes 0..15 (row = row0 + lane).
+  float v = 0.f;
+  bool have = false;
+  if (nc == 1) {
+    // Gather rows r / r+8 from the c == 0 lanes into lanes 0..15.
+    const float a_r = __shfl_sync(0xffffffffu, acc_r, (lane & 7) * 4);
+    const float a_r8 = __shfl_sync(0xffffffffu, acc_r8, (lane & 7) * 4);
+    v = lane < 8 ? a_r : a_r8;
+    have = lane < kTileRows;
+  } else {
+    const int slot = gw - w_first;
+    float* p = a.partial + ((int64_t)tile * a.maxc + slot) * kTileRows;
+    if (c == 0) {
+      p[r] = acc_r;
+      p[r + 8] = acc_r8;
+    }
+    // Publish: the warp barrier orders the lanes' stores before lane 0's release
+    // fence and counter increment (the last contributor acquires before reading).
+    __syncwarp();
+    int old = 0;
+    if (lane == 0) {
+      __threadfence();
+      old = atomicAdd(a.counters + tile, 1);
+    }
+    old = __shfl_sync(0xffffffffu, old, 0);
+    if (old == nc - 1) {
+      __threadfence();
+      if (lane < kTileRows) {
+        const float* base = a.partial + (int64_t)tile * a.maxc * kTileRows + lane;
+        float s = 0.f;
+        for (int i = 0; i < nc; ++i) s += __ldcg(base + i * kTileRows);
+        v = s;
+        have = true;
+      }
+      if (lane == 0) a.counters[tile] = 0;
+    }
+  }
+  const int64_t row = row0 + lane;
+  const __half hv = __float2half_rn(v);
+  if (have && row < a.N) a.y[row] = hv;
+  // all-or-nothing per warp: `have` is uniform across lanes 0..15 of the finishing warp
+  const bool any = __any_sync(0xffffffffu, have);
+  if (any && a.stats_out && row0 < a.stats_rows) {
+    const float f = (have && row < a.stats_rows) ? __half2float(hv) : 0.f;
+    const float f2 = f * f, f4 = f2 * f2;
+    float s2 = warp_sum(f2), s4 = warp_sum(f4), s6 = warp_sum(f4 * f2);
+    if (lane == 0) {
+      a.stats_out[tile * 3 + 0] = s2;
+      a.stats_out[tile * 3 + 1] = s4;
+      a.stats_out[tile * 3 + 2] = s6;
     }
   }
 }
 
-__global__ void splitk_reduce_kernel(const float* __restrict__ partial, int ksplit, int64_t N,
-                                     __half* __restrict__ y) {
-  const int64_t n = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (n >= N) return;
-  float s = 0.f;
-  for (int i = 0; i < ksplit; ++i) s += partial[(int64_t)i * N + n];
-  y[n] = __float2half_rn(s);
+// Build x (full K) in shared memory: each 8-value word permuted to the nibble order
+// the dequant produces (0,4,1,5,2,6,3,7), plus per-group sums of x.
+// V2 (TMA kernel) also pre-scales the odd-k ("hi" nibble) values by 1/16 and
+// writes corr[g] = 1024·Σ(stored values of group g): the dequant there feeds the
+// MMA 1024+q (even k) and 1024+16q (odd k), so Σ q·x = C − corr exactly.
+//
+// One round trip to memory: every input word a thread needs (at most
+// kMaxStageWords, i.e. K ≤ 8·256·kMaxStageWords) is loaded into registers
+// first; the row statistics are reduced from those registers; group sums come
+// from shuffles over the 8 consecutive threads that hold one group's words.
+// Largest K (in 8-value words per thread of a 256-thread CTA) each prologue supports.
+template <int MODE>
+struct StageWords {
+  static constexpr int value = MODE == 1 ? 4 : 8;
+};
+
+template <int MODE, bool V2>
+__device__ void stage_x(const LinArgs& a, __half* xp_s, float* xsum_s, float* corr_s, float* red) {
+  constexpr int kMaxStageWords = StageWords<MODE>::value;
+  const int64_t K = a.K;
+  const int words = (int)(K / 8);
+  const int nthr = blockDim.x;
+  const int tid = threadIdx.x;
+  uint4 in0[kMaxStageWords], in1[kMaxStageWords], in2[kMaxStageWords];
+  const __half* hsrc = a.h_in;
+  float stats_acc[3] = {0.f, 0.f, 0.f};
+  if (MODE == kModeAddRms && a.token) {
+    int64_t t = a.token[0];
+    if (t < 0 || t >= a.vocab) t = 0;  // out-of-range ids read row 0
+    hsrc = a.embed + t * K;
+  }
+  // ---- issue every load ----
+#pragma unroll
+  for (int i = 0; i < kMaxStageWords; ++i) {
+    const int wi = tid + i * nthr;
+    if (wi < words) {
+      if constexpr (MODE == kModeX) {
+        in0[i] = *reinterpret_cast<const uint4*>(a.x + (int64_t)wi * 8);
+      } else if constexpr (MODE == kModeAddRms) {
+        in0[i] = *reinterpret_cast<const uint4*>(hsrc + (int64_t)wi * 8);
+        in1[i] = a.delta ? *reinterpret_cast<const uint4*>(a.delta + (int64_t)wi * 8) : make_uint4(0, 0, 0, 0);
+        in2[i] = *reinterpret_cast<const uint4*>(a.norm_w + (int64_t)wi * 8);
+      } else {
+        in0[i] = *reinterpret_cast<const uint4*>(a.gate + (int64_t)wi * 8);
+        in1[i] = *reinterpret_cast<const uint4*>(a.up + (int64_t)wi * 8);
+      }
+    }
+  }
+  if (MODE == kModePoly) {
+    for (int i = tid; i < a.stats_count; i += nthr) {
+      stats_acc[0] += a.stats[i * 3 + 0];
+      stats_acc[1] += a.stats[i * 3 + 1];
+      stats_acc[2] += a.stats[i * 3 + 2];
+    }
+  }
+  // ---- row statistics ----
+  float inv = 1.f, r2 = 0.f, r4 = 0.f, r6 = 0.f, pw0 = 0.f, pw1 = 0.f, pw2 = 0.f, pb = 0.f;
+  if (MODE == kModeAddRms) {
+    float acc[1] = {0.f};
+#pragma unroll
+    for (int i = 0; i < kMaxStageWords; ++i) {
+      if (tid + i * nthr < words) {
+        const __half* hv = reinterpret_cast<const __half*>(&in0[i]);
+        const __half* dv = reinterpret_cast<const __half*>(&in1[i]);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const float v = a.delta ? round_through<__half>(__half2float(hv[j]) + __half2float(dv[j])) : __half2float(hv[j]);
+          acc[0] += v * v;
+        }
+      }
+    }
+    block_sum<1>(acc, red);
+    inv = rsqrtf(acc[0] / (float)K + a.eps);
+  } else if (MODE == kModePoly) {
+    block_sum<3>(stats_acc, red);
+    r2 = rsqrtf(stats_acc[0] * a.poly_inv_dim + a.poly_eps);
+    r4 = rsqrtf(stats_acc[1] * a.poly_inv_dim + a.poly_eps);
+    r6 = rsqrtf(stats_acc[2] * a.poly_inv_dim + a.poly_eps);
+    pw0 = __half2float(a.poly_w[0]);
+    pw1 = __half2float(a.poly_w[1]);
+    pw2 = __half2float(a.poly_w[2]);
+    pb = __half2float(a.poly_b[0]);
+  }
+  const bool write_h = MODE == kModeAddRms && a.h_out && blockIdx.x == 0;
+  // ---- build x, permute, group sums ----
+#pragma unroll
+  for (int i = 0; i < kMaxStageWords; ++i) {
+    const int wi = tid + i * nthr;
+    if (i * nthr >= words) break;  // uniform across the block
+    const bool act = wi < words;
+    __half h[8];
+    if (act) {
+      const __half* e0 = reinterpret_cast<const __half*>(&in0[i]);
+      const __half* e1 = reinterpret_cast<const __half*>(&in1[i]);
+      const __half* e2 = reinterpret_cast<const __half*>(&in2[i]);
+      if constexpr (MODE == kModeX) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) h[j] = e0[j];
+      } else if constexpr (MODE == kModeAddRms) {
+        float v[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+          v[j] = a.delta ? round_through<__half>(__half2float(e0[j]) + __half2float(e1[j])) : __half2float(e0[j]);
+        if (write_h) store_vec<__half, 8>(a.h_out + (int64_t)wi * 8, v);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) h[j] = __float2half_rn(v[j] * inv * __half2float(e2[j]));
+      } else {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const float g = __half2float(e0[j]);
+          const float g2 = g * g;
+          const float g3 = g2 * g;
+          const float p = pw0 * (g3 * r6) + pw1 * (g2 * r4) + pw2 * (g * r2) + pb;
+          h[j] = __float2half_rn(round_through<__half>(p) * __half2float(e1[j]));
+        }
+      }
+      if (V2) {
+        const __half sixteenth = __float2half_rn(0.0625f);
+#pragma unroll
+        for (int j = 1; j < 8; j += 2) h[j] = __hmul(h[j], sixteenth);
+      }
+      uint4 o;
+      __half* oe = reinterpret_cast<__half*>(&o);
+      oe[0] = h[0];
+      oe[1] = h[4];
+      oe[2] = h[1];
+      oe[3] = h[5];
+      oe[4] = h[2];
+      oe[5] = h[6];
+      oe[6] = h[3];
+      oe[7] = h[7];
+      *reinterpret_cast<uint4*>(xp_s + (int64_t)wi * 8) = o;
+    } else {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) h[j] = __float2half_rn(0.f);
+    }
+    // even-k (lo) and odd-k (hi) sums of this word, reduced over the group's 8 threads
+    float lo = 0.f, hi = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; j += 2) {
+      lo += __half2float(h[j]);
+      hi += __half2float(h[j + 1]);
+    }
+#pragma unroll
+    for (int o = 1; o < 8; o <<= 1) {
+      lo += __shfl_xor_sync(0xffffffffu, lo, o);
+      hi += __shfl_xor_sync(0xffffffffu, hi, o);
+    }
+    if (act && (wi & 7) == 0) {
+      const int g = wi >> 3;
+      if (V2) {
+        xsum_s[g] = lo + 16.f * hi;
+        corr_s[g] = 1024.f * (lo + hi);
+      } else {
+        xsum_s[g] = lo + hi;
+      }
+    }
+  }
+  __syncthreads();
+}
+
+template <int MODE>
+__global__ void __launch_bounds__(kThreads, 2) q4_gemv_kernel(LinArgs a) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  __half* xp_s = reinterpret_cast<__half*>(smem_raw);
+  float* xsum_s = reinterpret_cast<float*>(smem_raw + (size_t)a.K * sizeof(__half));
+  float* red = xsum_s + a.K / 64;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int r = lane >> 2, c = lane & 3;
+  const int gw = blockIdx.x * kWarps + warp;
+  const uint32_t units = (uint32_t)a.units, tw = (uint32_t)a.total_warps;
+  const int u0 = gw < a.total_warps ? (int)((uint32_t)gw * units / tw) : (int)units;
+  const int u1 = gw < a.total_warps ? (int)((uint32_t)(gw + 1) * units / tw) : (int)units;
+  const int nblk = a.nblk;
+  const int diff = r - (c >> 1);
+  const int q_lane = (diff >= 0 && (diff & 1) == 0) ? diff >> 1 : -1;
+
+  // Weights do not depend on the previous kernel: start streaming them first.
+  UnitRegs A, B;
+  int tile = u0 / nblk, blk = u0 - (u0 / nblk) * nblk;
+  if (u0 < u1) load_unit(A, a, tile, blk, r, c);
+  grid_dep_wait();
+  grid_dep_launch();
+  stage_x<MODE, false>(a, xp_s, xsum_s, nullptr, red);
+
+  float acc_r = 0.f, acc_r8 = 0.f;
+  for (int u = u0; u < u1; u += 2) {
+    const bool has1 = u + 1 < u1;
+    int t1 = tile, b1 = blk + 1;
+    if (b1 == nblk) { b1 = 0; ++t1; }
+    if (has1) load_unit(B, a, t1, b1, r, c);
+    compute_unit(A, a, blk, xp_s, xsum_s, c, q_lane, acc_r, acc_r8);
+    if (!has1 || t1 != tile) {
+      tile_epilogue(a, tile, gw, acc_r, acc_r8, lane);
+      acc_r = acc_r8 = 0.f;
+    }
+    if (has1) {
+      int t2 = t1, b2 = b1 + 1;
+      if (b2 == nblk) { b2 = 0; ++t2; }
+      if (u + 2 < u1) load_unit(A, a, t2, b2, r, c);
+      compute_unit(B, a, b1, xp_s, xsum_s, c, q_lane, acc_r, acc_r8);
+      if (u + 2 >= u1 || t2 != t1) {
+        tile_epilogue(a, t1, gw, acc_r, acc_r8, lane);
+        acc_r = acc_r8 = 0.f;
+      }
+      tile = t2;
+      blk = b2;
+    }
+  }
+}
+
+// ---- TMA variant: weights arrive in shared memory through a per-warp ring ------
+//
+// 8 warps per CTA and one CTA per SM, with a footprint (≈110 KB shared, 128
+// registers) that leaves room for the next kernel's CTA: launched with
+// programmatic serialization, it starts its own weight prefetch while this one
+// finishes. Each warp owns kStages ring slots of one
+// unit each — codes as two 128B-swizzled boxes of 16 rows × 128 B (so the
+// lanes' 8-byte reads are spread over the banks), scales and biases as
+// 16 × 16 B boxes — filled by 2D tiled TMA loads straight from the MLX layout
+// and tracked by one mbarrier per slot. Lane 0 refills a slot with the unit
+// kStages ahead as soon as the warp has read it.
+//
+// Compute: one MMA quad per quantization group. Lane (r, c) takes the 16
+// consecutive k of group g at 16c (two words per row), so a step's 16 k all
+// belong to one group and every B column carries the full x: C's columns are
+// all the group's dot products. Nibbles enter the MMA as fp16 1024+q (even k)
+// or 1024+16q (odd k, against x/16) — one LOP3 per nibble pair — and the
+// per-group constant 1024·Σx' is subtracted after the quad. Eight independent
+// quads per unit keep the tensor pipe and the scheduler busy.
+//
+// All mbarrier waits are bounded: on time-out the kernel records an error in
+// the workspace, lets its in-flight copies land (bounded) and stops.
+#ifndef MOTIF_GEMV_TMA_WARPS
+#define MOTIF_GEMV_TMA_WARPS 16
+#endif
+#ifndef MOTIF_GEMV_STAGES
+#define MOTIF_GEMV_STAGES 2
+#endif
+constexpr int kTmaWarps = MOTIF_GEMV_TMA_WARPS;
+constexpr int kTmaThreads = kTmaWarps * 32;
+constexpr int kStages = MOTIF_GEMV_STAGES;
+// Two CTAs per SM (so the next GEMV's prefetch can co-reside) when the ring is small enough.
+constexpr int kTmaMinBlocks = kTmaWarps * kStages <= 16 ? 2 : 1;
+constexpr int kTmaSmemCap = kTmaMinBlocks == 2 ? 113 * 1024 : 225 * 1024;
+constexpr int kSlotBytes = 5120;  // 2 × 2048 codes + 256 scales + 256 biases, 1 KiB aligned
+constexpr int kMaxPolls = 1 << 20;
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n" ::"r"(bar), "r"(count));
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(bar), "r"(bytes) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
+  for (int i = 0; i < kMaxPolls; ++i) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.b32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    if (ok) return true;
+  }
+  return false;
+}
+
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int x, int y, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];\n" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar)
+      : "memory");
+}
+
+__device__ __forceinline__ void issue_unit(const LinArgs& a, int tile, int blk, uint32_t slot, uint32_t bar) {
+  mbar_expect_tx(bar, 4096 + 256 + 256);
+  tma_load_2d(slot, &a.tm_w, blk * 256, tile * kTileRows, bar);
+  tma_load_2d(slot + 2048, &a.tm_w, blk * 256 + 128, tile * kTileRows, bar);
+  tma_load_2d(slot + 4096, &a.tm_s, blk * 16, tile * kTileRows, bar);
+  tma_load_2d(slot + 4352, &a.tm_b, blk * 16, tile * kTileRows, bar);
+}
+
+__device__ __forceinline__ uint2 lds64(const unsigned char* p) { return *reinterpret_cast<const uint2*>(p); }
+__device__ __forceinline__ uint4 lds128(const void* p) { return *reinterpret_cast<const uint4*>(p); }
+
+// Word of 8 nibbles -> (1024+n0, 1024+n4) (1024+16n1, 1024+16n5) (1024+n2, 1024+n6) (1024+16n3, 1024+16n7).
+__device__ __forceinline__ void dequant_word_offset(uint32_t w, uint32_t (&p)[4]) {
+  const uint32_t LO = 0x000F000Fu, HI = 0x00F000F0u, EX = 0x64006400u;
+  p[0] = lop3_and_or(w, LO, EX);
+  p[1] = lop3_and_or(w, HI, EX);
+  const uint32_t w8 = w >> 8;
+  p[2] = lop3_and_or(w8, LO, EX);
+  p[3] = lop3_and_or(w8, HI, EX);
+}
+
+// Address of lane c's 8 bytes of group gp (0..3) in row `row` of a 128B-swizzled 16 × 128 box.
+__device__ __forceinline__ const unsigned char* swz(const unsigned char* box, int row, int gp, int c) {
+  const int chunk = (2 * gp + (c >> 1)) ^ (row & 7);
+  return box + row * 128 + chunk * 16 + (c & 1) * 8;
+}
+
+__device__ __forceinline__ void compute_unit_tma(const unsigned char* slot, int blk,
+                                                 const __half* __restrict__ xp_s, const float* __restrict__ xsum_s,
+                                                 const float* __restrict__ corr_s, int r, int c, float& acc_r,
+                                                 float& acc_r8) {
+  const __half* xg = xp_s + (int64_t)blk * kBlockK + c * 16;
+  const int g0 = blk * 8;
+  // Operands of group g: the lane's 8 bytes of rows r and r+8, and its 16 x values.
+  uint2 wr = lds64(swz(slot, r, 0, c)), wr8 = lds64(swz(slot, r + 8, 0, c));
+  uint4 x0 = lds128(xg), x1 = lds128(xg + 8);
+  float a_r = 0.f, a_r8 = 0.f;
+#pragma unroll
+  for (int g = 0; g < 8; ++g) {
+    // Software pipeline: fetch group g+1's operands before group g's math.
+    uint2 nwr = wr, nwr8 = wr8;
+    uint4 nx0 = x0, nx1 = x1;
+    if (g + 1 < 8) {
+      const unsigned char* box = slot + ((g + 1) >> 2) * 2048;
+      nwr = lds64(swz(box, r, (g + 1) & 3, c));
+      nwr8 = lds64(swz(box, r + 8, (g + 1) & 3, c));
+      nx0 = lds128(xg + (g + 1) * 64);
+      nx1 = lds128(xg + (g + 1) * 64 + 8);
+    }
+    uint32_t P[4], P8[4], Q[4], Q8[4];
+    dequant_word_offset(wr.x, P);
+    dequant_word_offset(wr8.x, P8);
+    dequant_word_offset(wr.y, Q);
+    dequant_word_offset(wr8.y, Q8);
+    // Two independent accumulation chains per group (words 2c and 2c+1).
+    float C0[4] = {0.f, 0.f, 0.f, 0.f}, C1[4] = {0.f, 0.f, 0.f, 0.f};
+    mma16816(C0, P[0], P8[0], P[1], P8[1], x0.x, x0.y);
+    mma16816(C1, Q[0], Q8[0], Q[1], Q8[1], x1.x, x1.y);
+    mma16816(C0, P[2], P8[2], P[3], P8[3], x0.z, x0.w);
+    mma16816(C1, Q[2], Q8[2], Q[3], Q8[3], x1.z, x1.w);
+    // Every column of C holds the group's dot, so the four lanes of a row split the
+    // affine epilogue: lane c takes groups c and c+4 (the tile epilogue sums over c).
+    if ((g & 3) == c) {
+      const float corr = corr_s[g0 + g], xs = xsum_s[g0 + g];
+      const __half2 s2 = *reinterpret_cast<const __half2*>(slot + 4096 + r * 16 + (g & ~1) * 2);
+      const __half2 s28 = *reinterpret_cast<const __half2*>(slot + 4096 + (r + 8) * 16 + (g & ~1) * 2);
+      const __half2 b2 = *reinterpret_cast<const __half2*>(slot + 4352 + r * 16 + (g & ~1) * 2);
+      const __half2 b28 = *reinterpret_cast<const __half2*>(slot + 4352 + (r + 8) * 16 + (g & ~1) * 2);
+      const float sr = (g & 1) ? __high2float(s2) : __low2float(s2);
+      const float sr8 = (g & 1) ? __high2float(s28) : __low2float(s28);
+      const float br = (g & 1) ? __high2float(b2) : __low2float(b2);
+      const float br8 = (g & 1) ? __high2float(b28) : __low2float(b28);
+      a_r += sr * ((C0[0] + C1[0]) - corr) + br * xs;
+      a_r8 += sr8 * ((C0[2] + C1[2]) - corr) + br8 * xs;
+    }
+    wr = nwr;
+    wr8 = nwr8;
+    x0 = nx0;
+    x1 = nx1;
+  }
+  acc_r += a_r;
+  acc_r8 += a_r8;
+}
+
+template <int MODE>
+__global__ void __launch_bounds__(kTmaThreads, kTmaMinBlocks) q4_gemv_tma_kernel(const __grid_constant__ LinArgs a) {
+  // 1 KiB alignment (128B-swizzled TMA boxes); plain pointer arithmetic on the shared
+  // array keeps every slot/x access a shared-memory load.
+  extern __shared__ __align__(1024) unsigned char smem_tma[];
+  unsigned char* ring = smem_tma;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(ring + (size_t)kTmaWarps * kStages * kSlotBytes);
+  __half* xp_s = reinterpret_cast<__half*>(bars + kTmaWarps * kStages);
+  float* xsum_s = reinterpret_cast<float*>(xp_s + a.K);
+  float* corr_s = xsum_s + a.K / 64;
+  float* red = corr_s + a.K / 64;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int r = lane >> 2, c = lane & 3;
+  const int gw = blockIdx.x * kTmaWarps + warp;
+  const uint32_t units = (uint32_t)a.units, tw = (uint32_t)a.total_warps;
+  const int u0 = gw < a.total_warps ? (int)((uint32_t)gw * units / tw) : (int)units;
+  const int u1 = gw < a.total_warps ? (int)((uint32_t)(gw + 1) * units / tw) : (int)units;
+  const int nblk = a.nblk;
+  unsigned char* my_ring = ring + (size_t)warp * kStages * kSlotBytes;
+  uint64_t* my_bars = bars + warp * kStages;
+
+  if (lane == 0) {
+    for (int i = 0; i < kStages; ++i) mbar_init(smem_u32(&my_bars[i]), 1);
+    asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+  }
+  __syncwarp();
+  // (tile, blk) of the next unit to fetch; weights do not depend on the previous
+  // kernel, so the ring is filled before waiting for it.
+  int it = u0 / nblk, ib = u0 - (u0 / nblk) * nblk;
+  if (lane == 0) {
+    for (int i = 0; i < kStages && u0 + i < u1; ++i) {
+      issue_unit(a, it, ib, smem_u32(my_ring + i * kSlotBytes), smem_u32(&my_bars[i]));
+      if (++ib == nblk) { ib = 0; ++it; }
+    }
+  }
+  grid_dep_wait();
+  grid_dep_launch();
+  stage_x<MODE, true>(a, xp_s, xsum_s, corr_s, red);
+
+  float acc_r = 0.f, acc_r8 = 0.f;
+  bool ok = true;
+  int tile = u0 / nblk, blk = u0 - (u0 / nblk) * nblk;
+  for (int u = u0; u < u1; ++u) {
+    const int j = u - u0;
+    const int slot = j % kStages;
+    if (!mbar_wait(smem_u32(&my_bars[slot]), (uint32_t)((j / kStages) & 1))) {
+      ok = false;
+      // Let the copies still in flight (units after u, at most kStages-1) land before exiting (bounded).
+      for (int v = u + 1; v < u1 && v < u + kStages; ++v) {
+        const int jv = v - u0;
+        mbar_wait(smem_u32(&my_bars[jv % kStages]), (uint32_t)((jv / kStages) & 1));
+      }
+      break;
+    }
+    compute_unit_tma(my_ring + slot * kSlotBytes, blk, xp_s, xsum_s, corr_s, r, c, acc_r, acc_r8);
+    __syncwarp();
+    if (lane == 0 && u + kStages < u1) {
+      issue_unit(a, it, ib, smem_u32(my_ring + slot * kSlotBytes), smem_u32(&my_bars[slot]));
+      if (++ib == nblk) { ib = 0; ++it; }
+    }
+    if (u + 1 >= u1 || blk + 1 == nblk) {
+      tile_epilogue(a, tile, gw, acc_r, acc_r8, lane);
+      acc_r = acc_r8 = 0.f;
+    }
+    if (++blk == nblk) { blk = 0; ++tile; }
+  }
+  if (!ok && lane == 0 && a.err) atomicExch(a.err, 1);
 }
 
 // ---- general CUDA-core path: one warp per (row, m) --------------------------
@@ -280,35 +760,179 @@ __global__ void qlinear_general_kernel(const T* __restrict__ x, int64_t M, int64
   if (lane == 0) y[m * N + n] = from_f<T>(acc);
 }
 
-struct GemvPlan {
-  int ksplit;
-  int blocks_per_split;
+struct Plan {
+  int ctas;
+  int total_warps;
+  int64_t units;
+  int nblk, ntiles, maxc;
   size_t smem;
+  size_t ws_partial;  // bytes
+  size_t ws_counters;
 };
 
-GemvPlan plan_gemv(int64_t N, int64_t K) {
-  const int nblk = (int)ceil_div(K, kBlockK);
-  const int64_t ctas_n = ceil_div(N, kRowsPerCta);
-  // Enough CTAs to keep ~8 per SM streaming; at least 2 blocks (1024 K) per split.
-  int64_t want = ceil_div(148 * 8, ctas_n);
-  int64_t max_by_k = nblk / 2 > 0 ? nblk / 2 : 1;
-  int64_t ks = want < max_by_k ? want : max_by_k;
-  if (ks < 1) ks = 1;
-  int bps = (int)ceil_div(nblk, ks);
-  ks = ceil_div(nblk, bps);
-  GemvPlan p;
-  p.ksplit = (int)ks;
-  p.blocks_per_split = bps;
-  p.smem = (size_t)bps * kBlockK * sizeof(__half) + (size_t)bps * 8 * sizeof(float);
+int g_num_sms = 0;
+
+int num_sms() {
+  if (!g_num_sms) {
+    int dev = 0, n = 0;
+    if (cudaGetDevice(&dev) == cudaSuccess && cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess && n > 0)
+      g_num_sms = n;
+    else
+      g_num_sms = 148;
+  }
+  return g_num_sms;
+}
+
+Plan make_plan(int64_t N, int64_t K, int sms, int warps_per_cta) {
+  Plan p;
+  p.nblk = (int)ceil_div(K, kBlockK);
+  p.ntiles = (int)ceil_div(N, kTileRows);
+  p.units = (int64_t)p.ntiles * p.nblk;
+  int64_t ctas = sms;
+  if (ctas * warps_per_cta > p.units) ctas = ceil_div(p.units, warps_per_cta);
+  p.ctas = (int)(ctas < 1 ? 1 : ctas);
+  // With fewer units than warps, each working warp takes exactly one unit and the
+  // surplus warps (gw >= total_warps) stay idle, so every counted warp contributes.
+  p.total_warps = (int)(p.units < (int64_t)p.ctas * warps_per_cta ? p.units : (int64_t)p.ctas * warps_per_cta);
+  // Contributors per tile: a tile of nblk units meets at most ceil(nblk / min_units) + 1 warps.
+  const int64_t min_units = p.units / p.total_warps;
+  p.maxc = min_units > 0 ? (int)(ceil_div(p.nblk, min_units) + 1) : p.nblk + 1;
+  if (p.maxc > p.nblk + 1) p.maxc = p.nblk + 1;
+  p.smem = (size_t)K * sizeof(__half) + (size_t)(K / 64) * sizeof(float) + 32 * 3 * sizeof(float);
+  p.ws_partial = sizeof(float) * (size_t)p.ntiles * p.maxc * kTileRows;
+  p.ws_counters = sizeof(int) * (size_t)p.ntiles;
   return p;
 }
 
+size_t plan_ws_bytes(const Plan& p) { return kCounterBytes + p.ws_partial; }
+
 bool fast_path_ok(int dtype, int bits, int gs, int64_t K, const void* x, const void* w,
                   const void* sc, const void* bi) {
-  auto a = [](const void* p, int n) { return (reinterpret_cast<uintptr_t>(p) % n) == 0; };
-  return dtype == MOTIF_F16 && bits == 4 && gs == 64 && K % 128 == 0 && K <= (1 << 20) &&
-         a(x, 16) && a(w, 16) && a(sc, 4) && a(bi, 4);
+  auto al = [](const void* p, int n) { return (reinterpret_cast<uintptr_t>(p) % n) == 0; };
+  return dtype == MOTIF_F16 && bits == 4 && gs == 64 && K % 128 == 0 && K <= 16384 && (!x || al(x, 16)) &&
+         al(w, 16) && al(sc, 4) && al(bi, 4);
 }
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no libcuda link).
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encoder() {
+  static EncodeTiledFn fn = nullptr;
+  static bool tried = false;
+  if (!tried) {
+    tried = true;
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  }
+  return fn;
+}
+
+// 2D byte view (rows × inner_bytes, row pitch inner_bytes) with a box of box_rows × box_inner.
+bool encode_rows(CUtensorMap* m, const void* base, uint64_t inner_bytes, uint64_t rows, uint32_t box_inner,
+                 uint32_t box_rows, CUtensorMapSwizzle swizzle) {
+  EncodeTiledFn fn = encoder();
+  if (!fn) return false;
+  cuuint64_t dims[2] = {inner_bytes, rows};
+  cuuint64_t strides[1] = {inner_bytes};
+  cuuint32_t box[2] = {box_inner, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  return fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+size_t tma_smem_bytes(int64_t K) {
+  return 1024 + (size_t)kTmaWarps * kStages * kSlotBytes + (size_t)kTmaWarps * kStages * 8 + (size_t)K * 2 +
+         2 * (size_t)(K / 64) * 4 + 32 * 3 * 4;
+}
+
+// The TMA kernel needs K % 512 == 0 and 16-byte aligned rows of codes (K/2 bytes) and scales (K/32 bytes).
+bool try_tma(LinArgs& a) {
+  if (a.K % 512 || tma_smem_bytes(a.K) > (size_t)kTmaSmemCap) return false;
+  if ((reinterpret_cast<uintptr_t>(a.w) | reinterpret_cast<uintptr_t>(a.sc) | reinterpret_cast<uintptr_t>(a.bi)) % 16)
+    return false;
+  return encode_rows(&a.tm_w, a.w, (uint64_t)a.K / 2, (uint64_t)a.N, 128, kTileRows, CU_TENSOR_MAP_SWIZZLE_128B) &&
+         encode_rows(&a.tm_s, a.sc, (uint64_t)a.K / 32, (uint64_t)a.N, 16, kTileRows, CU_TENSOR_MAP_SWIZZLE_NONE) &&
+         encode_rows(&a.tm_b, a.bi, (uint64_t)a.K / 32, (uint64_t)a.N, 16, kTileRows, CU_TENSOR_MAP_SWIZZLE_NONE);
+}
+
+// Workspace bytes for shape (n, k): the larger of the two kernels' plans.
+size_t ws_bytes_for(int64_t n, int64_t k) {
+  const int sms = num_sms();
+  const Plan p8 = make_plan(n, k, sms, kWarps);
+  const Plan p16 = make_plan(n, k, sms, kTmaWarps);
+  size_t b = 0;
+  if (p8.units > p8.ntiles) b = plan_ws_bytes(p8);
+  if (k % 512 == 0 && p16.units > p16.ntiles && plan_ws_bytes(p16) > b) b = plan_ws_bytes(p16);
+  return b;
+}
+
+int launch_q4(LinArgs& a, void* workspace, size_t ws_bytes, cudaStream_t st) {
+  const bool tma = try_tma(a);
+  const Plan p = make_plan(a.N, a.K, num_sms(), tma ? kTmaWarps : kWarps);
+  if ((uint64_t)p.units * (uint64_t)p.total_warps >= (1ull << 32))
+    return fail(MOTIF_ERR_BAD_SHAPE, "quantized_linear: %lld x %lld too large", (long long)a.N, (long long)a.K);
+  a.nblk = p.nblk;
+  a.ntiles = p.ntiles;
+  a.units = p.units;
+  a.total_warps = p.total_warps;
+  a.maxc = p.maxc;
+  a.err = nullptr;
+  if (p.units > p.ntiles) {  // some tile may be split across warps
+    const size_t need = plan_ws_bytes(p);
+    if (!workspace || ws_bytes < need)
+      return fail(MOTIF_ERR_WORKSPACE, "quantized_linear: workspace %zu < %zu bytes", ws_bytes, need);
+    if (p.ntiles >= kCounterTiles)
+      return fail(MOTIF_ERR_BAD_SHAPE, "quantized_linear: n=%lld rows exceed %lld", (long long)a.N,
+                  (long long)((kCounterTiles - 1) * kTileRows));
+    a.counters = static_cast<int*>(workspace);
+    a.partial = reinterpret_cast<float*>(static_cast<char*>(workspace) + kCounterBytes);
+    a.err = a.counters + (kCounterTiles - 1);  // last counter slot doubles as the error word
+  } else {
+    a.counters = nullptr;
+    a.partial = nullptr;
+  }
+  static bool configured = false;
+  if (!configured) {
+    cudaError_t e = cudaSuccess;
+    for (auto k : {q4_gemv_kernel<0>, q4_gemv_kernel<1>, q4_gemv_kernel<2>})
+      if (e == cudaSuccess) e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024);
+    for (auto k : {q4_gemv_tma_kernel<0>, q4_gemv_tma_kernel<1>, q4_gemv_tma_kernel<2>})
+      if (e == cudaSuccess) e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, kTmaSmemCap);
+    if (e != cudaSuccess) return fail(MOTIF_ERR_CUDA, "quantized_linear: smem attribute: %s", cudaGetErrorString(e));
+    configured = true;
+  }
+  const int64_t max_k = 8LL * 256 * (a.mode == kModeAddRms ? StageWords<1>::value : StageWords<0>::value);
+  if (a.K > max_k)
+    return fail(MOTIF_ERR_BAD_SHAPE, "quantized_linear: K=%lld exceeds %lld for prologue mode %d", (long long)a.K,
+                (long long)max_k, a.mode);
+  if (!tma && p.smem > 160 * 1024) return fail(MOTIF_ERR_BAD_SHAPE, "quantized_linear: K=%lld too large", (long long)a.K);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(p.ctas);
+  cfg.blockDim = dim3(tma ? kTmaThreads : kThreads);
+  cfg.dynamicSmemBytes = tma ? tma_smem_bytes(a.K) : p.smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e;
+  switch (a.mode) {
+    case kModeX: e = tma ? cudaLaunchKernelEx(&cfg, q4_gemv_tma_kernel<0>, a) : cudaLaunchKernelEx(&cfg, q4_gemv_kernel<0>, a); break;
+    case kModeAddRms: e = tma ? cudaLaunchKernelEx(&cfg, q4_gemv_tma_kernel<1>, a) : cudaLaunchKernelEx(&cfg, q4_gemv_kernel<1>, a); break;
+    default: e = tma ? cudaLaunchKernelEx(&cfg, q4_gemv_tma_kernel<2>, a) : cudaLaunchKernelEx(&cfg, q4_gemv_kernel<2>, a); break;
+  }
+  if (e != cudaSuccess) return fail(MOTIF_ERR_CUDA, "quantized_linear launch: %s", cudaGetErrorString(e));
+  return check_launch("quantized_linear");
+}
+
+bool al16(const void* p) { return p == nullptr || (reinterpret_cast<uintptr_t>(p) % 16) == 0; }
 
 }  // namespace
 }  // namespace motif
@@ -319,9 +943,9 @@ extern "C" {
 
 size_t motif_quantized_linear_workspace_bytes(int64_t m, int64_t n, int64_t k, int bits,
                                               int group_size) {
-  if (bits != 4 || group_size != 64 || k % 128 != 0) return 0;
-  GemvPlan p = plan_gemv(n, k);
-  return p.ksplit > 1 ? sizeof(float) * (size_t)p.ksplit * (size_t)n * (size_t)(m > 0 ? 1 : 0) : 0;
+  (void)m;
+  if (bits != 4 || group_size != 64 || k % 128 != 0 || n <= 0) return 0;
+  return ws_bytes_for(n, k);
 }
 
 int motif_quantized_linear(int dtype, int bits, int group_size, const void* x, int64_t m,
@@ -337,36 +961,20 @@ int motif_quantized_linear(int dtype, int bits, int group_size, const void* x, i
   if (m == 0) return MOTIF_OK;
   cudaStream_t st = as_stream(stream);
   if (fast_path_ok(dtype, bits, group_size, k, x, w, scales, biases)) {
-    GemvPlan p = plan_gemv(n, k);
-    float* part = nullptr;
-    if (p.ksplit > 1) {
-      const size_t need = sizeof(float) * (size_t)p.ksplit * (size_t)n;
-      if (!workspace || workspace_bytes < need) {
-        // No (or short) workspace: run unsplit.
-        p.ksplit = 1;
-        p.blocks_per_split = (int)ceil_div(k, kBlockK);
-        p.smem = (size_t)p.blocks_per_split * kBlockK * sizeof(__half) + (size_t)p.blocks_per_split * 8 * sizeof(float);
-      } else {
-        part = static_cast<float*>(workspace);
-      }
-    }
-    static bool configured = false;
-    if (!configured) {
-      cudaError_t e = cudaFuncSetAttribute(q4_gemv_mma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-      if (e != cudaSuccess) return fail(MOTIF_ERR_CUDA, "quantized_linear: smem attribute: %s", cudaGetErrorString(e));
-      configured = true;
-    }
-    MOTIF_REQUIRE(p.smem <= 200 * 1024, MOTIF_ERR_BAD_SHAPE, "quantized_linear: K=%lld too large", (long long)k);
-    dim3 grid((unsigned)ceil_div(n, kRowsPerCta), p.ksplit);
     for (int64_t i = 0; i < m; ++i) {
-      const __half* xi = static_cast<const __half*>(x) + i * k;
-      __half* yi = static_cast<__half*>(y) + i * n;
-      q4_gemv_mma_kernel<<<grid, kGemvThreads, p.smem, st>>>(
-          xi, k, w, static_cast<const __half*>(scales), static_cast<const __half*>(biases), n,
-          p.blocks_per_split, yi, part);
-      if (part) splitk_reduce_kernel<<<ceil_div(n, 256), 256, 0, st>>>(part, p.ksplit, n, yi);
+      LinArgs a{};
+      a.w = w;
+      a.sc = static_cast<const __half*>(scales);
+      a.bi = static_cast<const __half*>(biases);
+      a.N = n;
+      a.K = k;
+      a.y = static_cast<__half*>(y) + i * n;
+      a.mode = kModeX;
+      a.x = static_cast<const __half*>(x) + i * k;
+      int rc = launch_q4(a, workspace, workspace_bytes, st);
+      if (rc) return rc;
     }
-    return check_launch("quantized_linear (mma)");
+    return MOTIF_OK;
   }
   const int warps = 8;
   const int64_t blocks = ceil_div(m * n, warps);
@@ -376,6 +984,71 @@ int motif_quantized_linear(int dtype, int bits, int group_size, const void* x, i
         static_cast<const T*>(biases), n, bits, group_size, static_cast<T*>(y));
   });
   return check_launch("quantized_linear (general)");
+}
+
+size_t motif_linear_fused_workspace_bytes(int64_t n, int64_t k) {
+  return motif_quantized_linear_workspace_bytes(1, n, k, 4, 64);
+}
+
+int motif_linear_fused(const motif_linear_io* io, const uint32_t* w, const void* scales,
+                       const void* biases, int64_t n, int64_t k, void* y, void* workspace,
+                       size_t workspace_bytes, void* stream) {
+  MOTIF_REQUIRE(io && w && scales && biases && y, MOTIF_ERR_NULL, "linear_fused: null pointer");
+  MOTIF_REQUIRE(n > 0 && k > 0 && k % 128 == 0 && k <= 65536, MOTIF_ERR_BAD_SHAPE,
+                "linear_fused: n=%lld k=%lld (k must be a multiple of 128)", (long long)n, (long long)k);
+  MOTIF_REQUIRE(fast_path_ok(MOTIF_F16, 4, 64, k, nullptr, w, scales, biases), MOTIF_ERR_BAD_SHAPE,
+                "linear_fused: misaligned weights");
+  LinArgs a{};
+  a.w = w;
+  a.sc = static_cast<const __half*>(scales);
+  a.bi = static_cast<const __half*>(biases);
+  a.N = n;
+  a.K = k;
+  a.y = static_cast<__half*>(y);
+  a.mode = io->mode;
+  switch (io->mode) {
+    case kModeX:
+      MOTIF_REQUIRE(io->x && al16(io->x), MOTIF_ERR_NULL, "linear_fused: mode 0 needs a 16-byte aligned x");
+      a.x = static_cast<const __half*>(io->x);
+      break;
+    case kModeAddRms:
+      MOTIF_REQUIRE((io->h_in || (io->token && io->embed)) && io->norm_w, MOTIF_ERR_NULL,
+                    "linear_fused: mode 1 needs h_in (or token+embed) and norm_w");
+      MOTIF_REQUIRE(al16(io->h_in) && al16(io->embed) && al16(io->delta) && al16(io->h_out) && al16(io->norm_w),
+                    MOTIF_ERR_BAD_SHAPE, "linear_fused: mode 1 vectors must be 16-byte aligned");
+      a.h_in = static_cast<const __half*>(io->h_in);
+      a.token = io->token;
+      a.embed = static_cast<const __half*>(io->embed);
+      a.vocab = io->vocab;
+      a.delta = static_cast<const __half*>(io->delta);
+      a.h_out = static_cast<__half*>(io->h_out);
+      a.norm_w = static_cast<const __half*>(io->norm_w);
+      a.eps = io->eps;
+      break;
+    case kModePoly:
+      MOTIF_REQUIRE(io->gate && io->up && io->stats && io->stats_count > 0 && io->poly_w && io->poly_b &&
+                        io->poly_dim > 0,
+                    MOTIF_ERR_NULL, "linear_fused: mode 2 needs gate, up, stats, polynorm weight/bias");
+      MOTIF_REQUIRE(al16(io->gate) && al16(io->up), MOTIF_ERR_BAD_SHAPE, "linear_fused: gate/up must be 16-byte aligned");
+      a.gate = static_cast<const __half*>(io->gate);
+      a.up = static_cast<const __half*>(io->up);
+      a.stats = io->stats;
+      a.stats_count = (int)io->stats_count;
+      a.poly_w = static_cast<const __half*>(io->poly_w);
+      a.poly_b = static_cast<const __half*>(io->poly_b);
+      a.poly_eps = io->poly_eps;
+      a.poly_inv_dim = 1.0f / (float)io->poly_dim;
+      break;
+    default:
+      return fail(MOTIF_ERR_BAD_SHAPE, "linear_fused: mode %d not in {0,1,2}", io->mode);
+  }
+  if (io->stats_out) {
+    MOTIF_REQUIRE(io->stats_rows > 0 && io->stats_rows % kTileRows == 0 && io->stats_rows <= n, MOTIF_ERR_BAD_SHAPE,
+                  "linear_fused: stats_rows must be a positive multiple of 16 and <= n");
+    a.stats_out = io->stats_out;
+    a.stats_rows = io->stats_rows;
+  }
+  return launch_q4(a, workspace, workspace_bytes, as_stream(stream));
 }
 
 }  // extern "C"

@@ -226,6 +226,7 @@ __global__ void rope_qkv_append_kernel(const __half* __restrict__ qkv,
                                        const int32_t* __restrict__ pos_dev,
                                        __half* __restrict__ q_out) {
   __shared__ float vals[D];
+  pdl_trigger();
   const int head = blockIdx.x;
   const int c = threadIdx.x;
   const int half = D / 2;

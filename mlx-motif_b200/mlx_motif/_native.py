@@ -40,8 +40,34 @@ class motif_kv4_slots(C.Structure):  # noqa: N801 — mirrors the C struct name
     ]
 
 
+class motif_linear_io(C.Structure):  # noqa: N801 — mirrors the C struct name
+    _fields_ = [
+        ("mode", C.c_int32),
+        ("x", C.c_void_p),
+        ("h_in", C.c_void_p),
+        ("token", C.c_void_p),
+        ("embed", C.c_void_p),
+        ("vocab", C.c_int64),
+        ("delta", C.c_void_p),
+        ("h_out", C.c_void_p),
+        ("norm_w", C.c_void_p),
+        ("eps", C.c_float),
+        ("gate", C.c_void_p),
+        ("up", C.c_void_p),
+        ("stats", C.c_void_p),
+        ("stats_count", C.c_int64),
+        ("poly_w", C.c_void_p),
+        ("poly_b", C.c_void_p),
+        ("poly_eps", C.c_float),
+        ("poly_dim", C.c_int64),
+        ("stats_out", C.c_void_p),
+        ("stats_rows", C.c_int64),
+    ]
+
+
 _P, _I, _L, _F, _S = C.c_void_p, C.c_int, C.c_int64, C.c_float, C.c_size_t
 _KV = C.POINTER(motif_kv4_slots)
+_IO = C.POINTER(motif_linear_io)
 
 # name -> (restype, argtypes); every symbol of include/motif_b200.h.
 SIGNATURES = {
@@ -72,6 +98,8 @@ SIGNATURES = {
     "motif_rope": (_I, [_I, _P, _L, _L, _L, _L, _L, _P, _P, _P, _P]),
     "motif_quantized_linear_workspace_bytes": (_S, [_L, _L, _L, _I, _I]),
     "motif_quantized_linear": (_I, [_I, _I, _I, _P, _L, _L, _P, _P, _P, _L, _P, _P, _S, _P]),
+    "motif_linear_fused_workspace_bytes": (_S, [_L, _L]),
+    "motif_linear_fused": (_I, [_IO, _P, _P, _P, _L, _L, _P, _P, _S, _P]),
     "motif_rms_norm": (_I, [_I, _P, _P, _F, _L, _L, _P, _P]),
     "motif_add_rms_norm": (_I, [_I, _P, _P, _P, _F, _L, _L, _P, _P]),
     "motif_embed_rms_norm": (_I, [_I, _P, _P, _L, _L, _P, _F, _P, _P, _P]),

@@ -28,7 +28,8 @@ def quantized_matmul(x: torch.Tensor, w: torch.Tensor, scales: torch.Tensor, bia
     y = out if out is not None else torch.empty((*lead, N), dtype=x.dtype, device=x.device)
     ws_bytes = lib.motif_quantized_linear_workspace_bytes(max(M, 1), N, K, bits, group_size)
     if workspace is None or workspace.numel() < ws_bytes:
-        workspace = torch.empty(max(ws_bytes, 16), dtype=torch.uint8, device=x.device)
+        # zero-filled: the split-K tile counters must start at zero (the kernel re-zeroes them)
+        workspace = torch.zeros(max(ws_bytes, 16), dtype=torch.uint8, device=x.device)
     check(lib.motif_quantized_linear(dtype_code(x), bits, group_size, ptr(xc), M, K, ptr(w), ptr(scales),
                                      ptr(biases), N, ptr(y), ptr(workspace), ws_bytes, stream(x.device)),
           "quantized_linear")

@@ -27,7 +27,7 @@ from dataclasses import dataclass
 
 import torch
 
-from ._native import check, lib, ptr, stream
+from ._native import check, lib, motif_linear_io, ptr, stream
 from .cache import MotifGroupedKVCache, MotifGroupedQuantizedKVCache
 from .linear import QuantizedLinear
 from .quantization import quantize
@@ -329,8 +329,11 @@ class MotifDecoder:
 
         f16 = torch.float16
         H, d = self.H, self.d
-        self.h = torch.zeros(H, dtype=f16, device=dev)
-        self.x = torch.zeros(H, dtype=f16, device=dev)
+        # Residual stream ping-pong: the qkv prologue reads h_a and writes h_b, the gate|up
+        # prologue reads h_b and writes h_a (a kernel never overwrites what its CTAs read).
+        self.h_a = torch.zeros(H, dtype=f16, device=dev)
+        self.h_b = torch.zeros(H, dtype=f16, device=dev)
+        self.x = torch.zeros(H, dtype=f16, device=dev)  # scratch input vector (timing helpers)
         self.qkv = torch.zeros(self.layers[0]["qkv"].out_dim, dtype=f16, device=dev)
         self.q = torch.zeros(self.q_heads * d, dtype=f16, device=dev)
         self.attn = torch.zeros(self.q_origin * 2 * d, dtype=f16, device=dev)
@@ -338,6 +341,10 @@ class MotifDecoder:
         self.gu = torch.zeros(2 * self.inter, dtype=f16, device=dev)
         self.act = torch.zeros(self.inter, dtype=f16, device=dev)
         self.dn = torch.zeros(H, dtype=f16, device=dev)
+        # PolyNorm statistics of the gate rows: one (Σg², Σg⁴, Σg⁶) triplet per 16-row tile.
+        self.stats_tiles = self.inter // 16
+        self.stats = torch.zeros(self.stats_tiles * 3, dtype=torch.float32, device=dev)
+        self.stats_sum = torch.zeros(3, dtype=torch.float32, device=dev)
         self.logits = torch.zeros(self.V, dtype=f16, device=dev)
         self.token = torch.zeros(1, dtype=torch.int32, device=dev)
         # pos_len[0] = position of the token being decoded, pos_len[1] = kv_len after its append.
@@ -345,9 +352,11 @@ class MotifDecoder:
         self._one_one = torch.ones(2, dtype=torch.int32, device=dev)
         self.inv_freq = rope_inv_freq(d, a.rope_theta, dev)
         self.scale = d ** -0.5
-        lin_ws = max(lib.motif_quantized_linear_workspace_bytes(1, ql.out_dim, ql.in_dim, 4, 64)
+        lin_ws = max(lib.motif_linear_fused_workspace_bytes(ql.out_dim, ql.in_dim)
                      for L in self.layers for ql in (L["qkv"], L["o"], L["gate_up"], L["down"]))
-        lin_ws = max(lin_ws, lib.motif_quantized_linear_workspace_bytes(1, self.V, H, 4, 64))
+        lin_ws = max(lin_ws, lib.motif_linear_fused_workspace_bytes(self.V, H))
+        if self.inter % 16:
+            raise ValueError("intermediate size per rank must be a multiple of 16")
         self.lin_ws = torch.zeros(max(lin_ws, 16), dtype=torch.uint8, device=dev)
         self.attn_ws_bytes = lib.motif_gda_decode_attention_workspace_bytes(self.q_heads, d, 64)
         self.attn_ws = torch.zeros(self.attn_ws_bytes, dtype=torch.uint8, device=dev)
@@ -394,18 +403,60 @@ class MotifDecoder:
         if self.tp_group is not None:
             torch.distributed.all_reduce(t, group=self.tp_group)
 
-    def _launch_step(self, with_head: bool) -> None:
-        """Enqueue one decode step on the current stream (no host sync, no allocation)."""
-        st = stream(self.device)
-        H, d = self.H, self.d
+    def _io(self, mode: int, **kw) -> motif_linear_io:
+        io = motif_linear_io()
+        io.mode = mode
+        for k, v in kw.items():
+            setattr(io, k, v)
+        return io
+
+    def _build_plan(self) -> None:
+        """Fixed C-ABI argument structs of every fused linear of a step (pointers never move)."""
         eps = self.args.rms_norm_eps
+        I = self.inter
+        gp = self.gu.data_ptr()
+        tp = self.tp_group is not None
+        plan = []
+        for li, L in enumerate(self.layers):
+            if li == 0:
+                qkv_io = self._io(1, token=ptr(self.token), embed=ptr(self.embed), vocab=self.V,
+                                  h_out=ptr(self.h_b), norm_w=ptr(L["input_norm"]), eps=eps)
+            else:
+                qkv_io = self._io(1, h_in=ptr(self.h_a), delta=ptr(self.dn), h_out=ptr(self.h_b),
+                                  norm_w=ptr(L["input_norm"]), eps=eps)
+            o_io = self._io(0, x=ptr(self.attn))
+            gu_io = self._io(1, h_in=ptr(self.h_b), delta=ptr(self.o), h_out=ptr(self.h_a),
+                             norm_w=ptr(L["post_norm"]), eps=eps, stats_out=ptr(self.stats), stats_rows=I)
+            stats_src, stats_n = (self.stats_sum, 1) if tp else (self.stats, self.stats_tiles)
+            dn_io = self._io(2, gate=gp, up=gp + 2 * I, stats=ptr(stats_src), stats_count=stats_n,
+                             poly_w=ptr(L["polynorm_w"]), poly_b=ptr(L["polynorm_b"]), poly_eps=1e-6,
+                             poly_dim=self.args.intermediate_size)
+            plan.append((qkv_io, o_io, gu_io, dn_io))
+        head_io = self._io(1, h_in=ptr(self.h_a), delta=ptr(self.dn), norm_w=ptr(self.final_norm), eps=eps)
+        self._plan = (plan, head_io)
+
+    def _linear(self, io, ql: QuantizedLinear, out: torch.Tensor, st: int) -> None:
+        check(lib.motif_linear_fused(io, ptr(ql.weight), ptr(ql.scales), ptr(ql.biases), ql.out_dim, ql.in_dim,
+                                     ptr(out), ptr(self.lin_ws), self.lin_ws.numel(), st), "linear_fused")
+
+    def _launch_step(self, with_head: bool) -> None:
+        """Enqueue one decode step on the current stream (no host sync, no allocation).
+
+        Per layer: qkv GEMV (prologue: [embedding +] residual + input RMSNorm), RoPE + 4-slot
+        append, dual-V attention + GDA post (2 kernels), o_proj GEMV, gate|up GEMV (prologue:
+        residual + post-attention RMSNorm; epilogue: PolyNorm statistics), down GEMV (prologue:
+        PolyNorm·up). Head: lm_head GEMV (prologue: residual + final norm), argmax.
+        """
+        if getattr(self, "_plan", None) is None:
+            self._build_plan()
+        plan, head_io = self._plan
+        st = stream(self.device)
         pos_p = self.pos_len.data_ptr()
         kvl_p = pos_p + 4
-        L0 = self.layers[0]
-        check(lib.motif_embed_rms_norm(0, ptr(self.token), ptr(self.embed), self.V, H, ptr(L0["input_norm"]), eps,
-                                       ptr(self.h), ptr(self.x), st), "embed")
+        tp = self.tp_group is not None
         for li, L in enumerate(self.layers):
-            L["qkv"](self.x, out=self.qkv, workspace=self.lin_ws)
+            qkv_io, o_io, gu_io, dn_io = plan[li]
+            self._linear(qkv_io, L["qkv"], self.qkv, st)
             check(lib.motif_rope_qkv_append(ptr(self.qkv), ptr(self.inv_freq), self.q_heads, self._slots[li], pos_p,
                                             ptr(self.q), st), "rope_qkv_append")
             check(lib.motif_gda_decode_attention(ptr(self.q), self._slots[li], self.scale, self.q_groups, self.gr, 0,
@@ -413,55 +464,27 @@ class MotifDecoder:
                                                  L["lambda_full"].numel(), L["lambda_init"],
                                                  self.args.attn_rms_norm_eps, ptr(self.attn), ptr(self.attn_ws),
                                                  self.attn_ws_bytes, st), "gda_decode_attention")
-            L["o"](self.attn, out=self.o, workspace=self.lin_ws)
+            self._linear(o_io, L["o"], self.o, st)
             self._allreduce(self.o)
-            check(lib.motif_add_rms_norm(0, ptr(self.h), ptr(self.o), ptr(L["post_norm"]), eps, 1, H, ptr(self.x), st),
-                  "add_rms_norm")
-            L["gate_up"](self.x, out=self.gu, workspace=self.lin_ws)
-            self._polynorm_mul(L, st)
-            L["down"](self.act, out=self.dn, workspace=self.lin_ws)
+            self._linear(gu_io, L["gate_up"], self.gu, st)
+            if tp:
+                # Full-row PolyNorm statistics across ranks (12 bytes over NCCL).
+                torch.sum(self.stats.view(-1, 3), dim=0, out=self.stats_sum)
+                self._allreduce(self.stats_sum)
+            self._linear(dn_io, L["down"], self.dn, st)
             self._allreduce(self.dn)
-            nxt = self.layers[li + 1]["input_norm"] if li + 1 < len(self.layers) else self.final_norm
-            check(lib.motif_add_rms_norm(0, ptr(self.h), ptr(self.dn), ptr(nxt), eps, 1, H, ptr(self.x), st),
-                  "add_rms_norm")
         if with_head:
-            self.lm_head(self.x, out=self.logits, workspace=self.lin_ws)
+            self._linear(head_io, self.lm_head, self.logits, st)
             check(lib.motif_argmax(0, ptr(self.logits), self.V, ptr(self.token), ptr(self.argmax_ws),
                                    self.argmax_ws_bytes, st), "argmax")
         self.pos_len.add_(self._one_one)
-
-    def _polynorm_mul(self, L, st) -> None:
-        if self.tp_group is not None:
-            self._polynorm_mul_tp(L)
-            return
-        I = self.inter
-        gp = self.gu.data_ptr()
-        check(lib.motif_polynorm_mul(0, gp, gp + 2 * I, 2 * I, ptr(L["polynorm_w"]), ptr(L["polynorm_b"]), 1e-6, 1, I,
-                                     ptr(self.act), st), "polynorm_mul")
-
-    def _polynorm_mul_tp(self, L) -> None:
-        # Full-row PolyNorm statistics over the sharded intermediate axis: all-reduce
-        # (Σx², Σx⁴, Σx⁶) then apply locally (torch glue; NCCL carries 12 bytes).
-        I = self.inter
-        g = self.gu[:I].float()
-        u = self.gu[I:].float()
-        g2 = g * g
-        stats = torch.stack([g2.sum(), (g2 * g2).sum(), (g2 * g2 * g2).sum()])
-        self._allreduce(stats)
-        n = float(self.args.intermediate_size)
-        eps = 1e-6
-        r2, r4, r6 = (torch.rsqrt(stats / n + eps)).unbind(0)
-        w = L["polynorm_w"].float()
-        b = L["polynorm_b"].float()
-        act = w[0] * (g2 * g * r6) + w[1] * (g2 * r4) + w[2] * (g * r2) + b[0]
-        self.act.copy_((act.half().float() * u).half())
 
     # ------------------------------------------------------------------ #
     def _graph(self, with_head: bool) -> torch.cuda.CUDAGraph:
         g = self._graphs.get(with_head)
         if g is None:
             # Warm up once outside capture (function attributes, NCCL comm init), then restore state.
-            saved = (self.pos_len.clone(), self.token.clone(), self.h.clone())
+            saved = (self.pos_len.clone(), self.token.clone())
             self._launch_step(with_head)
             self.pos_len.copy_(saved[0])
             self.token.copy_(saved[1])

@@ -79,5 +79,8 @@ def test_workspace_queries():
 
     assert N.lib.motif_sdpa_dual_v_workspace_bytes(1, 32, 128, 10) == 4 * 32 * 10 * 258
     assert N.lib.motif_quantized_linear_workspace_bytes(1, 4096, 14336, 4, 64) > 0
-    assert N.lib.motif_quantized_linear_workspace_bytes(1, 219520, 4096, 4, 64) == 0
+    # stream-K: tiles split across warps need partials + counters, a single K block never does
+    assert N.lib.motif_quantized_linear_workspace_bytes(1, 219520, 4096, 4, 64) > 0
+    assert N.lib.motif_quantized_linear_workspace_bytes(1, 4096, 512, 4, 64) == 0
+    assert N.lib.motif_linear_fused_workspace_bytes(8192, 4096) > 0
     assert N.lib.motif_argmax_workspace_bytes(219520) >= 8

@@ -362,3 +362,71 @@ def test_decoder_host_api_and_generate(cuda):
         t = b.decode_host(t)
         seq.append(t)
     assert seq == toks
+
+
+# ---------------------------------------------------------------- fused decode linear
+def _fused(N_, io, ql, out, ws):
+    N_.check(N_.lib.motif_linear_fused(io, ql[0].data_ptr(), ql[1].data_ptr(), ql[2].data_ptr(), ql[0].shape[0],
+                                       ql[0].shape[1] * 8, out.data_ptr(), ws.data_ptr(), ws.numel(), N_.stream()))
+
+
+def test_linear_fused_modes_match_oracle(cuda):
+    """mode 1 (embedding/residual + RMSNorm prologue, h_out), stats epilogue, mode 2
+    (PolyNorm·up prologue from tile statistics), repeated calls bit-identical."""
+    from mlx_motif import _native as N
+    from mlx_motif.quantization import quantize
+
+    rng = np.random.default_rng(31)
+    H, I, V = 4096, 14336, 64
+    h = rounded(rng.standard_normal(H), "float16")
+    dl = rounded(rng.standard_normal(H) * 0.5, "float16")
+    nw = rounded(1 + 0.02 * rng.standard_normal(H), "float16")
+    emb = rounded(rng.standard_normal((V, H)), "float16")
+    wgu = rounded(rng.standard_normal((2 * I, H)) * 0.02, "float16")
+    wd = rounded(rng.standard_normal((H, I)) * 0.02, "float16")
+    gu_q = quantize(up(wgu), 64, 4)
+    d_q = quantize(up(wd), 64, 4)
+    ws = torch.zeros(max(N.lib.motif_linear_fused_workspace_bytes(2 * I, H),
+                         N.lib.motif_linear_fused_workspace_bytes(H, I)), dtype=torch.uint8, device=cuda)
+    th, tdl, tnw, temb = up(h), up(dl), up(nw), up(emb)
+    h_out = torch.empty(H, dtype=torch.float16, device=cuda)
+    gu = torch.empty(2 * I, dtype=torch.float16, device=cuda)
+    stats = torch.zeros(I // 16 * 3, dtype=torch.float32, device=cuda)
+    io = N.motif_linear_io()
+    io.mode, io.h_in, io.delta, io.h_out, io.norm_w, io.eps = 1, th.data_ptr(), tdl.data_ptr(), h_out.data_ptr(), \
+        tnw.data_ptr(), 1e-6
+    io.stats_out, io.stats_rows = stats.data_ptr(), I
+    _fused(N, io, gu_q, gu, ws)
+    hs = (h.astype(np.float32) + dl.astype(np.float32)).astype(np.float16)
+    np.testing.assert_array_equal(down(h_out), hs.astype(np.float32))
+    xn = O.rms_norm(hs, nw, 1e-6).astype(np.float16)
+    trip_np = lambda t: (t[0].cpu().numpy().view(np.uint32), down(t[1]), down(t[2]))  # noqa: E731
+    ref_gu = O.quantized_matmul(xn, *trip_np(gu_q), 64, 4)
+    assert_close(down(gu), ref_gu, "float16", what="gate|up (mode 1)")
+    g16 = down(gu)[:I].astype(np.float64)
+    st = stats.view(-1, 3).sum(0).cpu().numpy()
+    np.testing.assert_allclose(st, [np.sum(g16 ** 2), np.sum(g16 ** 4), np.sum(g16 ** 6)], rtol=1e-4)
+    # mode 2: PolyNorm(gate)·up -> down
+    pw = up([1 / 3, 1 / 3, 1 / 3])
+    pb = up([0.0])
+    dn = torch.empty(H, dtype=torch.float16, device=cuda)
+    io2 = N.motif_linear_io()
+    io2.mode, io2.gate, io2.up = 2, gu.data_ptr(), gu.data_ptr() + 2 * I
+    io2.stats, io2.stats_count, io2.poly_w, io2.poly_b, io2.poly_eps, io2.poly_dim = stats.data_ptr(), I // 16, \
+        pw.data_ptr(), pb.data_ptr(), 1e-6, I
+    _fused(N, io2, d_q, dn, ws)
+    act = O.polynorm_mul_reference(down(gu)[:I], down(gu)[I:], [1 / 3] * 3, [0.0], 1e-6)
+    ref_dn = O.quantized_matmul(act, *trip_np(d_q), 64, 4)
+    assert_close(down(dn), ref_dn, "float16", what="down (mode 2)")
+    again = torch.empty_like(dn)
+    _fused(N, io2, d_q, again, ws)
+    assert torch.equal(again, dn), "split-K reduction must be deterministic and its counters reset"
+    # embedding gather prologue
+    tok = torch.tensor([17], dtype=torch.int32, device=cuda)
+    io3 = N.motif_linear_io()
+    io3.mode, io3.token, io3.embed, io3.vocab, io3.norm_w, io3.eps, io3.h_out = 1, tok.data_ptr(), temb.data_ptr(), \
+        V, tnw.data_ptr(), 1e-6, h_out.data_ptr()
+    _fused(N, io3, gu_q, gu, ws)
+    np.testing.assert_array_equal(down(h_out), emb[17])
+    ref3 = O.quantized_matmul(O.rms_norm(emb[17], nw, 1e-6).astype(np.float16), *trip_np(gu_q), 64, 4)
+    assert_close(down(gu), ref3, "float16", what="embedding prologue")
