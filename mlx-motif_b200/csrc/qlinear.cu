@@ -82,6 +82,11 @@ constexpr int kWarps = 8;
 constexpr int kThreads = kWarps * 32;
 constexpr int kBlockK = 512;
 constexpr int kTileRows = 16;
+// Staged x of the TMA kernel: each 64-value group takes 144 B (16 B of padding), so the
+// quad-diagonal lanes, which read four groups at the same offset, land on distinct banks.
+constexpr int kXGroupBytes = 144;
+// Zeros read by the lanes that feed no B column: covers groups c and c+4 (4·144 + 128 B).
+constexpr int kZeroBytes = 768;
 // Workspace layout: [tile counters: kCounterTiles int32][split-K partials]. The
 // counter region has a fixed size so that GEMVs of different shapes can share
 // one workspace: partials of one shape never land on another shape's counters.
@@ -308,8 +313,11 @@ struct StageWords {
   static constexpr int value = MODE == 1 ? 4 : 8;
 };
 
-template <int MODE, bool V2>
-__device__ void stage_x(const LinArgs& a, __half* xp_s, float* xsum_s, float* corr_s, float* red) {
+// `after_issue` runs on every thread once the input loads are in flight (the TMA
+// kernel issues the rest of its weight prefetch there, behind the staging loads).
+template <int MODE, bool V2, typename AfterIssue>
+__device__ void stage_x(const LinArgs& a, __half* xp_s, float* xsum_s, float* corr_s, float* red,
+                        AfterIssue&& after_issue) {
   constexpr int kMaxStageWords = StageWords<MODE>::value;
   const int64_t K = a.K;
   const int words = (int)(K / 8);
@@ -347,6 +355,7 @@ __device__ void stage_x(const LinArgs& a, __half* xp_s, float* xsum_s, float* co
       stats_acc[2] += a.stats[i * 3 + 2];
     }
   }
+  after_issue();
   // ---- row statistics ----
   float inv = 1.f, r2 = 0.f, r4 = 0.f, r6 = 0.f, pw0 = 0.f, pw1 = 0.f, pw2 = 0.f, pb = 0.f;
   if (MODE == kModeAddRms) {
@@ -423,7 +432,7 @@ __device__ void stage_x(const LinArgs& a, __half* xp_s, float* xsum_s, float* co
       oe[5] = h[6];
       oe[6] = h[3];
       oe[7] = h[7];
-      *reinterpret_cast<uint4*>(xp_s + (int64_t)wi * 8) = o;
+      *reinterpret_cast<uint4*>(xp_s + (int64_t)wi * 8 + (V2 ? (int64_t)(wi >> 3) * (kXGroupBytes / 2 - 64) : 0)) = o;
     } else {
 #pragma unroll
       for (int j = 0; j < 8; ++j) h[j] = __float2half_rn(0.f);
@@ -476,7 +485,7 @@ __global__ void __launch_bounds__(kThreads, 2) q4_gemv_kernel(LinArgs a) {
   if (u0 < u1) load_unit(A, a, tile, blk, r, c);
   grid_dep_wait();
   grid_dep_launch();
-  stage_x<MODE, false>(a, xp_s, xsum_s, nullptr, red);
+  stage_x<MODE, false>(a, xp_s, xsum_s, nullptr, red, [] {});
 
   float acc_r = 0.f, acc_r8 = 0.f;
   for (int u = u0; u < u1; u += 2) {
@@ -594,67 +603,69 @@ __device__ __forceinline__ void dequant_word_offset(uint32_t w, uint32_t (&p)[4]
   p[3] = lop3_and_or(w8, HI, EX);
 }
 
-// Address of lane c's 8 bytes of group gp (0..3) in row `row` of a 128B-swizzled 16 × 128 box.
-__device__ __forceinline__ const unsigned char* swz(const unsigned char* box, int row, int gp, int c) {
-  const int chunk = (2 * gp + (c >> 1)) ^ (row & 7);
-  return box + row * 128 + chunk * 16 + (c & 1) * 8;
-}
-
-__device__ __forceinline__ void compute_unit_tma(const unsigned char* slot, int blk,
-                                                 const __half* __restrict__ xp_s, const float* __restrict__ xsum_s,
-                                                 const float* __restrict__ corr_s, int r, int c, float& acc_r,
-                                                 float& acc_r8) {
-  const __half* xg = xp_s + (int64_t)blk * kBlockK + c * 16;
-  const int g0 = blk * 8;
-  // Operands of group g: the lane's 8 bytes of rows r and r+8, and its 16 x values.
-  uint2 wr = lds64(swz(slot, r, 0, c)), wr8 = lds64(swz(slot, r + 8, 0, c));
-  uint4 x0 = lds128(xg), x1 = lds128(xg + 8);
-  float a_r = 0.f, a_r8 = 0.f;
+// One unit (16 rows × 8 groups of 64) on the tensor pipe, one B column per group.
+//
+// Lane (r, c) supplies the A operand for rows r and r+8 of group c (MMAs into Ca)
+// and group c+4 (MMAs into Cb): the 32 code bytes of each, chunks 2c and 2c+1 of
+// the 128B-swizzled box. B column n is fed by the lanes with r == n; only the
+// quad-diagonal lane (r == c) holds x (the group's staged values, `xl`), every
+// other lane reads zeros, so column n of Ca/Cb accumulates exactly the dot of
+// group n / n+4 and the accumulators stay live for the whole unit. Lanes c < 2
+// then hold groups 2c, 2c+1 (Ca) and 2c+4, 2c+5 (Cb) of rows r and r+8 and apply
+// the affine epilogue s·(C − corr) + b·Σx once per unit.
+__device__ __forceinline__ void compute_unit_tma(const unsigned char* slot, const unsigned char* xl, uint32_t o0,
+                                                 uint32_t o1, int r, int c, int blk,
+                                                 const float* __restrict__ xsum_s, const float* __restrict__ corr_s,
+                                                 float& acc_r, float& acc_r8) {
+  float Ca[4] = {0.f, 0.f, 0.f, 0.f}, Cb[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-  for (int g = 0; g < 8; ++g) {
-    // Software pipeline: fetch group g+1's operands before group g's math.
-    uint2 nwr = wr, nwr8 = wr8;
-    uint4 nx0 = x0, nx1 = x1;
-    if (g + 1 < 8) {
-      const unsigned char* box = slot + ((g + 1) >> 2) * 2048;
-      nwr = lds64(swz(box, r, (g + 1) & 3, c));
-      nwr8 = lds64(swz(box, r + 8, (g + 1) & 3, c));
-      nx0 = lds128(xg + (g + 1) * 64);
-      nx1 = lds128(xg + (g + 1) * 64 + 8);
+  for (int h = 0; h < 2; ++h) {  // words 4h .. 4h+3 of each group
+    const uint32_t o = h ? o1 : o0;
+    const uint4 wa = lds128(slot + o), wa8 = lds128(slot + 1024 + o);
+    const uint4 wb = lds128(slot + 2048 + o), wb8 = lds128(slot + 3072 + o);
+    uint4 xa[4], xb[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      xa[i] = lds128(xl + h * 64 + i * 16);
+      xb[i] = lds128(xl + 4 * kXGroupBytes + h * 64 + i * 16);
     }
-    uint32_t P[4], P8[4], Q[4], Q8[4];
-    dequant_word_offset(wr.x, P);
-    dequant_word_offset(wr8.x, P8);
-    dequant_word_offset(wr.y, Q);
-    dequant_word_offset(wr8.y, Q8);
-    // Two independent accumulation chains per group (words 2c and 2c+1).
-    float C0[4] = {0.f, 0.f, 0.f, 0.f}, C1[4] = {0.f, 0.f, 0.f, 0.f};
-    mma16816(C0, P[0], P8[0], P[1], P8[1], x0.x, x0.y);
-    mma16816(C1, Q[0], Q8[0], Q[1], Q8[1], x1.x, x1.y);
-    mma16816(C0, P[2], P8[2], P[3], P8[3], x0.z, x0.w);
-    mma16816(C1, Q[2], Q8[2], Q[3], Q8[3], x1.z, x1.w);
-    // Every column of C holds the group's dot, so the four lanes of a row split the
-    // affine epilogue: lane c takes groups c and c+4 (the tile epilogue sums over c).
-    if ((g & 3) == c) {
-      const float corr = corr_s[g0 + g], xs = xsum_s[g0 + g];
-      const __half2 s2 = *reinterpret_cast<const __half2*>(slot + 4096 + r * 16 + (g & ~1) * 2);
-      const __half2 s28 = *reinterpret_cast<const __half2*>(slot + 4096 + (r + 8) * 16 + (g & ~1) * 2);
-      const __half2 b2 = *reinterpret_cast<const __half2*>(slot + 4352 + r * 16 + (g & ~1) * 2);
-      const __half2 b28 = *reinterpret_cast<const __half2*>(slot + 4352 + (r + 8) * 16 + (g & ~1) * 2);
-      const float sr = (g & 1) ? __high2float(s2) : __low2float(s2);
-      const float sr8 = (g & 1) ? __high2float(s28) : __low2float(s28);
-      const float br = (g & 1) ? __high2float(b2) : __low2float(b2);
-      const float br8 = (g & 1) ? __high2float(b28) : __low2float(b28);
-      a_r += sr * ((C0[0] + C1[0]) - corr) + br * xs;
-      a_r8 += sr8 * ((C0[2] + C1[2]) - corr) + br8 * xs;
+    const uint32_t* pa = &wa.x;
+    const uint32_t* pa8 = &wa8.x;
+    const uint32_t* pb = &wb.x;
+    const uint32_t* pb8 = &wb8.x;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      uint32_t P[4], P8[4], Q[4], Q8[4];
+      dequant_word_offset(pa[i], P);
+      dequant_word_offset(pa8[i], P8);
+      dequant_word_offset(pb[i], Q);
+      dequant_word_offset(pb8[i], Q8);
+      mma16816(Ca, P[0], P8[0], P[1], P8[1], xa[i].x, xa[i].y);
+      mma16816(Cb, Q[0], Q8[0], Q[1], Q8[1], xb[i].x, xb[i].y);
+      mma16816(Ca, P[2], P8[2], P[3], P8[3], xa[i].z, xa[i].w);
+      mma16816(Cb, Q[2], Q8[2], Q[3], Q8[3], xb[i].z, xb[i].w);
     }
-    wr = nwr;
-    wr8 = nwr8;
-    x0 = nx0;
-    x1 = nx1;
   }
-  acc_r += a_r;
-  acc_r8 += a_r8;
+  if (c < 2) {
+    const int g = blk * 8 + 2 * c;
+    const float2 cra = *reinterpret_cast<const float2*>(corr_s + g);
+    const float2 crb = *reinterpret_cast<const float2*>(corr_s + g + 4);
+    const float2 xsa = *reinterpret_cast<const float2*>(xsum_s + g);
+    const float2 xsb = *reinterpret_cast<const float2*>(xsum_s + g + 4);
+    const unsigned char* sp = slot + 4096 + r * 16 + 4 * c;  // scales of row r, groups 2c and 2c+1
+    const float2 sa = __half22float2(*reinterpret_cast<const __half2*>(sp));
+    const float2 sb = __half22float2(*reinterpret_cast<const __half2*>(sp + 8));
+    const float2 sa8 = __half22float2(*reinterpret_cast<const __half2*>(sp + 128));
+    const float2 sb8 = __half22float2(*reinterpret_cast<const __half2*>(sp + 136));
+    const float2 ba = __half22float2(*reinterpret_cast<const __half2*>(sp + 256));
+    const float2 bb = __half22float2(*reinterpret_cast<const __half2*>(sp + 264));
+    const float2 ba8 = __half22float2(*reinterpret_cast<const __half2*>(sp + 384));
+    const float2 bb8 = __half22float2(*reinterpret_cast<const __half2*>(sp + 392));
+    acc_r += sa.x * (Ca[0] - cra.x) + ba.x * xsa.x + sa.y * (Ca[1] - cra.y) + ba.y * xsa.y +
+             sb.x * (Cb[0] - crb.x) + bb.x * xsb.x + sb.y * (Cb[1] - crb.y) + bb.y * xsb.y;
+    acc_r8 += sa8.x * (Ca[2] - cra.x) + ba8.x * xsa.x + sa8.y * (Ca[3] - cra.y) + ba8.y * xsa.y +
+              sb8.x * (Cb[2] - crb.x) + bb8.x * xsb.x + sb8.y * (Cb[3] - crb.y) + bb8.y * xsb.y;
+  }
 }
 
 template <int MODE>
@@ -665,7 +676,10 @@ __global__ void __launch_bounds__(kTmaThreads, kTmaMinBlocks) q4_gemv_tma_kernel
   unsigned char* ring = smem_tma;
   uint64_t* bars = reinterpret_cast<uint64_t*>(ring + (size_t)kTmaWarps * kStages * kSlotBytes);
   __half* xp_s = reinterpret_cast<__half*>(bars + kTmaWarps * kStages);
-  float* xsum_s = reinterpret_cast<float*>(xp_s + a.K);
+  // zero_s is offset 64 B (mod 128) from the x rows so its broadcast read never shares a
+  // bank with the diagonal lanes' x reads.
+  unsigned char* zero_s = reinterpret_cast<unsigned char*>(xp_s) + (size_t)(a.K / 64) * kXGroupBytes + 64;
+  float* xsum_s = reinterpret_cast<float*>(zero_s + kZeroBytes);
   float* corr_s = xsum_s + a.K / 64;
   float* red = corr_s + a.K / 64;
 
@@ -679,23 +693,40 @@ __global__ void __launch_bounds__(kTmaThreads, kTmaMinBlocks) q4_gemv_tma_kernel
   unsigned char* my_ring = ring + (size_t)warp * kStages * kSlotBytes;
   uint64_t* my_bars = bars + warp * kStages;
 
+  if (threadIdx.x == 0) {
+    asm volatile("prefetch.tensormap [%0];\n" ::"l"(reinterpret_cast<uint64_t>(&a.tm_w)) : "memory");
+    asm volatile("prefetch.tensormap [%0];\n" ::"l"(reinterpret_cast<uint64_t>(&a.tm_s)) : "memory");
+    asm volatile("prefetch.tensormap [%0];\n" ::"l"(reinterpret_cast<uint64_t>(&a.tm_b)) : "memory");
+  }
   if (lane == 0) {
     for (int i = 0; i < kStages; ++i) mbar_init(smem_u32(&my_bars[i]), 1);
     asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
   }
   __syncwarp();
-  // (tile, blk) of the next unit to fetch; weights do not depend on the previous
-  // kernel, so the ring is filled before waiting for it.
+  // (tile, blk) of the next unit to fetch. Weights do not depend on the previous
+  // kernel: the first slot is filled before waiting for it, the others right after
+  // the x inputs are requested, so the staging loads queue behind one unit per warp
+  // instead of the whole ring.
   int it = u0 / nblk, ib = u0 - (u0 / nblk) * nblk;
-  if (lane == 0) {
-    for (int i = 0; i < kStages && u0 + i < u1; ++i) {
-      issue_unit(a, it, ib, smem_u32(my_ring + i * kSlotBytes), smem_u32(&my_bars[i]));
-      if (++ib == nblk) { ib = 0; ++it; }
-    }
+  if (lane == 0 && u0 < u1) {
+    issue_unit(a, it, ib, smem_u32(my_ring), smem_u32(&my_bars[0]));
+    if (++ib == nblk) { ib = 0; ++it; }
   }
+  for (int i = threadIdx.x; i < kZeroBytes / 16; i += blockDim.x) reinterpret_cast<uint4*>(zero_s)[i] = make_uint4(0, 0, 0, 0);
   grid_dep_wait();
   grid_dep_launch();
-  stage_x<MODE, true>(a, xp_s, xsum_s, corr_s, red);
+  stage_x<MODE, true>(a, xp_s, xsum_s, corr_s, red, [&] {
+    if (lane == 0) {
+      for (int i = 1; i < kStages && u0 + i < u1; ++i) {
+        issue_unit(a, it, ib, smem_u32(my_ring + i * kSlotBytes), smem_u32(&my_bars[i]));
+        if (++ib == nblk) { ib = 0; ++it; }
+      }
+    }
+  });
+  // Per-lane operand addresses (see compute_unit_tma).
+  const uint32_t o0 = r * 128 + (((2 * c) ^ r) * 16), o1 = r * 128 + (((2 * c + 1) ^ r) * 16);
+  const bool diag = r == c;
+  const unsigned char* xrow = reinterpret_cast<const unsigned char*>(xp_s) + c * kXGroupBytes;
 
   float acc_r = 0.f, acc_r8 = 0.f;
   bool ok = true;
@@ -712,7 +743,8 @@ __global__ void __launch_bounds__(kTmaThreads, kTmaMinBlocks) q4_gemv_tma_kernel
       }
       break;
     }
-    compute_unit_tma(my_ring + slot * kSlotBytes, blk, xp_s, xsum_s, corr_s, r, c, acc_r, acc_r8);
+    const unsigned char* xl = diag ? xrow + blk * 8 * kXGroupBytes : zero_s;
+    compute_unit_tma(my_ring + slot * kSlotBytes, xl, o0, o1, r, c, blk, xsum_s, corr_s, acc_r, acc_r8);
     __syncwarp();
     if (lane == 0 && u + kStages < u1) {
       issue_unit(a, it, ib, smem_u32(my_ring + slot * kSlotBytes), smem_u32(&my_bars[slot]));
@@ -847,8 +879,8 @@ bool encode_rows(CUtensorMap* m, const void* base, uint64_t inner_bytes, uint64_
 }
 
 size_t tma_smem_bytes(int64_t K) {
-  return 1024 + (size_t)kTmaWarps * kStages * kSlotBytes + (size_t)kTmaWarps * kStages * 8 + (size_t)K * 2 +
-         2 * (size_t)(K / 64) * 4 + 32 * 3 * 4;
+  return (size_t)kTmaWarps * kStages * kSlotBytes + (size_t)kTmaWarps * kStages * 8 +
+         (size_t)(K / 64) * kXGroupBytes + 64 + kZeroBytes + 2 * (size_t)(K / 64) * 4 + 32 * 3 * 4;
 }
 
 // The TMA kernel needs K % 512 == 0 and 16-byte aligned rows of codes (K/2 bytes) and scales (K/32 bytes).
