@@ -302,19 +302,29 @@ def time_gemvs(model) -> dict:
 
 
 def time_attention(model) -> dict:
-    """CUDA-event time (graph replay) of the 48 layers' fused attention at the current kv_len."""
+    """CUDA-event time (graph replay) of the 48 layers' attention step at the current kv_len: the
+    one-launch RoPE + cache append + dual-V attention + GDA merge (motif_gda_decode_step), or the
+    attention alone when the model runs the two-call path."""
     from mlx_motif._native import check, lib, ptr, stream
 
     kv_len = int(model.pos_len[1].item())
-    kvl_p = model.pos_len.data_ptr() + 4
+    pos_p = model.pos_len.data_ptr()
+    kvl_p = pos_p + 4
 
     def run():
         st = stream(model.device)
         for li, L in enumerate(model.layers):
-            check(lib.motif_gda_decode_attention(ptr(model.q), model._slots[li], model.scale, model.q_groups, model.gr,
-                                                 0, kvl_p, ptr(L["subln"]), ptr(L["lambda_full"]),
-                                                 L["lambda_full"].numel(), L["lambda_init"], 1e-5, ptr(model.attn),
-                                                 ptr(model.attn_ws), model.attn_ws_bytes, st))
+            if model.fused_attn:
+                # writes row pos from the last qkv: the slot the next decode step overwrites
+                check(lib.motif_gda_decode_step(ptr(model.qkv), ptr(model.inv_freq), model._slots[li], pos_p,
+                                                model.scale, model.q_groups, model.gr, ptr(L["subln"]),
+                                                ptr(L["lambda_full"]), L["lambda_full"].numel(), L["lambda_init"],
+                                                1e-5, ptr(model.attn), ptr(model.attn_ws), model.attn_ws_bytes, st))
+            else:
+                check(lib.motif_gda_decode_attention(ptr(model.q), model._slots[li], model.scale, model.q_groups,
+                                                     model.gr, 0, kvl_p, ptr(L["subln"]), ptr(L["lambda_full"]),
+                                                     L["lambda_full"].numel(), L["lambda_init"], 1e-5,
+                                                     ptr(model.attn), ptr(model.attn_ws), model.attn_ws_bytes, st))
 
     best = _graph_time(run)
     kv_bytes = model.kv_bytes_per_token(kv_len)

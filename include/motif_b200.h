@@ -167,6 +167,23 @@ MOTIF_API int motif_gda_decode_attention(const void* q, const motif_kv4_slots* c
                                float eps, void* out, void* workspace, size_t workspace_bytes,
                                void* stream);
 
+/* The decoder's whole attention step for one layer in ONE launch:
+ * motif_rope_qkv_append followed by motif_gda_decode_attention (reference
+ * model.py:580-657 and 716-768: RoPE of q/k, the 4-slot cache write, both
+ * sdpa_dual_v calls and gda_post_split). qkv: the fused projection row
+ * [q heads | k1,k2 pairs | v1,v2 pairs] (fp16); pos_len: device int32
+ * [pos, kv_len] — the new k/v row is written at pos and the attention covers
+ * positions [0, kv_len). Results equal the two-call sequence bit for bit.
+ * workspace: motif_gda_decode_step_workspace_bytes(q_heads, 128, splits)
+ * bytes (splits <= 64), zero-filled before first use; its first 256 bytes
+ * hold per-group counters that the kernel leaves zeroed. */
+MOTIF_API size_t motif_gda_decode_step_workspace_bytes(int64_t q_heads, int64_t head_dim, int64_t max_splits);
+MOTIF_API int motif_gda_decode_step(const void* qkv, const float* inv_freq, const motif_kv4_slots* cache,
+                                    const int32_t* pos_len, float scale, int64_t q_groups, int64_t gr,
+                                    const void* subln_w, const float* lambda_full, int64_t lambda_len,
+                                    float lambda_init, float eps, void* out, void* workspace,
+                                    size_t workspace_bytes, void* stream);
+
 /* ---- affine quantization ---------------------------------------------------
  * MLX-layout affine group quantization along the last axis (bits 4 or 8):
  * data (rows, dim*bits/32) uint32 little-endian, scales/biases

@@ -19,6 +19,7 @@
 #include <cmath>
 
 #include "common.cuh"
+#include "kvquant.cuh"
 
 namespace motif {
 namespace {
@@ -248,10 +249,11 @@ constexpr int kMaxSplits = 64;
 // computed by one warp (two splits per lane) into shared memory.
 __device__ __forceinline__ void split_weights(const float* __restrict__ base, int n_active, int stride,
                                               float* f_out, float* L_out, int lane) {
-  const float m0 = lane < n_active ? base[lane * stride] : -INFINITY;
-  const float m1 = lane + 32 < n_active ? base[(lane + 32) * stride] : -INFINITY;
-  const float l0 = lane < n_active ? base[lane * stride + 1] : 0.f;
-  const float l1 = lane + 32 < n_active ? base[(lane + 32) * stride + 1] : 0.f;
+  // L2 loads: the partials may have been written by other CTAs of the same launch.
+  const float m0 = lane < n_active ? __ldcg(base + lane * stride) : -INFINITY;
+  const float m1 = lane + 32 < n_active ? __ldcg(base + (lane + 32) * stride) : -INFINITY;
+  const float l0 = lane < n_active ? __ldcg(base + lane * stride + 1) : 0.f;
+  const float l1 = lane + 32 < n_active ? __ldcg(base + (lane + 32) * stride + 1) : 0.f;
   const float M = warp_max(fmaxf(m0, m1));
   const float f0 = (M != -INFINITY && m0 != -INFINITY) ? exp2f(m0 - M) : 0.f;
   const float f1 = (M != -INFINITY && m1 != -INFINITY) ? exp2f(m1 - M) : 0.f;
@@ -267,12 +269,12 @@ __device__ __forceinline__ float merge_channel(const float* __restrict__ base, c
   float o0 = 0.f, o1 = 0.f, o2 = 0.f, o3 = 0.f;
   int s = 0;
   for (; s + 4 <= n_active; s += 4) {
-    o0 += f[s] * base[s * stride + 2 + ch];
-    o1 += f[s + 1] * base[(s + 1) * stride + 2 + ch];
-    o2 += f[s + 2] * base[(s + 2) * stride + 2 + ch];
-    o3 += f[s + 3] * base[(s + 3) * stride + 2 + ch];
+    o0 += f[s] * __ldcg(base + s * stride + 2 + ch);
+    o1 += f[s + 1] * __ldcg(base + (s + 1) * stride + 2 + ch);
+    o2 += f[s + 2] * __ldcg(base + (s + 2) * stride + 2 + ch);
+    o3 += f[s + 3] * __ldcg(base + (s + 3) * stride + 2 + ch);
   }
-  for (; s < n_active; ++s) o0 += f[s] * base[s * stride + 2 + ch];
+  for (; s < n_active; ++s) o0 += f[s] * __ldcg(base + s * stride + 2 + ch);
   return (o0 + o1) + (o2 + o3);
 }
 
@@ -299,36 +301,49 @@ __global__ void attn_combine_kernel(const float* __restrict__ ws, int nsplit, in
 // Merge split partials of one GDA group and apply gda_post_split:
 // out[h_o] = (o − λ·n) · rsqrt(mean d² + eps) · w · (1 − λ_init), with the
 // attention outputs rounded through fp16 first (the reference materialises
-// them as fp16 arrays between the two kernels).
+// them as fp16 arrays between the two kernels). Run by a CTA of 2D threads.
 template <int D, int GR>
-__global__ void gda_combine_kernel(const float* __restrict__ ws, int nsplit, int kv_len_host,
-                                   const int32_t* __restrict__ kv_len_dev, int q_origin,
-                                   const __half* __restrict__ subln_w,
-                                   const float* __restrict__ lam, int lam_mode, float out_scale,
-                                   float eps, __half* __restrict__ out) {
+__device__ __forceinline__ void gda_merge_group(const float* __restrict__ ws, int nsplit, int n_active, int g,
+                                                int q_origin, const __half* __restrict__ subln_w,
+                                                const float* __restrict__ lam, int lam_mode, float out_scale,
+                                                float eps, __half* __restrict__ out) {
   __shared__ float scratch[32 * GR];
   __shared__ float f_s[GR + 1][kMaxSplits];
   __shared__ float L_s[GR + 1];
-  pdl_trigger();
-  const int g = blockIdx.x;
   const int ch = threadIdx.x;  // 0 .. 2D-1
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int kv_len = kv_len_dev ? *kv_len_dev : kv_len_host;
-  int p0, p1, n_active;
-  split_range(kv_len, nsplit, 0, p0, p1, n_active);
   constexpr int stride = 2 * D + 2;
   if (warp <= GR) {
     const int head = warp < GR ? g * GR + warp : q_origin + g;
     split_weights(ws + (int64_t)head * nsplit * stride, n_active, stride, f_s[warp], &L_s[warp], lane);
   }
   __syncthreads();
-  float val[GR + 1];
+  // Σ_s f_j[s] · o_{j,s}[ch] for all GR+1 heads at once (their loads are independent).
+  const float* hb[GR + 1];
+  float acc[GR + 1];
 #pragma unroll
   for (int j = 0; j <= GR; ++j) {
-    const int head = j < GR ? g * GR + j : q_origin + g;
-    const float O = merge_channel(ws + (int64_t)head * nsplit * stride, f_s[j], n_active, stride, ch);
-    val[j] = round_through<__half>(L_s[j] > 0.f ? O / L_s[j] : 0.f);
+    hb[j] = ws + (int64_t)(j < GR ? g * GR + j : q_origin + g) * nsplit * stride + 2 + ch;
+    acc[j] = 0.f;
   }
+  int s = 0;
+  for (; s + 2 <= n_active; s += 2) {
+    float a0[GR + 1], a1[GR + 1];
+#pragma unroll
+    for (int j = 0; j <= GR; ++j) {
+      a0[j] = __ldcg(hb[j] + s * stride);
+      a1[j] = __ldcg(hb[j] + (s + 1) * stride);
+    }
+#pragma unroll
+    for (int j = 0; j <= GR; ++j) acc[j] += f_s[j][s] * a0[j] + f_s[j][s + 1] * a1[j];
+  }
+  if (s < n_active) {
+#pragma unroll
+    for (int j = 0; j <= GR; ++j) acc[j] += f_s[j][s] * __ldcg(hb[j] + s * stride);
+  }
+  float val[GR + 1];
+#pragma unroll
+  for (int j = 0; j <= GR; ++j) val[j] = round_through<__half>(L_s[j] > 0.f ? acc[j] / L_s[j] : 0.f);
   float d[GR], ssq[GR];
 #pragma unroll
   for (int j = 0; j < GR; ++j) {
@@ -344,6 +359,256 @@ __global__ void gda_combine_kernel(const float* __restrict__ ws, int nsplit, int
     const float inv = rsqrtf(ssq[j] / (float)(2 * D) + eps);
     out[(int64_t)(g * GR + j) * 2 * D + ch] = __float2half_rn(d[j] * inv * w * out_scale);
   }
+}
+
+template <int D, int GR>
+__global__ void gda_combine_kernel(const float* __restrict__ ws, int nsplit, int kv_len_host,
+                                   const int32_t* __restrict__ kv_len_dev, int q_origin,
+                                   const __half* __restrict__ subln_w,
+                                   const float* __restrict__ lam, int lam_mode, float out_scale,
+                                   float eps, __half* __restrict__ out) {
+  pdl_trigger();
+  const int kv_len = kv_len_dev ? *kv_len_dev : kv_len_host;
+  int p0, p1, n_active;
+  split_range(kv_len, nsplit, 0, p0, p1, n_active);
+  gda_merge_group<D, GR>(ws, nsplit, n_active, blockIdx.x, q_origin, subln_w, lam, lam_mode, out_scale, eps, out);
+}
+
+// ---- fused decode step: RoPE + 4-slot append + split-KV dual-V attention + GDA merge ----
+//
+// One launch per layer replaces rope_qkv_append, attn_split and gda_combine. Grid
+// (nsplit, q_groups), 256 threads. Every CTA rotates the q heads of its group straight
+// from the qkv row; the CTA whose position range holds `pos` first writes the new k/v
+// row of its group (RoPE on k, quantized when the cache is) and then reads it back like
+// any other row, so the attention sees exactly the stored values. Each CTA leaves its
+// softmax partials in the workspace; the last CTA of a group to arrive (per-group
+// counter at the head of the workspace, reset by that CTA) merges them and applies
+// gda_post_split.
+constexpr size_t kFusedCtlBytes = 256;  // per-group arrival counters (int32), zero between calls
+
+struct FusedArgs {
+  const __half* qkv;
+  const float* inv_freq;
+  int q_heads;   // q_origin + q_groups
+  int q_origin;  // q_groups · gr
+  int groups;    // q_groups = kv heads per slot
+  motif_kv4_slots cache;
+  const int32_t* pos_len;  // [pos, kv_len]
+  float scale_log2;
+  const __half* subln_w;
+  const float* lam;
+  int lam_mode;
+  float out_scale;
+  float eps;
+  __half* out;
+  float* ws;      // split partials
+  int* counters;  // [groups]
+};
+
+template <int BITS, int GR, int LPG>
+__global__ void __launch_bounds__(kAttnThreads) gda_fused_kernel(FusedArgs f) {
+  constexpr int D = 128, CPL = D / 32, NH = GR + 1, half = D / 2;
+  __shared__ float s_row[4][D];
+  __shared__ float s_cs[half], s_sn[half];
+  __shared__ int s_last;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int split = blockIdx.x, nsplit = gridDim.x;
+  const int g = blockIdx.y;
+  const int64_t cap = f.cache.capacity;
+  // a device kv_len beyond the cache is clamped (never read past the slots)
+  const int pos = f.pos_len[0], kv_len = max(0, min(f.pos_len[1], (int)cap));
+  int p0, p1, n_active;
+  split_range(kv_len, nsplit, split, p0, p1, n_active);
+  if (n_active < 1) n_active = 1;  // kv_len 0: split 0 still merges (to zeros)
+  if (split >= n_active) return;
+  const motif_kv4_slots& kv = f.cache;
+  const int64_t row0 = (int64_t)g * cap;
+  float ka[kPosPerWarp][CPL], kb[kPosPerWarp][CPL], x1[kPosPerWarp][CPL], x2[kPosPerWarp][CPL];
+  auto load_round = [&](int base) {
+#pragma unroll
+    for (int u = 0; u < kPosPerWarp; ++u) {
+      if (base + u < p1) {
+        const int64_t r = row0 + base + u;
+        load_kv<__half, D, BITS>(kv.data[0], kv.scales[0], kv.biases[0], r, lane, kv.group_size, ka[u]);
+        load_kv<__half, D, BITS>(kv.data[1], kv.scales[1], kv.biases[1], r, lane, kv.group_size, kb[u]);
+        load_kv<__half, D, BITS>(kv.data[2], kv.scales[2], kv.biases[2], r, lane, kv.group_size, x1[u]);
+        load_kv<__half, D, BITS>(kv.data[3], kv.scales[3], kv.biases[3], r, lane, kv.group_size, x2[u]);
+      }
+    }
+  };
+  const bool append = pos >= 0 && pos < cap && ((pos >= p0 && pos < p1) || (split == 0 && pos >= kv_len));
+  // The first round of this warp's rows does not depend on the RoPE work below (except in
+  // the CTA that writes row pos): start it now.
+  if (!append) load_round(p0 + warp * kPosPerWarp);
+  // RoPE angles of this position, shared by every head of the CTA
+  if (threadIdx.x < half) rope_angle(threadIdx.x, pos, f.inv_freq, s_cs[threadIdx.x], s_sn[threadIdx.x]);
+  __syncthreads();
+
+  // ---- append the new row of this group (k1, k2, v1, v2 by warps 0..3) ----
+  if (append) {
+    if (warp < 4) {
+      const int head = warp < 2 ? f.q_heads + 2 * g + warp : f.q_heads + 2 * f.groups + 2 * g + (warp - 2);
+      const __half* src = f.qkv + (int64_t)head * D;
+      const int64_t row = (int64_t)g * cap + pos;
+      __half hv[CPL];
+#pragma unroll
+      for (int j = 0; j < CPL; ++j) {
+        const int c = lane * CPL + j;
+        const int k = c < half ? c : c - half;
+        hv[j] = __float2half_rn(warp < 2 ? rope_rotate(src, c, half, s_cs[k], s_sn[k]) : __half2float(src[c]));
+      }
+      if constexpr (BITS == 16) {
+        __half* dst = static_cast<__half*>(f.cache.data[warp]) + row * D + lane * CPL;
+#pragma unroll
+        for (int j = 0; j < CPL; ++j) dst[j] = hv[j];
+      } else {
+#pragma unroll
+        for (int j = 0; j < CPL; ++j) s_row[warp][lane * CPL + j] = __half2float(hv[j]);
+        __syncwarp();
+        // lanes 0 .. D/8-1 quantize 8 channels each (the others feed zeros to the shuffles)
+        const bool act = lane < D / 8;
+        float x8[8];
+#pragma unroll
+        for (int t = 0; t < 8; ++t) x8[t] = act ? s_row[warp][lane * 8 + t] : 0.f;
+        uint32_t words[2];
+        float sc, bi;
+        quant_group<LPG>(x8, BITS, words, sc, bi);
+        if (act) {
+          constexpr int EL = 32 / BITS;
+          uint32_t* d = static_cast<uint32_t*>(f.cache.data[warp]) + row * (D / EL) + (lane * 8) / EL;
+          d[0] = words[0];
+          if constexpr (BITS == 8) d[1] = words[1];
+          const int gs = f.cache.group_size;
+          if (((lane * 8) % gs) == 0) {
+            const int64_t gi = row * (D / gs) + (lane * 8) / gs;
+            static_cast<__half*>(f.cache.scales[warp])[gi] = __float2half_rn(sc);
+            static_cast<__half*>(f.cache.biases[warp])[gi] = __float2half_rn(bi);
+          }
+        }
+      }
+    }
+    __syncthreads();  // the row is read back below (global writes ordered for the CTA)
+  }
+
+  // ---- rotated q of the group's GR origin heads and its noise head ----
+  float q[NH][CPL];
+#pragma unroll
+  for (int h = 0; h < NH; ++h) {
+    const int head = h < GR ? g * GR + h : f.q_origin + g;
+    const __half* src = f.qkv + (int64_t)head * D;
+#pragma unroll
+    for (int j = 0; j < CPL; ++j) {
+      const int c = lane * CPL + j, k = c < half ? c : c - half;
+      q[h][j] = __half2float(__float2half_rn(rope_rotate(src, c, half, s_cs[k], s_sn[k]))) * f.scale_log2;
+    }
+  }
+
+  float m[NH], l[NH], o1[NH][CPL], o2[NH][CPL];
+#pragma unroll
+  for (int h = 0; h < NH; ++h) {
+    m[h] = -INFINITY;
+    l[h] = 0.f;
+#pragma unroll
+    for (int c = 0; c < CPL; ++c) o1[h][c] = o2[h][c] = 0.f;
+  }
+  if (append) load_round(p0 + warp * kPosPerWarp);  // after the new row is written
+  for (int base = p0 + warp * kPosPerWarp; base < p1; base += kRoundPositions) {
+    if (base != p0 + warp * kPosPerWarp) load_round(base);
+#pragma unroll
+    for (int u = 0; u < kPosPerWarp; ++u) {
+      if (base + u >= p1) break;
+      float s[NH];
+#pragma unroll
+      for (int h = 0; h < GR; ++h) {
+        float t = 0.f;
+#pragma unroll
+        for (int c = 0; c < CPL; ++c) t += q[h][c] * ka[u][c];
+        s[h] = t;
+      }
+      {
+        float t = 0.f;
+#pragma unroll
+        for (int c = 0; c < CPL; ++c) t += q[GR][c] * kb[u][c];
+        s[GR] = t;
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+#pragma unroll
+        for (int h = 0; h < NH; ++h) s[h] += __shfl_xor_sync(0xffffffffu, s[h], o);
+      }
+#pragma unroll
+      for (int h = 0; h < NH; ++h) {
+        const float mn = fmaxf(m[h], s[h]);
+        const float fac = exp2f(m[h] - mn);
+        const float e = exp2f(s[h] - mn);
+        m[h] = mn;
+        l[h] = l[h] * fac + e;
+#pragma unroll
+        for (int c = 0; c < CPL; ++c) {
+          o1[h][c] = o1[h][c] * fac + e * x1[u][c];
+          o2[h][c] = o2[h][c] * fac + e * x2[u][c];
+        }
+      }
+    }
+  }
+
+  // The next kernel (the o projection) may start streaming its weights now: this CTA's
+  // cache reads are done, so they no longer compete with it.
+  pdl_trigger();
+  // ---- merge the warps' partial softmax states, write this split's partials ----
+  extern __shared__ float smem[];
+  float* sm_ml = smem;                       // [warp][h][2]
+  float* sm_o = smem + kAttnWarps * NH * 2;  // [warp][h][2D]
+#pragma unroll
+  for (int h = 0; h < NH; ++h) {
+    if (lane == 0) {
+      sm_ml[(warp * NH + h) * 2 + 0] = m[h];
+      sm_ml[(warp * NH + h) * 2 + 1] = l[h];
+    }
+    float* dst = sm_o + (int64_t)(warp * NH + h) * 2 * D + lane * CPL;
+#pragma unroll
+    for (int c = 0; c < CPL; ++c) {
+      dst[c] = o1[h][c];
+      dst[D + c] = o2[h][c];
+    }
+  }
+  __syncthreads();
+  for (int it = threadIdx.x; it < NH * 2 * D; it += kAttnThreads) {
+    const int h = it / (2 * D);
+    const int ch = it - h * 2 * D;
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < kAttnWarps; ++w) M = fmaxf(M, sm_ml[(w * NH + h) * 2]);
+    float L = 0.f, O = 0.f;
+    if (M != -INFINITY) {
+#pragma unroll
+      for (int w = 0; w < kAttnWarps; ++w) {
+        const float mw = sm_ml[(w * NH + h) * 2];
+        if (mw == -INFINITY) continue;
+        const float fw = exp2f(mw - M);
+        L += sm_ml[(w * NH + h) * 2 + 1] * fw;
+        O += sm_o[(int64_t)(w * NH + h) * 2 * D + ch] * fw;
+      }
+    }
+    const int hh = h < GR ? g * GR + h : f.q_origin + g;
+    float* p = f.ws + ((int64_t)hh * nsplit + split) * (2 * D + 2);
+    p[2 + ch] = O;
+    if (ch == 0) {
+      p[0] = M;
+      p[1] = L;
+    }
+  }
+
+  // ---- the last CTA of the group merges ----
+  __threadfence();  // release this CTA's partials before counting in
+  __syncthreads();
+  if (threadIdx.x == 0) s_last = atomicAdd(f.counters + g, 1) == n_active - 1;
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();  // acquire the other CTAs' partials
+  gda_merge_group<D, GR>(f.ws, nsplit, n_active, g, f.q_origin, f.subln_w, f.lam, f.lam_mode, f.out_scale, f.eps,
+                         f.out);
+  if (threadIdx.x == 0) f.counters[g] = 0;  // ready for the next launch
 }
 
 template <typename T, int D, int BITS, int MAXA, int NB>
@@ -613,6 +878,95 @@ int motif_gda_decode_attention(const void* q, const motif_kv4_slots* cache, floa
   }
 #undef MOTIF_FUSED
   return check_launch("gda decode attention");
+}
+
+size_t motif_gda_decode_step_workspace_bytes(int64_t q_heads, int64_t head_dim, int64_t max_splits) {
+  if (q_heads <= 0 || head_dim <= 0 || max_splits <= 0) return 0;
+  return kFusedCtlBytes + partial_bytes(q_heads, head_dim, max_splits < kMaxSplits ? max_splits : kMaxSplits);
+}
+
+int motif_gda_decode_step(const void* qkv, const float* inv_freq, const motif_kv4_slots* cache,
+                          const int32_t* pos_len, float scale, int64_t q_groups, int64_t gr,
+                          const void* subln_w, const float* lambda_full, int64_t lambda_len,
+                          float lambda_init, float eps, void* out, void* workspace,
+                          size_t workspace_bytes, void* stream) {
+  MOTIF_REQUIRE(qkv && inv_freq && cache && pos_len && subln_w && lambda_full && out && workspace, MOTIF_ERR_NULL,
+                "gda_decode_step: null pointer");
+  const motif_kv4_slots& c = *cache;
+  for (int i = 0; i < 4; ++i) MOTIF_REQUIRE(c.data[i], MOTIF_ERR_NULL, "gda_decode_step: slot %d null", i);
+  MOTIF_REQUIRE(c.batch == 1 && c.head_dim == 128, MOTIF_ERR_BAD_CONTRACT, "gda_decode_step: batch 1, head_dim 128 only");
+  MOTIF_REQUIRE(c.heads == q_groups && q_groups > 0, MOTIF_ERR_BAD_CONTRACT,
+                "gda_decode_step: kv heads per slot (%lld) must equal q_groups (%lld)", (long long)c.heads,
+                (long long)q_groups);
+  MOTIF_REQUIRE(gr == 3 || gr == 4, MOTIF_ERR_BAD_CONTRACT, "gda_decode_step: gr=%lld not built (3, 4)", (long long)gr);
+  MOTIF_REQUIRE(c.capacity > 0 && c.capacity < (1ll << 31), MOTIF_ERR_BAD_SHAPE, "gda_decode_step: capacity");
+  const int64_t q_origin = q_groups * gr;
+  const int64_t q_heads = q_origin + q_groups;
+  int lam_mode;
+  if (lambda_len == 1) lam_mode = 0;
+  else if (lambda_len == q_groups) lam_mode = 1;
+  else if (lambda_len == q_origin) lam_mode = 2;
+  else return fail(MOTIF_ERR_BAD_SHAPE, "gda_decode_step: lambda_len %lld", (long long)lambda_len);
+  const int bits = c.bits;
+  MOTIF_REQUIRE(bits == 16 || ((bits == 4 || bits == 8) && c.scales[0] && c.biases[0] && c.scales[1] && c.biases[1] &&
+                               c.scales[2] && c.biases[2] && c.scales[3] && c.biases[3] &&
+                               (c.group_size == 32 || c.group_size == 64 || c.group_size == 128)),
+                MOTIF_ERR_BAD_CONTRACT, "gda_decode_step: cache bits/group_size");
+  MOTIF_REQUIRE(q_groups * sizeof(int) <= kFusedCtlBytes, MOTIF_ERR_BAD_SHAPE, "gda_decode_step: too many groups");
+  MOTIF_REQUIRE(workspace_bytes > kFusedCtlBytes, MOTIF_ERR_WORKSPACE, "gda_decode_step: workspace too small");
+  const int64_t max_splits_ws = (workspace_bytes - kFusedCtlBytes) / partial_bytes(q_heads, 128, 1);
+  MOTIF_REQUIRE(max_splits_ws >= 1, MOTIF_ERR_WORKSPACE, "gda_decode_step: workspace too small");
+  const int nsplit = choose_splits(q_groups, c.capacity, max_splits_ws);
+
+  FusedArgs f{};
+  f.qkv = static_cast<const __half*>(qkv);
+  f.inv_freq = inv_freq;
+  f.q_heads = (int)q_heads;
+  f.q_origin = (int)q_origin;
+  f.groups = (int)q_groups;
+  f.cache = c;
+  f.pos_len = pos_len;
+  f.scale_log2 = scale * kLog2e;
+  f.subln_w = static_cast<const __half*>(subln_w);
+  f.lam = lambda_full;
+  f.lam_mode = lam_mode;
+  f.out_scale = 1.0f - lambda_init;
+  f.eps = eps;
+  f.out = static_cast<__half*>(out);
+  f.counters = static_cast<int*>(workspace);
+  f.ws = reinterpret_cast<float*>(static_cast<char*>(workspace) + kFusedCtlBytes);
+  cudaStream_t st = as_stream(stream);
+  dim3 grid(nsplit, (unsigned)q_groups);
+  cudaError_t e = cudaSuccess;
+#define MOTIF_FUSED_LAUNCH(BITS, GR, LPG)                                                              \
+  {                                                                                                     \
+    auto kern = gda_fused_kernel<BITS, GR, LPG>;                                                        \
+    const size_t smem = sizeof(float) * (size_t)kAttnWarps * (GR + 1) * (2 + 2 * 128);                 \
+    static bool configured = false;                                                                     \
+    if (!configured) {                                                                                  \
+      e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);           \
+      configured = e == cudaSuccess;                                                                    \
+    }                                                                                                   \
+    if (e == cudaSuccess) kern<<<grid, kAttnThreads, smem, st>>>(f);                                    \
+  }
+#define MOTIF_FUSED_BITS(GR)                                                    \
+  if (bits == 16) MOTIF_FUSED_LAUNCH(16, GR, 8)                                 \
+  else if (c.group_size == 32) {                                                \
+    if (bits == 4) MOTIF_FUSED_LAUNCH(4, GR, 4) else MOTIF_FUSED_LAUNCH(8, GR, 4) \
+  } else if (c.group_size == 64) {                                              \
+    if (bits == 4) MOTIF_FUSED_LAUNCH(4, GR, 8) else MOTIF_FUSED_LAUNCH(8, GR, 8) \
+  } else {                                                                      \
+    if (bits == 4) MOTIF_FUSED_LAUNCH(4, GR, 16) else MOTIF_FUSED_LAUNCH(8, GR, 16) \
+  }
+  if (gr == 3) {
+    MOTIF_FUSED_BITS(3)
+  } else {
+    MOTIF_FUSED_BITS(4)
+  }
+#undef MOTIF_FUSED_BITS
+#undef MOTIF_FUSED_LAUNCH
+  if (e != cudaSuccess) return fail(MOTIF_ERR_CUDA, "gda_decode_step: smem attribute: %s", cudaGetErrorString(e));
+  return check_launch("gda decode step");
 }
 
 }  // extern "C"

@@ -8,55 +8,10 @@
 // (one packed word at 4 bits, two at 8 bits); the gs/8 threads of one group
 // are consecutive lanes and reduce min/max with xor-shuffles.
 #include "common.cuh"
+#include "kvquant.cuh"
 
 namespace motif {
 namespace {
-
-// Quantize one group whose values are spread over LPG consecutive lanes, 8 per
-// lane. Returns this lane's packed word(s) and the group's scale and bias.
-template <int LPG>
-__device__ __forceinline__ void quant_group(const float (&v)[8], int bits, uint32_t (&words)[2],
-                                            float& scale_out, float& bias_out) {
-  float mx = v[0], mn = v[0];
-#pragma unroll
-  for (int j = 1; j < 8; ++j) {
-    mx = fmaxf(mx, v[j]);
-    mn = fminf(mn, v[j]);
-  }
-#pragma unroll
-  for (int o = LPG / 2; o > 0; o >>= 1) {
-    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-    mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, o));
-  }
-  const float n_bins = (float)((1 << bits) - 1);
-  float scale = fmaxf(__fdiv_rn(__fsub_rn(mx, mn), n_bins), 1e-7f);
-  const bool side = fabsf(mn) > fabsf(mx);
-  scale = side ? scale : -scale;
-  const float edge = side ? mn : mx;
-  const float q0 = roundf(__fdiv_rn(edge, scale));
-  const bool at_zero = (q0 == 0.0f);
-  scale = at_zero ? scale : __fdiv_rn(edge, q0);
-  const float bias = at_zero ? 0.0f : edge;
-  uint32_t codes[8];
-#pragma unroll
-  for (int j = 0; j < 8; ++j) {
-    float t = roundf(__fdiv_rn(__fsub_rn(v[j], bias), scale));
-    t = fminf(fmaxf(t, 0.0f), n_bins);
-    codes[j] = (uint32_t)t;
-  }
-  if (bits == 4) {
-    uint32_t w = 0;
-#pragma unroll
-    for (int j = 0; j < 8; ++j) w |= codes[j] << (4 * j);
-    words[0] = w;
-    words[1] = 0;
-  } else {  // 8 bits
-    words[0] = codes[0] | (codes[1] << 8) | (codes[2] << 16) | (codes[3] << 24);
-    words[1] = codes[4] | (codes[5] << 8) | (codes[6] << 16) | (codes[7] << 24);
-  }
-  scale_out = scale;
-  bias_out = bias;
-}
 
 // Maps a logical input row to its source pointer and its destination row.
 struct RowMap {
@@ -212,8 +167,8 @@ __global__ void rope_kernel(const T* __restrict__ x, int64_t rows, int S, int D,
   sincosf(theta, &sn, &cs);
   const float x1 = to_f<T>(x[row * D + k]);
   const float x2 = to_f<T>(x[row * D + k + half]);
-  y[row * D + k] = from_f<T>(x1 * cs - x2 * sn);
-  y[row * D + k + half] = from_f<T>(x1 * sn + x2 * cs);
+  y[row * D + k] = from_f<T>(__fsub_rn(__fmul_rn(x1, cs), __fmul_rn(x2, sn)));
+  y[row * D + k + half] = from_f<T>(__fadd_rn(__fmul_rn(x1, sn), __fmul_rn(x2, cs)));
 }
 
 // ---- decode prologue: RoPE(q), RoPE(k), 4-slot append ------------------------
@@ -236,13 +191,7 @@ __global__ void rope_qkv_append_kernel(const __half* __restrict__ qkv,
   const bool is_k = !is_q && head < q_heads + 2 * kv2;
   float v;
   if (is_q || is_k) {
-    const int k = c < half ? c : c - half;
-    const float theta = __fmul_rn((float)pos, inv_freq[k]);
-    float sn, cs;
-    sincosf(theta, &sn, &cs);
-    const float x1 = __half2float(src[k]);
-    const float x2 = __half2float(src[k + half]);
-    v = c < half ? x1 * cs - x2 * sn : x1 * sn + x2 * cs;
+    v = rope_channel(src, c, half, pos, inv_freq);
   } else {
     v = __half2float(src[c]);
   }

@@ -358,7 +358,12 @@ class MotifDecoder:
         if self.inter % 16:
             raise ValueError("intermediate size per rank must be a multiple of 16")
         self.lin_ws = torch.zeros(max(lin_ws, 16), dtype=torch.uint8, device=dev)
-        self.attn_ws_bytes = lib.motif_gda_decode_attention_workspace_bytes(self.q_heads, d, 64)
+        # MOTIF_FUSED_ATTN=0 runs RoPE/append and the attention as two calls (for comparisons).
+        self.fused_attn = os.environ.get("MOTIF_FUSED_ATTN", "1") != "0"
+        if self.fused_attn:
+            self.attn_ws_bytes = lib.motif_gda_decode_step_workspace_bytes(self.q_heads, d, 64)
+        else:
+            self.attn_ws_bytes = lib.motif_gda_decode_attention_workspace_bytes(self.q_heads, d, 64)
         self.attn_ws = torch.zeros(self.attn_ws_bytes, dtype=torch.uint8, device=dev)
         self.argmax_ws_bytes = lib.motif_argmax_workspace_bytes(self.V)
         self.argmax_ws = torch.zeros(self.argmax_ws_bytes, dtype=torch.uint8, device=dev)
@@ -457,13 +462,20 @@ class MotifDecoder:
         for li, L in enumerate(self.layers):
             qkv_io, o_io, gu_io, dn_io = plan[li]
             self._linear(qkv_io, L["qkv"], self.qkv, st)
-            check(lib.motif_rope_qkv_append(ptr(self.qkv), ptr(self.inv_freq), self.q_heads, self._slots[li], pos_p,
-                                            ptr(self.q), st), "rope_qkv_append")
-            check(lib.motif_gda_decode_attention(ptr(self.q), self._slots[li], self.scale, self.q_groups, self.gr, 0,
-                                                 kvl_p, ptr(L["subln"]), ptr(L["lambda_full"]),
-                                                 L["lambda_full"].numel(), L["lambda_init"],
-                                                 self.args.attn_rms_norm_eps, ptr(self.attn), ptr(self.attn_ws),
-                                                 self.attn_ws_bytes, st), "gda_decode_attention")
+            if self.fused_attn:
+                check(lib.motif_gda_decode_step(ptr(self.qkv), ptr(self.inv_freq), self._slots[li], pos_p, self.scale,
+                                                self.q_groups, self.gr, ptr(L["subln"]), ptr(L["lambda_full"]),
+                                                L["lambda_full"].numel(), L["lambda_init"],
+                                                self.args.attn_rms_norm_eps, ptr(self.attn), ptr(self.attn_ws),
+                                                self.attn_ws_bytes, st), "gda_decode_step")
+            else:
+                check(lib.motif_rope_qkv_append(ptr(self.qkv), ptr(self.inv_freq), self.q_heads, self._slots[li],
+                                                pos_p, ptr(self.q), st), "rope_qkv_append")
+                check(lib.motif_gda_decode_attention(ptr(self.q), self._slots[li], self.scale, self.q_groups, self.gr,
+                                                     0, kvl_p, ptr(L["subln"]), ptr(L["lambda_full"]),
+                                                     L["lambda_full"].numel(), L["lambda_init"],
+                                                     self.args.attn_rms_norm_eps, ptr(self.attn), ptr(self.attn_ws),
+                                                     self.attn_ws_bytes, st), "gda_decode_attention")
             self._linear(o_io, L["o"], self.o, st)
             self._allreduce(self.o)
             self._linear(gu_io, L["gate_up"], self.gu, st)

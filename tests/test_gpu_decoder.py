@@ -284,6 +284,75 @@ def test_fused_rope_append_and_gda_attention(cuda, cache_kind, kv_len):
     assert_close(down(out), ref.reshape(-1).astype(np.float64), "float16", what="fused attention")
 
 
+@pytest.mark.parametrize("cache_kind", ["fp16", "q4", "q8", "q4g32"])
+@pytest.mark.parametrize("kv_len", [1, 37, 200, 3000])
+def test_gda_decode_step_equals_two_call_path(cuda, cache_kind, kv_len):
+    """motif_gda_decode_step (one launch) == motif_rope_qkv_append + motif_gda_decode_attention
+    bit for bit: the attention output and every slot of the cache (codes, scales, biases);
+    a repeated launch gives the same output (its per-group counters reset)."""
+    from mlx_motif import _native as N
+    from mlx_motif.cache import MotifGroupedKVCache, MotifGroupedQuantizedKVCache
+    from mlx_motif.model import rope_inv_freq
+
+    rng = np.random.default_rng(100 + kv_len)
+    G, gr, d, cap = 8, 3, 128, 4096
+    qh = G * (gr + 1)
+    pos = kv_len - 1
+    hist = [up(rounded(rng.standard_normal((1, G, pos, d)) * 0.5, "float16")) for _ in range(4)]
+    tq = up(rounded(rng.standard_normal(qh * d + 4 * G * d), "float16"))
+
+    def make():
+        if cache_kind == "fp16":
+            c = MotifGroupedKVCache(max_size=cap)
+            if pos:
+                c.update_and_fetch_4(*hist)
+        else:
+            gs = 32 if cache_kind == "q4g32" else 64
+            c = MotifGroupedQuantizedKVCache(gs, 8 if cache_kind == "q8" else 4, max_size=cap)
+            if pos:
+                c.update_and_fetch_4_quantized(*hist)
+        if not pos:
+            c._grow(1, G, 1, d, torch.float16, cuda)
+        return c
+
+    ca, cb = make(), make()
+    inv = rope_inv_freq(d, 10000.0, cuda)
+    pos_t = torch.tensor([pos, kv_len], dtype=torch.int32, device=cuda)
+    t_sub = up(rounded(1 + 0.02 * rng.standard_normal(2 * d), "float16"))
+    t_lam = torch.tensor(rng.uniform(0.1, 0.6, G * gr).astype(np.float32), device=cuda)
+    # two-call path on cache a
+    q_out = torch.empty(qh * d, dtype=torch.float16, device=cuda)
+    sa = ca.slots_struct()
+    N.check(N.lib.motif_rope_qkv_append(tq.data_ptr(), inv.data_ptr(), qh, sa, pos_t.data_ptr(), q_out.data_ptr(),
+                                        N.stream()))
+    ref = torch.empty(G * gr * 2 * d, dtype=torch.float16, device=cuda)
+    ws_b = N.lib.motif_gda_decode_attention_workspace_bytes(qh, d, 64)
+    ws = torch.zeros(ws_b, dtype=torch.uint8, device=cuda)
+    N.check(N.lib.motif_gda_decode_attention(q_out.data_ptr(), sa, d ** -0.5, G, gr, 0, pos_t.data_ptr() + 4,
+                                             t_sub.data_ptr(), t_lam.data_ptr(), G * gr, 0.8, 1e-5, ref.data_ptr(),
+                                             ws.data_ptr(), ws_b, N.stream()))
+    # one launch on cache b, twice
+    sb = cb.slots_struct()
+    fb = N.lib.motif_gda_decode_step_workspace_bytes(qh, d, 64)
+    fws = torch.zeros(fb, dtype=torch.uint8, device=cuda)
+    outs = []
+    for _ in range(2):
+        out = torch.full((G * gr * 2 * d,), float("nan"), dtype=torch.float16, device=cuda)
+        N.check(N.lib.motif_gda_decode_step(tq.data_ptr(), inv.data_ptr(), sb, pos_t.data_ptr(), d ** -0.5, G, gr,
+                                            t_sub.data_ptr(), t_lam.data_ptr(), G * gr, 0.8, 1e-5, out.data_ptr(),
+                                            fws.data_ptr(), fb, N.stream()), "gda_decode_step")
+        torch.cuda.synchronize()
+        outs.append(out)
+    assert torch.equal(outs[0], ref), "fused step differs from the two-call path"
+    assert torch.equal(outs[1], ref), "repeated fused step differs (counters not reset?)"
+    assert torch.equal(fws[:256], torch.zeros(256, dtype=torch.uint8, device=cuda))
+    names = ("k1", "k2", "v1", "v2")
+    for n in names:
+        a, b = getattr(ca, n), getattr(cb, n)
+        for x, y in (zip(a, b) if isinstance(a, tuple) else [(a, b)]):
+            assert torch.equal(x[..., :kv_len, :], y[..., :kv_len, :]), f"cache slot {n} differs"
+
+
 # ---------------------------------------------------------------- whole decoder
 def _tiny_args():
     return O.OracleArgs(hidden_size=256, num_hidden_layers=3, intermediate_size=512, num_noise_heads=8,
