@@ -176,7 +176,11 @@ MOTIF_API int motif_gda_decode_attention(const void* q, const motif_kv4_slots* c
  * positions [0, kv_len). Results equal the two-call sequence bit for bit.
  * workspace: motif_gda_decode_step_workspace_bytes(q_heads, 128, splits)
  * bytes (splits <= 64), zero-filled before first use; its first 256 bytes
- * hold per-group counters that the kernel leaves zeroed. */
+ * hold per-group counters that the kernel leaves zeroed.
+ * Launched with programmatic dependent launch: before it waits for the
+ * previous kernel in the stream it already reads pos_len, inv_freq and the
+ * cache rows other than pos, so that previous kernel must not write those
+ * (in the decoder it is the qkv projection). */
 MOTIF_API size_t motif_gda_decode_step_workspace_bytes(int64_t q_heads, int64_t head_dim, int64_t max_splits);
 MOTIF_API int motif_gda_decode_step(const void* qkv, const float* inv_freq, const motif_kv4_slots* cache,
                                     const int32_t* pos_len, float scale, int64_t q_groups, int64_t gr,

@@ -442,6 +442,10 @@ __global__ void __launch_bounds__(kAttnThreads) gda_fused_kernel(FusedArgs f) {
   if (!append) load_round(p0 + warp * kPosPerWarp);
   // RoPE angles of this position, shared by every head of the CTA
   if (threadIdx.x < half) rope_angle(threadIdx.x, pos, f.inv_freq, s_cs[threadIdx.x], s_sn[threadIdx.x]);
+  // Launched with programmatic serialization: everything above reads only data that
+  // kernels before the previous one wrote (cache rows < pos, pos_len, inv_freq). The qkv
+  // row comes from the previous kernel (the qkv projection): wait for it here.
+  asm volatile("griddepcontrol.wait;\n" ::: "memory");
   __syncthreads();
 
   // ---- append the new row of this group (k1, k2, v1, v2 by warps 0..3) ----
@@ -947,7 +951,19 @@ int motif_gda_decode_step(const void* qkv, const float* inv_freq, const motif_kv
       e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);           \
       configured = e == cudaSuccess;                                                                    \
     }                                                                                                   \
-    if (e == cudaSuccess) kern<<<grid, kAttnThreads, smem, st>>>(f);                                    \
+    if (e == cudaSuccess) {                                                                             \
+      cudaLaunchConfig_t cfg = {};                                                                      \
+      cfg.gridDim = grid;                                                                               \
+      cfg.blockDim = dim3(kAttnThreads);                                                                \
+      cfg.dynamicSmemBytes = smem;                                                                      \
+      cfg.stream = st;                                                                                  \
+      cudaLaunchAttribute attr[1];                                                                      \
+      attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;                                  \
+      attr[0].val.programmaticStreamSerializationAllowed = 1;                                           \
+      cfg.attrs = attr;                                                                                 \
+      cfg.numAttrs = 1;                                                                                 \
+      e = cudaLaunchKernelEx(&cfg, kern, f);                                                            \
+    }                                                                                                   \
   }
 #define MOTIF_FUSED_BITS(GR)                                                    \
   if (bits == 16) MOTIF_FUSED_LAUNCH(16, GR, 8)                                 \
@@ -965,7 +981,7 @@ int motif_gda_decode_step(const void* qkv, const float* inv_freq, const motif_kv
   }
 #undef MOTIF_FUSED_BITS
 #undef MOTIF_FUSED_LAUNCH
-  if (e != cudaSuccess) return fail(MOTIF_ERR_CUDA, "gda_decode_step: smem attribute: %s", cudaGetErrorString(e));
+  if (e != cudaSuccess) return fail(MOTIF_ERR_CUDA, "gda_decode_step: launch: %s", cudaGetErrorString(e));
   return check_launch("gda decode step");
 }
 
