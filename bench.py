@@ -384,7 +384,7 @@ def run_b200(a) -> None:
         torch.cuda.synchronize()
         torch.cuda.cudart().cudaProfilerStop()
         if rank == 0:
-            print(json.dumps({"profile_steps": a.steps, "kernels_per_step": model_launches(args, world)}))
+            print(json.dumps({"profile_steps": a.steps, "kernels_per_step": model_launches(model)}))
         return
 
     sampler = ClockSampler(local) if rank == 0 else None
@@ -484,7 +484,7 @@ def run_b200(a) -> None:
                        "model": "motif-12.7B-class (48L, H4096, 24+8 q heads, 8 kv/slot, I14336, V219520)",
                        "global_batch": 1, "seq_len": PROMPT_LEN, "parallelism": f"tp{world}" if world > 1 else "single",
                        "l2": "inputs larger than L2: 6.85 GB of weights stream from HBM every step"},
-            "e2e": e2e, "gpu_launches": model_launches(args, world) * a.steps,
+            "e2e": e2e, "gpu_launches": model_launches(model) * a.steps,
             "roofline": roofline, "cpu_baseline": cpu, "clocks": clocks, "extra": extra,
         }
         print(json.dumps(line), flush=True)
@@ -494,20 +494,14 @@ def run_b200(a) -> None:
         dist.destroy_process_group()
 
 
-def model_launches(args, world: int) -> int:
-    """Kernels of this library per decode step (torch's one-element position increment excluded)."""
-    from mlx_motif._native import lib
-
-    H, d = args.hidden_size, args.d
-    qkv_n = (args.q_heads * d + 4 * args.k_noise_heads * d) // world
-    shapes = [(qkv_n, H), (H, args.q_origin * 2 * d // world), (2 * args.intermediate_size // world, H),
-              (H, args.intermediate_size // world)]
-    per_layer = 0
-    for n, k in shapes:
-        per_layer += 1 + (1 if lib.motif_quantized_linear_workspace_bytes(1, n, k, 4, 64) > 0 else 0)
-    per_layer += 1 + 2 + 1 + 1 + 1  # rope+append, attention (2), add_rms, polynorm_mul, add_rms
-    head = 1 + (1 if lib.motif_quantized_linear_workspace_bytes(1, args.vocab_size, H, 4, 64) > 0 else 0) + 2
-    return 1 + args.num_hidden_layers * per_layer + head
+def model_launches(model) -> int:
+    """Kernels of this library per decode step with the head: per layer the four q4 GEMVs (norms,
+    residuals and PolyNorm fused into their prologues) and the attention step (one fused launch, or
+    RoPE/append + split-KV + combine), then the lm_head GEMV (its epilogue picks the token, or two
+    argmax kernels; torch's position increment in that case is not counted)."""
+    per_layer = 4 + (1 if model.fused_attn else 3)
+    head = 1 + (0 if model.fused_argmax else 2)
+    return len(model.layers) * per_layer + head
 
 
 # --------------------------------------------------------------------------- #

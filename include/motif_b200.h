@@ -257,6 +257,13 @@ MOTIF_API int motif_quantized_linear(int dtype, int bits, int group_size, const 
  *           (h_out must not alias h_in).
  *   mode 2: x = fp16(polynorm(gate))·up, PolyNorm statistics = the sum of
  *           stats_count (Σg², Σg⁴, Σg⁶) triplets at `stats`, mean over poly_dim.
+ * argmax_out (optional): the greedy token — index of the largest fp16 output
+ * (first on ties, NaN below everything, as motif_argmax) — written once the
+ * last output tile is done; the lm_head then needs no argmax launch (greedy
+ * sampling in mlx-lm generate_step). pos_len_inc (optional, with argmax_out):
+ * int32[2] incremented by one each after the token is written (the decode
+ * step's position and kv_len). This state lives in the workspace's counter
+ * region, so a workspace serves one such launch at a time.
  * stats_out (optional): for output rows [0, stats_rows) (a multiple of 16),
  * one (Σy², Σy⁴, Σy⁶) triplet per 16-row tile of the fp16-rounded outputs.
  * workspace: motif_linear_fused_workspace_bytes(n, k) bytes, zero-filled
@@ -286,6 +293,8 @@ typedef struct motif_linear_io {
   int64_t poly_dim;
   float* stats_out;
   int64_t stats_rows;
+  int32_t* argmax_out;
+  int32_t* pos_len_inc;
 } motif_linear_io;
 
 MOTIF_API size_t motif_linear_fused_workspace_bytes(int64_t n, int64_t k);

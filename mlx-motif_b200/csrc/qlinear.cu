@@ -90,8 +90,14 @@ constexpr int kZeroBytes = 768;
 // Workspace layout: [tile counters: kCounterTiles int32][split-K partials]. The
 // counter region has a fixed size so that GEMVs of different shapes can share
 // one workspace: partials of one shape never land on another shape's counters.
-constexpr int64_t kCounterTiles = 16384;  // N up to 262144 rows
+constexpr int64_t kCounterTiles = 16384;
 constexpr size_t kCounterBytes = sizeof(int) * kCounterTiles;
+// Control words at the top of the counter region: [kCounterTiles-1] error word,
+// [kCounterTiles-2] argmax tiles finished, [kCounterTiles-4 .. -3] argmax key (8-byte aligned).
+constexpr int64_t kErrSlot = kCounterTiles - 1;
+constexpr int64_t kAmaxTilesSlot = kCounterTiles - 2;
+constexpr int64_t kAmaxKeySlot = kCounterTiles - 4;
+constexpr int64_t kTileCounterCap = kCounterTiles - 4;  // split-tile counters: N up to 262080 rows
 
 enum : int { kModeX = 0, kModeAddRms = 1, kModePoly = 2 };
 
@@ -134,6 +140,11 @@ struct LinArgs {
   // epilogue
   float* stats_out;
   int64_t stats_rows;
+  // fused greedy argmax over the outputs (optional)
+  unsigned long long* amax_key;  // packed (ordered value, inverted index), 0 between calls
+  int* amax_tiles;               // finished tiles, 0 between calls
+  int32_t* argmax_out;
+  int32_t* pos_len_inc;
 };
 
 struct UnitRegs {
@@ -293,6 +304,38 @@ __device__ void tile_epilogue(const LinArgs& a, int tile, int gw, float acc_r, f
       a.stats_out[tile * 3 + 0] = s2;
       a.stats_out[tile * 3 + 1] = s4;
       a.stats_out[tile * 3 + 2] = s6;
+    }
+  }
+  if (a.argmax_out && any) {
+    // Key of this lane's row: value bits mapped to an unsigned order (NaN as -inf) above the
+    // inverted row index, so the largest key is the largest value at its first index.
+    unsigned long long key = 0;
+    if (have && row < a.N) {
+      float f = __half2float(hv);
+      if (isnan(f)) f = -INFINITY;
+      const uint32_t b = __float_as_uint(f);
+      const uint32_t hi = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+      key = ((unsigned long long)hi << 32) | (0xFFFFFFFFu - (uint32_t)row);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const unsigned long long other = __shfl_xor_sync(0xffffffffu, key, o);
+      key = other > key ? other : key;
+    }
+    if (lane == 0) {
+      atomicMax(a.amax_key, key);
+      __threadfence();
+      if (atomicAdd(a.amax_tiles, 1) == a.ntiles - 1) {
+        // every tile's key is in: publish the token and reset the state
+        __threadfence();
+        const unsigned long long k = atomicExch(a.amax_key, 0ull);
+        atomicExch(a.amax_tiles, 0);
+        a.argmax_out[0] = k == 0 ? 0 : (int32_t)(0xFFFFFFFFu - (uint32_t)(k & 0xFFFFFFFFull));
+        if (a.pos_len_inc) {
+          a.pos_len_inc[0] += 1;
+          a.pos_len_inc[1] += 1;
+        }
+      }
     }
   }
 }
@@ -919,15 +962,22 @@ int launch_q4(LinArgs& a, void* workspace, size_t ws_bytes, cudaStream_t st) {
     const size_t need = plan_ws_bytes(p);
     if (!workspace || ws_bytes < need)
       return fail(MOTIF_ERR_WORKSPACE, "quantized_linear: workspace %zu < %zu bytes", ws_bytes, need);
-    if (p.ntiles >= kCounterTiles)
+    if (p.ntiles > kTileCounterCap)
       return fail(MOTIF_ERR_BAD_SHAPE, "quantized_linear: n=%lld rows exceed %lld", (long long)a.N,
-                  (long long)((kCounterTiles - 1) * kTileRows));
+                  (long long)(kTileCounterCap * kTileRows));
     a.counters = static_cast<int*>(workspace);
     a.partial = reinterpret_cast<float*>(static_cast<char*>(workspace) + kCounterBytes);
-    a.err = a.counters + (kCounterTiles - 1);  // last counter slot doubles as the error word
+    a.err = a.counters + kErrSlot;
   } else {
     a.counters = nullptr;
     a.partial = nullptr;
+  }
+  if (a.argmax_out) {  // the argmax state lives in the workspace's control words
+    if (!workspace || ws_bytes < kCounterBytes)
+      return fail(MOTIF_ERR_WORKSPACE, "linear_fused: argmax needs a workspace of >= %zu bytes", kCounterBytes);
+    int* ctl = static_cast<int*>(workspace);
+    a.amax_key = reinterpret_cast<unsigned long long*>(ctl + kAmaxKeySlot);
+    a.amax_tiles = ctl + kAmaxTilesSlot;
   }
   static bool configured = false;
   if (!configured) {
@@ -1019,7 +1069,8 @@ int motif_quantized_linear(int dtype, int bits, int group_size, const void* x, i
 }
 
 size_t motif_linear_fused_workspace_bytes(int64_t n, int64_t k) {
-  return motif_quantized_linear_workspace_bytes(1, n, k, 4, 64);
+  const size_t b = motif_quantized_linear_workspace_bytes(1, n, k, 4, 64);
+  return b > kCounterBytes ? b : kCounterBytes;  // the control words (argmax state) always fit
 }
 
 int motif_linear_fused(const motif_linear_io* io, const uint32_t* w, const void* scales,
@@ -1074,6 +1125,9 @@ int motif_linear_fused(const motif_linear_io* io, const uint32_t* w, const void*
     default:
       return fail(MOTIF_ERR_BAD_SHAPE, "linear_fused: mode %d not in {0,1,2}", io->mode);
   }
+  MOTIF_REQUIRE(!io->pos_len_inc || io->argmax_out, MOTIF_ERR_BAD_CONTRACT, "linear_fused: pos_len_inc needs argmax_out");
+  a.argmax_out = io->argmax_out;
+  a.pos_len_inc = io->pos_len_inc;
   if (io->stats_out) {
     MOTIF_REQUIRE(io->stats_rows > 0 && io->stats_rows % kTileRows == 0 && io->stats_rows <= n, MOTIF_ERR_BAD_SHAPE,
                   "linear_fused: stats_rows must be a positive multiple of 16 and <= n");

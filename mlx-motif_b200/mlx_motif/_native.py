@@ -62,6 +62,8 @@ class motif_linear_io(C.Structure):  # noqa: N801 — mirrors the C struct name
         ("poly_dim", C.c_int64),
         ("stats_out", C.c_void_p),
         ("stats_rows", C.c_int64),
+        ("argmax_out", C.c_void_p),
+        ("pos_len_inc", C.c_void_p),
     ]
 
 

@@ -437,7 +437,11 @@ class MotifDecoder:
                              poly_w=ptr(L["polynorm_w"]), poly_b=ptr(L["polynorm_b"]), poly_eps=1e-6,
                              poly_dim=self.args.intermediate_size)
             plan.append((qkv_io, o_io, gu_io, dn_io))
-        head_io = self._io(1, h_in=ptr(self.h_a), delta=ptr(self.dn), norm_w=ptr(self.final_norm), eps=eps)
+        # The lm_head GEMV also picks the greedy token and advances pos_len (MOTIF_FUSED_ARGMAX=0: separate
+        # argmax launches).
+        self.fused_argmax = os.environ.get("MOTIF_FUSED_ARGMAX", "1") != "0"
+        extra = dict(argmax_out=ptr(self.token), pos_len_inc=ptr(self.pos_len)) if self.fused_argmax else {}
+        head_io = self._io(1, h_in=ptr(self.h_a), delta=ptr(self.dn), norm_w=ptr(self.final_norm), eps=eps, **extra)
         self._plan = (plan, head_io)
 
     def _linear(self, io, ql: QuantizedLinear, out: torch.Tensor, st: int) -> None:
@@ -450,7 +454,8 @@ class MotifDecoder:
         Per layer: qkv GEMV (prologue: [embedding +] residual + input RMSNorm), RoPE + 4-slot
         append, dual-V attention + GDA post (2 kernels), o_proj GEMV, gate|up GEMV (prologue:
         residual + post-attention RMSNorm; epilogue: PolyNorm statistics), down GEMV (prologue:
-        PolyNorm·up). Head: lm_head GEMV (prologue: residual + final norm), argmax.
+        PolyNorm·up). Head: lm_head GEMV (prologue: residual + final norm; epilogue: greedy token and
+        position advance, or a separate argmax when MOTIF_FUSED_ARGMAX=0).
         """
         if getattr(self, "_plan", None) is None:
             self._build_plan()
@@ -485,8 +490,14 @@ class MotifDecoder:
                 self._allreduce(self.stats_sum)
             self._linear(dn_io, L["down"], self.dn, st)
             self._allreduce(self.dn)
+        self._head(with_head, head_io, st)
+
+    def _head(self, with_head: bool, head_io, st: int) -> None:
+        """lm_head + greedy token + position advance (one launch when the argmax is fused)."""
         if with_head:
             self._linear(head_io, self.lm_head, self.logits, st)
+            if self.fused_argmax:
+                return  # the GEMV wrote the token and advanced pos_len
             check(lib.motif_argmax(0, ptr(self.logits), self.V, ptr(self.token), ptr(self.argmax_ws),
                                    self.argmax_ws_bytes, st), "argmax")
         self.pos_len.add_(self._one_one)

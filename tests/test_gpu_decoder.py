@@ -208,6 +208,39 @@ def test_quantized_cache_state_roundtrip(cuda, bits):
     assert cache.trim(2) == 2 and cache.offset == 1 and cache.is_trimmable()
 
 
+@pytest.mark.parametrize("N_rows,K", [(1000, 512), (219520 // 8, 4096), (300, 384)])
+def test_linear_fused_argmax_epilogue(cuda, N_rows, K):
+    """argmax_out / pos_len_inc of motif_linear_fused: the first index of the largest fp16 output
+    (rows 5 and 13 tie), a NaN output never wins, equal to motif_argmax on the written outputs,
+    pos_len advanced by one per launch, state reset between launches (TMA path for K % 512 == 0,
+    register path otherwise)."""
+    from mlx_motif import _native as N
+    from mlx_motif.quantization import quantize
+
+    rng = np.random.default_rng(N_rows + K)
+    w = rng.standard_normal((N_rows, K)).astype(np.float32) * 0.02
+    w[5] = w[13] = 1.0  # same 16-row tile: identical accumulation order, so an exact tie
+    q = quantize(up(rounded(w, "float16")), 64, 4)
+    q[1][3, 0] = float("nan")  # row 3's output is NaN
+    x = up(rounded(np.abs(rng.standard_normal(K)) * 0.01, "float16"))
+    y = torch.empty(N_rows, dtype=torch.float16, device=cuda)
+    tok = torch.full((1,), -1, dtype=torch.int32, device=cuda)
+    pos_len = torch.tensor([10, 11], dtype=torch.int32, device=cuda)
+    ws = torch.zeros(N.lib.motif_linear_fused_workspace_bytes(N_rows, K), dtype=torch.uint8, device=cuda)
+    io = N.motif_linear_io()
+    io.mode, io.x, io.argmax_out, io.pos_len_inc = 0, x.data_ptr(), tok.data_ptr(), pos_len.data_ptr()
+    ref = torch.empty(1, dtype=torch.int32, device=cuda)
+    aws = torch.empty(N.lib.motif_argmax_workspace_bytes(N_rows), dtype=torch.uint8, device=cuda)
+    for i in range(2):
+        tok.fill_(-1)
+        _fused(N, io, q, y, ws)
+        N.check(N.lib.motif_argmax(0, y.data_ptr(), N_rows, ref.data_ptr(), aws.data_ptr(), aws.numel(), N.stream()))
+        torch.cuda.synchronize()
+        assert torch.isnan(y[3]).item()
+        assert int(tok.item()) == 5 == int(ref.item()), (int(tok.item()), int(ref.item()))
+        assert pos_len.tolist() == [11 + i, 12 + i]
+
+
 # ---------------------------------------------------------------- fused decode layer attention
 @pytest.mark.parametrize("cache_kind", ["fp16", "q4", "q8"])
 @pytest.mark.parametrize("kv_len", [1, 37, 200, 3000])
