@@ -441,7 +441,9 @@ def run_b200(a) -> None:
     # ---- config[2]: p16k with q4 and fp16 caches ----
     if not a.no_long:
         weights = model.weights_dict()
+        model._graphs.clear()  # graphs may hold NCCL calls: released before the communicator
         del model
+        model = None
         torch.cuda.empty_cache()
         for kind in ("q4", "fp16"):
             m = MotifDecoder(args, weights, cache=kind, max_seq=16000 + a.warmup + a.steps + 8, device=dev,
@@ -466,6 +468,7 @@ def run_b200(a) -> None:
                 "attention_ms_per_step": round(att["ms_48_layers"], 4),
                 "peak_hbm_bytes": int(torch.cuda.max_memory_allocated(dev)),
             }
+            m._graphs.clear()
             del m
             torch.cuda.empty_cache()
 
@@ -488,6 +491,9 @@ def run_b200(a) -> None:
             "roofline": roofline, "cpu_baseline": cpu, "clocks": clocks, "extra": extra,
         }
         print(json.dumps(line), flush=True)
+    if model is not None:
+        model._graphs.clear()
+    torch.cuda.synchronize()
     if world > 1:
         import torch.distributed as dist
 
@@ -500,7 +506,10 @@ def model_launches(model) -> int:
     RoPE/append + split-KV + combine), then the lm_head GEMV (its epilogue picks the token, or two
     argmax kernels; torch's position increment in that case is not counted)."""
     per_layer = 4 + (1 if model.fused_attn else 3)
-    head = 1 + (0 if model.fused_argmax else 2)
+    if model.tp_group is not None:
+        head = 2  # vocabulary shard GEMV + key decode (the all-reduce is NCCL's)
+    else:
+        head = 1 + (0 if model.fused_argmax else 2)
     return len(model.layers) * per_layer + head
 
 

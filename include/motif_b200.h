@@ -264,6 +264,23 @@ MOTIF_API int motif_quantized_linear(int dtype, int bits, int group_size, const 
  * int32[2] incremented by one each after the token is written (the decode
  * step's position and kv_len). This state lives in the workspace's counter
  * region, so a workspace serves one such launch at a time.
+ * argmax_key_out (optional, for a vocabulary shard of a tensor-parallel
+ * lm_head): the winner as one int64 key — order-preserving value bits above
+ * the inverted GLOBAL row (row + argmax_row_offset), top bit flipped — so the
+ * largest key over all shards (an int64 MAX all-reduce) is the global greedy
+ * token; motif_argmax_key_decode turns it into the token.
+ * Tensor-parallel exchange (replaces the all-reduces of a row-parallel
+ * o_proj / down_proj and of the PolyNorm statistics, reference model.py:836
+ * and 267): a producer stores each fp32 output row (tp_out) and/or each tile
+ * statistic (tp_stats) into every rank's buffer as a (value, number) pair —
+ * one 8-byte store, so a pair is valid on its own and no fence or flag is
+ * needed; a consumer reads the pairs of all ranks, re-reading (bounded) any
+ * whose number is not yet this exchange's: tp_in in mode 1 (the residual delta
+ * is the fp16-rounded sum of the ranks' partials, summed in rank order, so
+ * every rank gets the same bits), tp_stats_in in mode 2. Buffers come from
+ * motif_ipc_alloc / motif_ipc_open and must be zeroed whenever the position
+ * is rewound. A wait that runs out sets the workspace's error word and the
+ * kernel goes on (its outputs are then garbage).
  * stats_out (optional): for output rows [0, stats_rows) (a multiple of 16),
  * one (Σy², Σy⁴, Σy⁶) triplet per 16-row tile of the fp16-rounded outputs.
  * workspace: motif_linear_fused_workspace_bytes(n, k) bytes, zero-filled
@@ -295,12 +312,37 @@ typedef struct motif_linear_io {
   int64_t stats_rows;
   int32_t* argmax_out;
   int32_t* pos_len_inc;
+  int64_t* argmax_key_out;
+  int64_t argmax_row_offset;
+  /* tensor-parallel exchange over peer memory (optional; tp_world <= 8). Every
+   * value travels as one 8-byte (fp32 value, int32 number) pair, number =
+   * (*tp_seq + 1) * 1024 + tp_tag. */
+  int32_t tp_world;
+  const int32_t* tp_seq;        /* device int32 (the decode position) */
+  int32_t tp_tag;               /* 0..1023: which exchange of the step */
+  int64_t* tp_out[8];           /* producer: this rank's output rows' pairs in each rank's buffer */
+  int64_t* tp_stats[8];         /* producer: this rank's tile statistics' pairs in each rank's buffer */
+  const int64_t* tp_in;         /* consumer, mode 1: [tp_world][K] pairs; delta = fp16(sum of the ranks') */
+  const int64_t* tp_stats_in;   /* consumer, mode 2: [stats_count][3] pairs of all ranks' tiles */
 } motif_linear_io;
 
 MOTIF_API size_t motif_linear_fused_workspace_bytes(int64_t n, int64_t k);
 MOTIF_API int motif_linear_fused(const motif_linear_io* io, const uint32_t* w, const void* scales,
                                  const void* biases, int64_t n, int64_t k, void* y, void* workspace,
                                  size_t workspace_bytes, void* stream);
+
+/* ---- peer-to-peer buffers for the tensor-parallel exchange --------------------
+ * No reference counterpart (the reference runs on one device). One buffer per
+ * rank from cudaMalloc, shared with the other processes of the node through
+ * CUDA IPC: motif_ipc_alloc returns the pointer and a handle of
+ * motif_ipc_handle_bytes() bytes; the other ranks motif_ipc_open that handle.
+ * The buffer is zero-filled. */
+MOTIF_API size_t motif_ipc_handle_bytes(void);
+MOTIF_API int motif_ipc_alloc(size_t bytes, void** ptr, void* handle);
+MOTIF_API int motif_ipc_open(const void* handle, void** ptr);
+MOTIF_API int motif_ipc_close(void* ptr);
+MOTIF_API int motif_ipc_zero(void* ptr, size_t bytes, void* stream);
+MOTIF_API int motif_ipc_free(void* ptr);
 
 /* ---- decoder glue (model.py:845-905) ---------------------------------------- */
 /* y = rms_norm(x) * w (nn.RMSNorm, model.py:850-851, 864). */
@@ -315,6 +357,9 @@ MOTIF_API int motif_embed_rms_norm(int dtype, const int32_t* token_dev, const vo
 /* Greedy sampler: first index of the maximum of logits (n,) -> *out_index
  * (argmax at temperature 0 in mlx_lm generate_step). */
 MOTIF_API size_t motif_argmax_workspace_bytes(int64_t n);
+/* Token (and optional pos_len int32[2] += 1) from a key of argmax_key_out,
+ * after the shards' keys were combined with an int64 MAX all-reduce. */
+MOTIF_API int motif_argmax_key_decode(const int64_t* key, int32_t* token, int32_t* pos_len_inc, void* stream);
 MOTIF_API int motif_argmax(int dtype, const void* logits, int64_t n, int32_t* out_index, void* workspace,
                  size_t workspace_bytes, void* stream);
 

@@ -259,6 +259,17 @@ __global__ void argmax_final_kernel(const Best* __restrict__ part, int nparts,
   if (threadIdx.x == 0) out[0] = best.i == 0x7fffffff ? 0 : best.i;
 }
 
+// Token from a combined argmax key (see argmax_key_out of motif_linear_fused).
+__global__ void argmax_key_decode_kernel(const long long* __restrict__ key, int32_t* __restrict__ token,
+                                         int32_t* __restrict__ pos_len) {
+  const unsigned long long k = (unsigned long long)key[0] ^ 0x8000000000000000ull;
+  token[0] = k == 0 ? 0 : (int32_t)(0xFFFFFFFFu - (uint32_t)(k & 0xFFFFFFFFull));
+  if (pos_len) {
+    pos_len[0] += 1;
+    pos_len[1] += 1;
+  }
+}
+
 constexpr int kArgmaxThreads = 256;
 int argmax_parts(int64_t n) {
   int64_t p = ceil_div(n, kArgmaxThreads * 8);
@@ -376,6 +387,12 @@ int motif_gda_post(int dtype, const void* merged, const void* subln_w, const flo
 }
 
 size_t motif_argmax_workspace_bytes(int64_t n) { return sizeof(Best) * (size_t)argmax_parts(n); }
+
+int motif_argmax_key_decode(const int64_t* key, int32_t* token, int32_t* pos_len_inc, void* stream) {
+  MOTIF_REQUIRE(key && token, MOTIF_ERR_NULL, "argmax_key_decode: null pointer");
+  argmax_key_decode_kernel<<<1, 1, 0, as_stream(stream)>>>(reinterpret_cast<const long long*>(key), token, pos_len_inc);
+  return check_launch("argmax_key_decode");
+}
 
 int motif_argmax(int dtype, const void* logits, int64_t n, int32_t* out_index, void* workspace,
                  size_t workspace_bytes, void* stream) {

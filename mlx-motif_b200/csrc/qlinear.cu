@@ -145,7 +145,50 @@ struct LinArgs {
   int* amax_tiles;               // finished tiles, 0 between calls
   int32_t* argmax_out;
   int32_t* pos_len_inc;
+  long long* argmax_key_out;
+  int64_t argmax_row_offset;
+  // tensor-parallel exchange over peer memory (tp_world 0: none); values travel as
+  // (fp32 bits, number) pairs, one 8-byte store each
+  int tp_world;
+  const int* tp_seq;
+  int tp_tag;
+  long long* tp_out[8];
+  long long* tp_stats[8];
+  const long long* tp_in;
+  const long long* tp_stats_in;
 };
+
+constexpr unsigned long long kTpWaitNs = 2000ull * 1000 * 1000;  // exchange wait limit (2 s)
+
+__device__ __forceinline__ unsigned long long global_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+__device__ __forceinline__ int tp_number(const LinArgs& a) { return (*a.tp_seq + 1) * 1024 + a.tp_tag; }
+
+__device__ __forceinline__ long long tp_pair(float v, int number) {
+  return (long long)(((unsigned long long)(uint32_t)number << 32) | __float_as_uint(v));
+}
+
+// Read an exchanged pair written by some rank (L2, so a peer's store is seen), re-reading
+// until it carries `number`; on time-out it records the error and returns what is there.
+__device__ __forceinline__ float tp_read(const long long* p, int number, int* err) {
+  long long x = __ldcg(p);
+  if ((int)(x >> 32) != number) {
+    const unsigned long long t0 = global_ns();
+    do {
+      __nanosleep(32);
+      x = __ldcg(p);
+      if (global_ns() - t0 > kTpWaitNs) {
+        if (err) atomicExch(err, 2);
+        break;
+      }
+    } while ((int)(x >> 32) != number);
+  }
+  return __uint_as_float((uint32_t)x);
+}
 
 struct UnitRegs {
   uint4 wr[4];
@@ -293,20 +336,36 @@ __device__ void tile_epilogue(const LinArgs& a, int tile, int gw, float acc_r, f
   }
   const int64_t row = row0 + lane;
   const __half hv = __float2half_rn(v);
-  if (have && row < a.N) a.y[row] = hv;
+  if (have && row < a.N) {
+    a.y[row] = hv;
+    if (a.tp_world && a.tp_out[0]) {  // this rank's fp32 rows into every rank's exchange buffer
+      const long long pr = tp_pair(v, tp_number(a));
+      for (int r = 0; r < a.tp_world; ++r) a.tp_out[r][row] = pr;
+    }
+  }
   // all-or-nothing per warp: `have` is uniform across lanes 0..15 of the finishing warp
   const bool any = __any_sync(0xffffffffu, have);
-  if (any && a.stats_out && row0 < a.stats_rows) {
+  if (any && (a.stats_out || (a.tp_world && a.tp_stats[0])) && row0 < a.stats_rows) {
     const float f = (have && row < a.stats_rows) ? __half2float(hv) : 0.f;
     const float f2 = f * f, f4 = f2 * f2;
     float s2 = warp_sum(f2), s4 = warp_sum(f4), s6 = warp_sum(f4 * f2);
     if (lane == 0) {
-      a.stats_out[tile * 3 + 0] = s2;
-      a.stats_out[tile * 3 + 1] = s4;
-      a.stats_out[tile * 3 + 2] = s6;
+      if (a.stats_out) {
+        a.stats_out[tile * 3 + 0] = s2;
+        a.stats_out[tile * 3 + 1] = s4;
+        a.stats_out[tile * 3 + 2] = s6;
+      }
+      if (a.tp_world && a.tp_stats[0]) {
+        const int num = tp_number(a);
+        for (int r = 0; r < a.tp_world; ++r) {
+          a.tp_stats[r][tile * 3 + 0] = tp_pair(s2, num);
+          a.tp_stats[r][tile * 3 + 1] = tp_pair(s4, num);
+          a.tp_stats[r][tile * 3 + 2] = tp_pair(s6, num);
+        }
+      }
     }
   }
-  if (a.argmax_out && any) {
+  if ((a.argmax_out || a.argmax_key_out) && any) {
     // Key of this lane's row: value bits mapped to an unsigned order (NaN as -inf) above the
     // inverted row index, so the largest key is the largest value at its first index.
     unsigned long long key = 0;
@@ -315,7 +374,7 @@ __device__ void tile_epilogue(const LinArgs& a, int tile, int gw, float acc_r, f
       if (isnan(f)) f = -INFINITY;
       const uint32_t b = __float_as_uint(f);
       const uint32_t hi = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
-      key = ((unsigned long long)hi << 32) | (0xFFFFFFFFu - (uint32_t)row);
+      key = ((unsigned long long)hi << 32) | (0xFFFFFFFFu - (uint32_t)(row + a.argmax_row_offset));
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
@@ -330,7 +389,8 @@ __device__ void tile_epilogue(const LinArgs& a, int tile, int gw, float acc_r, f
         __threadfence();
         const unsigned long long k = atomicExch(a.amax_key, 0ull);
         atomicExch(a.amax_tiles, 0);
-        a.argmax_out[0] = k == 0 ? 0 : (int32_t)(0xFFFFFFFFu - (uint32_t)(k & 0xFFFFFFFFull));
+        if (a.argmax_key_out) *a.argmax_key_out = (long long)(k ^ 0x8000000000000000ull);
+        if (a.argmax_out) a.argmax_out[0] = k == 0 ? 0 : (int32_t)(0xFFFFFFFFu - (uint32_t)(k & 0xFFFFFFFFull));
         if (a.pos_len_inc) {
           a.pos_len_inc[0] += 1;
           a.pos_len_inc[1] += 1;
@@ -359,13 +419,31 @@ struct StageWords {
 // `after_issue` runs on every thread once the input loads are in flight (the TMA
 // kernel issues the rest of its weight prefetch there, behind the staging loads).
 template <int MODE, bool V2, typename AfterIssue>
-__device__ void stage_x(const LinArgs& a, __half* xp_s, float* xsum_s, float* corr_s, float* red,
+__device__ void stage_x(const LinArgs& a, __half* xp_s, float* xsum_s, float* corr_s, float* red, __half* delta_s,
                         AfterIssue&& after_issue) {
   constexpr int kMaxStageWords = StageWords<MODE>::value;
   const int64_t K = a.K;
   const int words = (int)(K / 8);
   const int nthr = blockDim.x;
   const int tid = threadIdx.x;
+  const __half* delta = a.delta;
+  if (MODE == kModeAddRms && a.tp_in) {
+    // Tensor-parallel consumer: delta = fp16(Σ_r partial_r) over the ranks' exchanged rows,
+    // summed in rank order so every rank gets the same bits.
+    const int num = tp_number(a);
+    for (int w = tid; w < words; w += nthr) {
+      float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll 4
+      for (int r = 0; r < a.tp_world; ++r) {
+        const long long* p = a.tp_in + (int64_t)r * K + (int64_t)w * 8;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[j] += tp_read(p + j, num, a.err);
+      }
+      store_vec<__half, 8>(delta_s + (int64_t)w * 8, acc);
+    }
+    __syncthreads();
+    delta = delta_s;
+  }
   uint4 in0[kMaxStageWords], in1[kMaxStageWords], in2[kMaxStageWords];
   const __half* hsrc = a.h_in;
   float stats_acc[3] = {0.f, 0.f, 0.f};
@@ -383,7 +461,7 @@ __device__ void stage_x(const LinArgs& a, __half* xp_s, float* xsum_s, float* co
         in0[i] = *reinterpret_cast<const uint4*>(a.x + (int64_t)wi * 8);
       } else if constexpr (MODE == kModeAddRms) {
         in0[i] = *reinterpret_cast<const uint4*>(hsrc + (int64_t)wi * 8);
-        in1[i] = a.delta ? *reinterpret_cast<const uint4*>(a.delta + (int64_t)wi * 8) : make_uint4(0, 0, 0, 0);
+        in1[i] = delta ? *reinterpret_cast<const uint4*>(delta + (int64_t)wi * 8) : make_uint4(0, 0, 0, 0);
         in2[i] = *reinterpret_cast<const uint4*>(a.norm_w + (int64_t)wi * 8);
       } else {
         in0[i] = *reinterpret_cast<const uint4*>(a.gate + (int64_t)wi * 8);
@@ -392,10 +470,19 @@ __device__ void stage_x(const LinArgs& a, __half* xp_s, float* xsum_s, float* co
     }
   }
   if (MODE == kModePoly) {
-    for (int i = tid; i < a.stats_count; i += nthr) {
-      stats_acc[0] += a.stats[i * 3 + 0];
-      stats_acc[1] += a.stats[i * 3 + 1];
-      stats_acc[2] += a.stats[i * 3 + 2];
+    if (a.tp_stats_in) {  // all ranks' tile statistics, exchanged as pairs
+      const int num = tp_number(a);
+      for (int i = tid; i < a.stats_count; i += nthr) {
+        stats_acc[0] += tp_read(a.tp_stats_in + i * 3 + 0, num, a.err);
+        stats_acc[1] += tp_read(a.tp_stats_in + i * 3 + 1, num, a.err);
+        stats_acc[2] += tp_read(a.tp_stats_in + i * 3 + 2, num, a.err);
+      }
+    } else {
+      for (int i = tid; i < a.stats_count; i += nthr) {
+        stats_acc[0] += a.stats[i * 3 + 0];
+        stats_acc[1] += a.stats[i * 3 + 1];
+        stats_acc[2] += a.stats[i * 3 + 2];
+      }
     }
   }
   after_issue();
@@ -410,7 +497,7 @@ __device__ void stage_x(const LinArgs& a, __half* xp_s, float* xsum_s, float* co
         const __half* dv = reinterpret_cast<const __half*>(&in1[i]);
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
-          const float v = a.delta ? round_through<__half>(__half2float(hv[j]) + __half2float(dv[j])) : __half2float(hv[j]);
+          const float v = delta ? round_through<__half>(__half2float(hv[j]) + __half2float(dv[j])) : __half2float(hv[j]);
           acc[0] += v * v;
         }
       }
@@ -446,7 +533,7 @@ __device__ void stage_x(const LinArgs& a, __half* xp_s, float* xsum_s, float* co
         float v[8];
 #pragma unroll
         for (int j = 0; j < 8; ++j)
-          v[j] = a.delta ? round_through<__half>(__half2float(e0[j]) + __half2float(e1[j])) : __half2float(e0[j]);
+          v[j] = delta ? round_through<__half>(__half2float(e0[j]) + __half2float(e1[j])) : __half2float(e0[j]);
         if (write_h) store_vec<__half, 8>(a.h_out + (int64_t)wi * 8, v);
 #pragma unroll
         for (int j = 0; j < 8; ++j) h[j] = __float2half_rn(v[j] * inv * __half2float(e2[j]));
@@ -511,6 +598,7 @@ __global__ void __launch_bounds__(kThreads, 2) q4_gemv_kernel(LinArgs a) {
   __half* xp_s = reinterpret_cast<__half*>(smem_raw);
   float* xsum_s = reinterpret_cast<float*>(smem_raw + (size_t)a.K * sizeof(__half));
   float* red = xsum_s + a.K / 64;
+  __half* delta_s = reinterpret_cast<__half*>(red + 32 * 3);  // K halves when a.tp_in is set
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int r = lane >> 2, c = lane & 3;
@@ -528,7 +616,7 @@ __global__ void __launch_bounds__(kThreads, 2) q4_gemv_kernel(LinArgs a) {
   if (u0 < u1) load_unit(A, a, tile, blk, r, c);
   grid_dep_wait();
   grid_dep_launch();
-  stage_x<MODE, false>(a, xp_s, xsum_s, nullptr, red, [] {});
+  stage_x<MODE, false>(a, xp_s, xsum_s, nullptr, red, delta_s, [] {});
 
   float acc_r = 0.f, acc_r8 = 0.f;
   for (int u = u0; u < u1; u += 2) {
@@ -725,6 +813,7 @@ __global__ void __launch_bounds__(kTmaThreads, kTmaMinBlocks) q4_gemv_tma_kernel
   float* xsum_s = reinterpret_cast<float*>(zero_s + kZeroBytes);
   float* corr_s = xsum_s + a.K / 64;
   float* red = corr_s + a.K / 64;
+  __half* delta_s = reinterpret_cast<__half*>(red + 32 * 3);  // K halves when a.tp_in is set
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int r = lane >> 2, c = lane & 3;
@@ -758,7 +847,7 @@ __global__ void __launch_bounds__(kTmaThreads, kTmaMinBlocks) q4_gemv_tma_kernel
   for (int i = threadIdx.x; i < kZeroBytes / 16; i += blockDim.x) reinterpret_cast<uint4*>(zero_s)[i] = make_uint4(0, 0, 0, 0);
   grid_dep_wait();
   grid_dep_launch();
-  stage_x<MODE, true>(a, xp_s, xsum_s, corr_s, red, [&] {
+  stage_x<MODE, true>(a, xp_s, xsum_s, corr_s, red, delta_s, [&] {
     if (lane == 0) {
       for (int i = 1; i < kStages && u0 + i < u1; ++i) {
         issue_unit(a, it, ib, smem_u32(my_ring + i * kSlotBytes), smem_u32(&my_bars[i]));
@@ -921,14 +1010,15 @@ bool encode_rows(CUtensorMap* m, const void* base, uint64_t inner_bytes, uint64_
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-size_t tma_smem_bytes(int64_t K) {
+size_t tma_smem_bytes(int64_t K, bool tp_in = false) {
   return (size_t)kTmaWarps * kStages * kSlotBytes + (size_t)kTmaWarps * kStages * 8 +
-         (size_t)(K / 64) * kXGroupBytes + 64 + kZeroBytes + 2 * (size_t)(K / 64) * 4 + 32 * 3 * 4;
+         (size_t)(K / 64) * kXGroupBytes + 64 + kZeroBytes + 2 * (size_t)(K / 64) * 4 + 32 * 3 * 4 +
+         (tp_in ? (size_t)K * 2 : 0);
 }
 
 // The TMA kernel needs K % 512 == 0 and 16-byte aligned rows of codes (K/2 bytes) and scales (K/32 bytes).
 bool try_tma(LinArgs& a) {
-  if (a.K % 512 || tma_smem_bytes(a.K) > (size_t)kTmaSmemCap) return false;
+  if (a.K % 512 || tma_smem_bytes(a.K, a.tp_in != nullptr) > (size_t)kTmaSmemCap) return false;
   if ((reinterpret_cast<uintptr_t>(a.w) | reinterpret_cast<uintptr_t>(a.sc) | reinterpret_cast<uintptr_t>(a.bi)) % 16)
     return false;
   return encode_rows(&a.tm_w, a.w, (uint64_t)a.K / 2, (uint64_t)a.N, 128, kTileRows, CU_TENSOR_MAP_SWIZZLE_128B) &&
@@ -972,7 +1062,7 @@ int launch_q4(LinArgs& a, void* workspace, size_t ws_bytes, cudaStream_t st) {
     a.counters = nullptr;
     a.partial = nullptr;
   }
-  if (a.argmax_out) {  // the argmax state lives in the workspace's control words
+  if (a.argmax_out || a.argmax_key_out) {  // the argmax state lives in the workspace's control words
     if (!workspace || ws_bytes < kCounterBytes)
       return fail(MOTIF_ERR_WORKSPACE, "linear_fused: argmax needs a workspace of >= %zu bytes", kCounterBytes);
     int* ctl = static_cast<int*>(workspace);
@@ -993,11 +1083,18 @@ int launch_q4(LinArgs& a, void* workspace, size_t ws_bytes, cudaStream_t st) {
   if (a.K > max_k)
     return fail(MOTIF_ERR_BAD_SHAPE, "quantized_linear: K=%lld exceeds %lld for prologue mode %d", (long long)a.K,
                 (long long)max_k, a.mode);
-  if (!tma && p.smem > 160 * 1024) return fail(MOTIF_ERR_BAD_SHAPE, "quantized_linear: K=%lld too large", (long long)a.K);
+  if (!tma && p.smem + (a.tp_in ? (size_t)a.K * 2 : 0) > 160 * 1024)
+    return fail(MOTIF_ERR_BAD_SHAPE, "quantized_linear: K=%lld too large", (long long)a.K);
+  if (a.tp_world) {  // the exchange waits report through the workspace's error word
+    if (!workspace || ws_bytes < kCounterBytes)
+      return fail(MOTIF_ERR_WORKSPACE, "linear_fused: tensor-parallel exchange needs a workspace of >= %zu bytes",
+                  kCounterBytes);
+    a.err = static_cast<int*>(workspace) + kErrSlot;
+  }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(p.ctas);
   cfg.blockDim = dim3(tma ? kTmaThreads : kThreads);
-  cfg.dynamicSmemBytes = tma ? tma_smem_bytes(a.K) : p.smem;
+  cfg.dynamicSmemBytes = tma ? tma_smem_bytes(a.K, a.tp_in != nullptr) : p.smem + (a.tp_in ? (size_t)a.K * 2 : 0);
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -1126,8 +1223,36 @@ int motif_linear_fused(const motif_linear_io* io, const uint32_t* w, const void*
       return fail(MOTIF_ERR_BAD_SHAPE, "linear_fused: mode %d not in {0,1,2}", io->mode);
   }
   MOTIF_REQUIRE(!io->pos_len_inc || io->argmax_out, MOTIF_ERR_BAD_CONTRACT, "linear_fused: pos_len_inc needs argmax_out");
+  MOTIF_REQUIRE(io->argmax_row_offset >= 0 && io->argmax_row_offset + n <= 0xFFFFFFFFll, MOTIF_ERR_BAD_SHAPE,
+                "linear_fused: argmax rows must fit 32 bits");
   a.argmax_out = io->argmax_out;
   a.pos_len_inc = io->pos_len_inc;
+  a.argmax_key_out = reinterpret_cast<long long*>(io->argmax_key_out);
+  a.argmax_row_offset = io->argmax_row_offset;
+  if (io->tp_world) {
+    MOTIF_REQUIRE(io->tp_world >= 1 && io->tp_world <= 8 && io->tp_seq && io->tp_tag >= 0 && io->tp_tag < 1024,
+                  MOTIF_ERR_BAD_CONTRACT, "linear_fused: tp_world %d (1..8) needs tp_seq, tp_tag %d (0..1023)",
+                  io->tp_world, io->tp_tag);
+    MOTIF_REQUIRE(!io->tp_in || io->mode == kModeAddRms, MOTIF_ERR_BAD_CONTRACT, "linear_fused: tp_in needs mode 1");
+    MOTIF_REQUIRE(!io->tp_in || !io->delta, MOTIF_ERR_BAD_CONTRACT, "linear_fused: tp_in replaces delta");
+    MOTIF_REQUIRE(!io->tp_stats_in || io->mode == kModePoly, MOTIF_ERR_BAD_CONTRACT,
+                  "linear_fused: tp_stats_in needs mode 2");
+    MOTIF_REQUIRE(!io->tp_stats[0] || (io->stats_rows > 0 && io->stats_rows % kTileRows == 0 && io->stats_rows <= n),
+                  MOTIF_ERR_BAD_SHAPE, "linear_fused: tp_stats needs stats_rows");
+    for (int r = 0; r < io->tp_world; ++r)
+      MOTIF_REQUIRE((!io->tp_out[0] || io->tp_out[r]) && (!io->tp_stats[0] || io->tp_stats[r]), MOTIF_ERR_NULL,
+                    "linear_fused: tp_out/tp_stats of rank %d", r);
+    a.tp_world = io->tp_world;
+    a.tp_seq = io->tp_seq;
+    a.tp_tag = io->tp_tag;
+    for (int r = 0; r < 8; ++r) {
+      a.tp_out[r] = reinterpret_cast<long long*>(io->tp_out[r]);
+      a.tp_stats[r] = reinterpret_cast<long long*>(io->tp_stats[r]);
+    }
+    a.tp_in = reinterpret_cast<const long long*>(io->tp_in);
+    a.tp_stats_in = reinterpret_cast<const long long*>(io->tp_stats_in);
+    if (io->tp_stats[0] && !io->stats_out) a.stats_rows = io->stats_rows;
+  }
   if (io->stats_out) {
     MOTIF_REQUIRE(io->stats_rows > 0 && io->stats_rows % kTileRows == 0 && io->stats_rows <= n, MOTIF_ERR_BAD_SHAPE,
                   "linear_fused: stats_rows must be a positive multiple of 16 and <= n");

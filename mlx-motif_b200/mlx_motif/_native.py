@@ -64,6 +64,15 @@ class motif_linear_io(C.Structure):  # noqa: N801 — mirrors the C struct name
         ("stats_rows", C.c_int64),
         ("argmax_out", C.c_void_p),
         ("pos_len_inc", C.c_void_p),
+        ("argmax_key_out", C.c_void_p),
+        ("argmax_row_offset", C.c_int64),
+        ("tp_world", C.c_int32),
+        ("tp_seq", C.c_void_p),
+        ("tp_tag", C.c_int32),
+        ("tp_out", C.c_void_p * 8),
+        ("tp_stats", C.c_void_p * 8),
+        ("tp_in", C.c_void_p),
+        ("tp_stats_in", C.c_void_p),
     ]
 
 
@@ -112,6 +121,13 @@ SIGNATURES = {
     "motif_embed_rms_norm": (_I, [_I, _P, _P, _L, _L, _P, _F, _P, _P, _P]),
     "motif_argmax_workspace_bytes": (_S, [_L]),
     "motif_argmax": (_I, [_I, _P, _L, _P, _P, _S, _P]),
+    "motif_argmax_key_decode": (_I, [_P, _P, _P, _P]),
+    "motif_ipc_handle_bytes": (_S, []),
+    "motif_ipc_alloc": (_I, [_S, C.POINTER(C.c_void_p), _P]),
+    "motif_ipc_open": (_I, [_P, C.POINTER(C.c_void_p)]),
+    "motif_ipc_close": (_I, [_P]),
+    "motif_ipc_zero": (_I, [_P, _S, _P]),
+    "motif_ipc_free": (_I, [_P]),
 }
 
 

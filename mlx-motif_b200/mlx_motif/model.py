@@ -211,7 +211,9 @@ def tp_shard_plan(args: ModelArgs, rank: int, world: int) -> dict:
     head and its kv head of every slot stay on one rank, so attention and
     gda_post need no exchange); o_proj keeps the matching input columns;
     gate/up keep rows [r·I/w, (r+1)·I/w) and down the matching columns. The
-    two row-parallel outputs (o_proj, down_proj) are summed across ranks.
+    two row-parallel outputs (o_proj, down_proj) are summed across ranks. The
+    lm_head keeps vocabulary rows [r·V/w, (r+1)·V/w); the greedy token is the
+    largest of the ranks' packed argmax keys (one int64 MAX all-reduce).
     """
     G, gr, d, Hk, I = args.num_noise_heads, args.grouped_ratio, args.d, args.k_noise_heads, args.intermediate_size
     if G % world or Hk % world or I % world or G != Hk:
@@ -224,10 +226,15 @@ def tp_shard_plan(args: ModelArgs, rank: int, world: int) -> dict:
         G * (gr + 1) * d + torch.arange(2 * rank * kpr * d, 2 * (rank + 1) * kpr * d),  # (k1,k2) pairs
         G * (gr + 1) * d + 2 * Hk * d + torch.arange(2 * rank * kpr * d, 2 * (rank + 1) * kpr * d),  # (v1,v2)
     ])
+    V = args.vocab_size
+    if V % world:
+        raise ValueError(f"TP {world}: vocab {V} must split evenly")
+    vpr = V // world
     return dict(
         qkv_rows=qkv_rows,
         o_cols=(rank * gpr * gr * 2 * d, (rank + 1) * gpr * gr * 2 * d),
         mlp_rows=(rank * ipr, (rank + 1) * ipr),
+        vocab_rows=(rank * vpr, (rank + 1) * vpr),
     )
 
 
@@ -292,6 +299,12 @@ class MotifDecoder:
         self.embed = _t(weights["embed"], dev, torch.float16)
         self.final_norm = _t(weights["final_norm"], dev, torch.float16)
         self.lm_head = weights["lm_head"] if isinstance(weights["lm_head"], QuantizedLinear) else _ql(weights["lm_head"], dev)
+        # Under TP the lm_head is this rank's vocabulary shard, rows [v0, v0 + V_local).
+        self.V_local = self.lm_head.out_dim
+        rank = 0 if tp_group is None else torch.distributed.get_rank(tp_group)
+        self.v0 = rank * self.V_local
+        if self.V_local * self.tp != a.vocab_size:
+            raise ValueError(f"lm_head rows {self.V_local} x TP {self.tp} != vocab {a.vocab_size}")
         self.layers = []
         for L in weights["layers"]:
             if "gate_up" in L:
@@ -345,7 +358,8 @@ class MotifDecoder:
         self.stats_tiles = self.inter // 16
         self.stats = torch.zeros(self.stats_tiles * 3, dtype=torch.float32, device=dev)
         self.stats_sum = torch.zeros(3, dtype=torch.float32, device=dev)
-        self.logits = torch.zeros(self.V, dtype=f16, device=dev)
+        self.logits = torch.zeros(self.V_local, dtype=f16, device=dev)
+        self.amax_key = torch.zeros(1, dtype=torch.int64, device=dev)  # TP: this rank's argmax key
         self.token = torch.zeros(1, dtype=torch.int32, device=dev)
         # pos_len[0] = position of the token being decoded, pos_len[1] = kv_len after its append.
         self.pos_len = torch.tensor([0, 1], dtype=torch.int32, device=dev)
@@ -354,7 +368,7 @@ class MotifDecoder:
         self.scale = d ** -0.5
         lin_ws = max(lib.motif_linear_fused_workspace_bytes(ql.out_dim, ql.in_dim)
                      for L in self.layers for ql in (L["qkv"], L["o"], L["gate_up"], L["down"]))
-        lin_ws = max(lin_ws, lib.motif_linear_fused_workspace_bytes(self.V, H))
+        lin_ws = max(lin_ws, lib.motif_linear_fused_workspace_bytes(self.V_local, H))
         if self.inter % 16:
             raise ValueError("intermediate size per rank must be a multiple of 16")
         self.lin_ws = torch.zeros(max(lin_ws, 16), dtype=torch.uint8, device=dev)
@@ -365,12 +379,18 @@ class MotifDecoder:
         else:
             self.attn_ws_bytes = lib.motif_gda_decode_attention_workspace_bytes(self.q_heads, d, 64)
         self.attn_ws = torch.zeros(self.attn_ws_bytes, dtype=torch.uint8, device=dev)
-        self.argmax_ws_bytes = lib.motif_argmax_workspace_bytes(self.V)
+        self.argmax_ws_bytes = lib.motif_argmax_workspace_bytes(self.V_local)
         self.argmax_ws = torch.zeros(self.argmax_ws_bytes, dtype=torch.uint8, device=dev)
         self.offset = 0  # host mirror of pos_len[0]
         self._graphs: dict[bool, torch.cuda.CUDAGraph] = {}
         self.pinned_in = torch.zeros(1, dtype=torch.int32).pin_memory()
         self.pinned_out = torch.zeros(1, dtype=torch.int32).pin_memory()
+        # Tensor parallelism exchanges the row-parallel outputs and the PolyNorm statistics through
+        # peer memory inside the GEMVs (MOTIF_TP_NCCL=1: NCCL all-reduces instead).
+        self.tp_exchange = self.tp_group is not None and os.environ.get("MOTIF_TP_NCCL", "0") != "1"
+        self._xbuf = None
+        if self.tp_exchange:
+            self._setup_exchange()
 
     # ------------------------------------------------------------------ #
     def _check_shapes(self) -> None:
@@ -404,6 +424,82 @@ class MotifDecoder:
         return len(self.layers) * 4 * self.kv_heads * kv_len * per_row
 
     # ------------------------------------------------------------------ #
+    def _setup_exchange(self) -> None:
+        """One peer-visible buffer per rank (CUDA IPC) holding, for the two layer parities, every
+        rank's o_proj and down_proj partial rows and PolyNorm tile statistics, each value as an
+        8-byte (fp32, exchange number) pair. Ranks trade the IPC handles over the process group
+        and open each other's buffers."""
+        import ctypes as C
+
+        W, H = self.tp, self.H
+        me = torch.distributed.get_rank(self.tp_group)
+        ntl = self.inter // 16
+        part = W * H * 8
+        off = dict(o=0, dn=2 * part, st=4 * part)
+        total = off["st"] + 2 * W * ntl * 3 * 8
+        ptr = C.c_void_p()
+        handle = (C.c_char * lib.motif_ipc_handle_bytes())()
+        check(lib.motif_ipc_alloc(total, C.byref(ptr), handle), "ipc_alloc")
+        handles = [None] * W
+        torch.distributed.all_gather_object(handles, bytes(handle), group=self.tp_group)
+        peers = []
+        for r in range(W):
+            if r == me:
+                peers.append(ptr.value)
+            else:
+                q = C.c_void_p()
+                check(lib.motif_ipc_open(handles[r], C.byref(q)), "ipc_open")
+                peers.append(q.value)
+        self._xbuf, self._xpeers, self._xoff, self._xme, self._xntl = ptr.value, peers, off, me, ntl
+        self._xbytes = total
+
+    def _x_slot(self, kind: str, par: int, src: int) -> int:
+        """Byte offset of source rank src's slot of exchange `kind` ("o", "dn", "st") at parity par."""
+        W, H = self.tp, self.H
+        if kind == "st":
+            return self._xoff["st"] + (par * W + src) * self._xntl * 3 * 8
+        return self._xoff[kind] + (par * W + src) * H * 8
+
+    def _x_producer(self, io, out: str, layer: int) -> None:
+        """io stores its rows (out "o"/"dn") or tile statistics ("st") of `layer` into every rank."""
+        io.tp_world, io.tp_seq, io.tp_tag = self.tp, self.pos_len.data_ptr(), layer
+        for r, base in enumerate(self._xpeers):
+            if out == "st":
+                io.tp_stats[r] = base + self._x_slot("st", layer & 1, self._xme)
+            else:
+                io.tp_out[r] = base + self._x_slot(out, layer & 1, self._xme)
+
+    def _x_consumer(self, io, layer: int, kind: str) -> None:
+        """io reads exchange `kind` of `layer`: the ranks' rows ("o"/"dn": its residual delta is their
+        sum) or tile statistics ("st")."""
+        io.tp_world, io.tp_seq, io.tp_tag = self.tp, self.pos_len.data_ptr(), layer
+        if kind == "st":
+            io.tp_stats_in = self._xbuf + self._x_slot("st", layer & 1, 0)
+        else:
+            io.tp_in = self._xbuf + self._x_slot(kind, layer & 1, 0)
+
+    def _tp_reset_flags(self) -> None:
+        """After the position is rewound every rank zeroes its exchange buffer between two
+        barriers, so no pair can still carry the number of a step that is about to run again."""
+        if not self.tp_exchange:
+            return
+        torch.cuda.synchronize(self.device)
+        torch.distributed.barrier(group=self.tp_group)
+        check(lib.motif_ipc_zero(self._xbuf, self._xbytes, stream(self.device)), "ipc_zero")
+        torch.cuda.synchronize(self.device)
+        torch.distributed.barrier(group=self.tp_group)
+
+    def release_exchange(self) -> None:
+        """Close the peers' buffers and free this rank's (call on every rank, after a barrier)."""
+        if self._xbuf is None:
+            return
+        torch.cuda.synchronize(self.device)
+        for r, base in enumerate(self._xpeers):
+            if r != self._xme:
+                check(lib.motif_ipc_close(base), "ipc_close")
+        check(lib.motif_ipc_free(self._xbuf), "ipc_free")
+        self._xbuf = None
+
     def _allreduce(self, t: torch.Tensor) -> None:
         if self.tp_group is not None:
             torch.distributed.all_reduce(t, group=self.tp_group)
@@ -421,27 +517,53 @@ class MotifDecoder:
         I = self.inter
         gp = self.gu.data_ptr()
         tp = self.tp_group is not None
+        X = self.tp_exchange
         plan = []
         for li, L in enumerate(self.layers):
             if li == 0:
                 qkv_io = self._io(1, token=ptr(self.token), embed=ptr(self.embed), vocab=self.V,
                                   h_out=ptr(self.h_b), norm_w=ptr(L["input_norm"]), eps=eps)
+            elif X:  # residual delta = the ranks' down_proj partials of the previous layer
+                qkv_io = self._io(1, h_in=ptr(self.h_a), h_out=ptr(self.h_b), norm_w=ptr(L["input_norm"]), eps=eps)
+                self._x_consumer(qkv_io, li - 1, "dn")
             else:
                 qkv_io = self._io(1, h_in=ptr(self.h_a), delta=ptr(self.dn), h_out=ptr(self.h_b),
                                   norm_w=ptr(L["input_norm"]), eps=eps)
             o_io = self._io(0, x=ptr(self.attn))
-            gu_io = self._io(1, h_in=ptr(self.h_b), delta=ptr(self.o), h_out=ptr(self.h_a),
-                             norm_w=ptr(L["post_norm"]), eps=eps, stats_out=ptr(self.stats), stats_rows=I)
-            stats_src, stats_n = (self.stats_sum, 1) if tp else (self.stats, self.stats_tiles)
-            dn_io = self._io(2, gate=gp, up=gp + 2 * I, stats=ptr(stats_src), stats_count=stats_n,
-                             poly_w=ptr(L["polynorm_w"]), poly_b=ptr(L["polynorm_b"]), poly_eps=1e-6,
-                             poly_dim=self.args.intermediate_size)
+            if X:
+                self._x_producer(o_io, "o", li)
+                gu_io = self._io(1, h_in=ptr(self.h_b), h_out=ptr(self.h_a), norm_w=ptr(L["post_norm"]), eps=eps,
+                                 stats_rows=I)
+                self._x_consumer(gu_io, li, "o")
+                self._x_producer(gu_io, "st", li)
+                dn_io = self._io(2, gate=gp, up=gp + 2 * I, stats=ptr(self.stats), stats_count=self.tp * self._xntl,
+                                 poly_w=ptr(L["polynorm_w"]), poly_b=ptr(L["polynorm_b"]), poly_eps=1e-6,
+                                 poly_dim=self.args.intermediate_size)
+                self._x_consumer(dn_io, li, "st")
+                self._x_producer(dn_io, "dn", li)
+            else:
+                gu_io = self._io(1, h_in=ptr(self.h_b), delta=ptr(self.o), h_out=ptr(self.h_a),
+                                 norm_w=ptr(L["post_norm"]), eps=eps, stats_out=ptr(self.stats), stats_rows=I)
+                stats_src, stats_n = (self.stats_sum, 1) if tp else (self.stats, self.stats_tiles)
+                dn_io = self._io(2, gate=gp, up=gp + 2 * I, stats=ptr(stats_src), stats_count=stats_n,
+                                 poly_w=ptr(L["polynorm_w"]), poly_b=ptr(L["polynorm_b"]), poly_eps=1e-6,
+                                 poly_dim=self.args.intermediate_size)
             plan.append((qkv_io, o_io, gu_io, dn_io))
         # The lm_head GEMV also picks the greedy token and advances pos_len (MOTIF_FUSED_ARGMAX=0: separate
         # argmax launches).
-        self.fused_argmax = os.environ.get("MOTIF_FUSED_ARGMAX", "1") != "0"
-        extra = dict(argmax_out=ptr(self.token), pos_len_inc=ptr(self.pos_len)) if self.fused_argmax else {}
-        head_io = self._io(1, h_in=ptr(self.h_a), delta=ptr(self.dn), norm_w=ptr(self.final_norm), eps=eps, **extra)
+        self.fused_argmax = tp or os.environ.get("MOTIF_FUSED_ARGMAX", "1") != "0"
+        if tp:  # this rank's key; the ranks' keys are combined by an all-reduce
+            extra = dict(argmax_key_out=ptr(self.amax_key), argmax_row_offset=self.v0)
+        elif self.fused_argmax:
+            extra = dict(argmax_out=ptr(self.token), pos_len_inc=ptr(self.pos_len))
+        else:
+            extra = {}
+        if X:
+            head_io = self._io(1, h_in=ptr(self.h_a), norm_w=ptr(self.final_norm), eps=eps, **extra)
+            self._x_consumer(head_io, len(self.layers) - 1, "dn")
+        else:
+            head_io = self._io(1, h_in=ptr(self.h_a), delta=ptr(self.dn), norm_w=ptr(self.final_norm), eps=eps,
+                               **extra)
         self._plan = (plan, head_io)
 
     def _linear(self, io, ql: QuantizedLinear, out: torch.Tensor, st: int) -> None:
@@ -482,23 +604,30 @@ class MotifDecoder:
                                                      self.args.attn_rms_norm_eps, ptr(self.attn), ptr(self.attn_ws),
                                                      self.attn_ws_bytes, st), "gda_decode_attention")
             self._linear(o_io, L["o"], self.o, st)
-            self._allreduce(self.o)
+            if not self.tp_exchange:
+                self._allreduce(self.o)
             self._linear(gu_io, L["gate_up"], self.gu, st)
-            if tp:
+            if tp and not self.tp_exchange:
                 # Full-row PolyNorm statistics across ranks (12 bytes over NCCL).
                 torch.sum(self.stats.view(-1, 3), dim=0, out=self.stats_sum)
                 self._allreduce(self.stats_sum)
             self._linear(dn_io, L["down"], self.dn, st)
-            self._allreduce(self.dn)
+            if not self.tp_exchange:
+                self._allreduce(self.dn)
         self._head(with_head, head_io, st)
 
     def _head(self, with_head: bool, head_io, st: int) -> None:
         """lm_head + greedy token + position advance (one launch when the argmax is fused)."""
         if with_head:
             self._linear(head_io, self.lm_head, self.logits, st)
+            if self.tp_group is not None:
+                torch.distributed.all_reduce(self.amax_key, op=torch.distributed.ReduceOp.MAX, group=self.tp_group)
+                check(lib.motif_argmax_key_decode(ptr(self.amax_key), ptr(self.token), ptr(self.pos_len), st),
+                      "argmax_key_decode")
+                return
             if self.fused_argmax:
                 return  # the GEMV wrote the token and advanced pos_len
-            check(lib.motif_argmax(0, ptr(self.logits), self.V, ptr(self.token), ptr(self.argmax_ws),
+            check(lib.motif_argmax(0, ptr(self.logits), self.V_local, ptr(self.token), ptr(self.argmax_ws),
                                    self.argmax_ws_bytes, st), "argmax")
         self.pos_len.add_(self._one_one)
 
@@ -512,6 +641,7 @@ class MotifDecoder:
             self.pos_len.copy_(saved[0])
             self.token.copy_(saved[1])
             torch.cuda.synchronize(self.device)
+            self._tp_reset_flags()
             g = torch.cuda.CUDAGraph()
             with torch.cuda.graph(g):
                 self._launch_step(with_head)
@@ -523,6 +653,7 @@ class MotifDecoder:
         self.offset = 0
         for c in self.caches:
             c.offset = 0
+        self._tp_reset_flags()
 
     def _bump_host(self, n: int = 1) -> None:
         self.offset += n
@@ -594,6 +725,7 @@ class MotifDecoder:
         self.offset = n
         for c in self.caches:
             c.offset = n
+        self._tp_reset_flags()
 
     # ------------------------------------------------------------------ #
     @classmethod
@@ -646,8 +778,12 @@ class MotifDecoder:
                 polynorm_b=torch.zeros(1, dtype=f16, device=dev),
             ))
             del qkv, o, gate, up, down
-        weights = dict(embed=randn(a.vocab_size, H), final_norm=norm_w(H), lm_head=qlin(randn(a.vocab_size, H)),
-                       layers=layers)
+        embed = randn(a.vocab_size, H)
+        final_norm = norm_w(H)
+        head = randn(a.vocab_size, H)
+        if world > 1:
+            head = head[plan["vocab_rows"][0]:plan["vocab_rows"][1]].contiguous()
+        weights = dict(embed=embed, final_norm=final_norm, lm_head=qlin(head), layers=layers)
         return cls(args, weights, cache=cache, max_seq=max_seq, device=dev, tp_group=tp_group)
 
 

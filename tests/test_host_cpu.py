@@ -73,8 +73,8 @@ def test_lambda_helpers_match_oracle():
 def test_tp_shard_plan_matches_oracle_sharding(world):
     from mlx_motif.model import ModelArgs, tp_shard_plan
 
-    oa = O.OracleArgs(hidden_size=128, num_hidden_layers=1, intermediate_size=512, vocab_size=50)
-    ma = ModelArgs(hidden_size=128, num_hidden_layers=1, intermediate_size=512, vocab_size=50)
+    oa = O.OracleArgs(hidden_size=128, num_hidden_layers=1, intermediate_size=512, vocab_size=64)
+    ma = ModelArgs(hidden_size=128, num_hidden_layers=1, intermediate_size=512, vocab_size=64)
     w = O.make_synthetic_weights(oa, seed=0)
     for rank in range(world):
         sh = O.shard_weights_tp(oa, w, rank, world)["layers"][0]
@@ -86,6 +86,8 @@ def test_tp_shard_plan_matches_oracle_sharding(world):
         r0, r1 = plan["mlp_rows"]
         np.testing.assert_array_equal(L["gate"][0][r0:r1], sh["gate"][0])
         np.testing.assert_array_equal(L["down"][1][:, r0 // 64:r1 // 64], sh["down"][1])
+        v0, v1 = plan["vocab_rows"]
+        assert (v0, v1) == (rank * 64 // world, (rank + 1) * 64 // world)
 
 
 # ---------------------------------------------------------------- gloo TP decode
@@ -169,3 +171,49 @@ def test_tp2_gloo_decode_equals_single_rank():
     for i, tok in enumerate((1, 7, 9)):
         logits, _ = ref.step(tok)
         np.testing.assert_allclose(tp_logits[i].astype(np.float32), logits.astype(np.float32), atol=2e-2, rtol=2e-2)
+
+
+# ---------------------------------------------------------------- vocabulary-parallel argmax
+def _argmax_key(v: np.ndarray, row0: int) -> np.ndarray:
+    """The packed key of the lm_head epilogue (argmax_key_out): order-preserving fp32 bits of the
+    fp16 value (NaN as -inf) above the inverted global row, top bit flipped for int64 order."""
+    f = v.astype(np.float32).copy()
+    f[np.isnan(f)] = -np.inf
+    b = f.view(np.uint32).astype(np.uint64)
+    hi = np.where(b & 0x80000000, ~b & 0xFFFFFFFF, b | 0x80000000)
+    rows = np.arange(row0, row0 + len(v), dtype=np.uint64)
+    key = (hi << np.uint64(32)) | (np.uint64(0xFFFFFFFF) - rows)
+    return (key ^ np.uint64(1 << 63)).view(np.int64)
+
+
+def _key_worker(rank, world, port, logits, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        n = len(logits) // world
+        k = torch.tensor([_argmax_key(logits[rank * n:(rank + 1) * n], rank * n).max()])
+        dist.all_reduce(k, op=dist.ReduceOp.MAX)
+        u = int(k.item()) ^ (1 << 63) if int(k.item()) >= 0 else (int(k.item()) + (1 << 64)) ^ (1 << 63)
+        q.put(0 if u == 0 else 0xFFFFFFFF - (u & 0xFFFFFFFF))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_vocab_parallel_argmax_keys_over_gloo():
+    """Shard keys combined by an int64 MAX all-reduce give the first index of the global maximum,
+    with NaN ranked below everything (ties across shards and inside one shard)."""
+    rng = np.random.default_rng(11)
+    logits = rng.standard_normal(64).astype(np.float16)
+    logits[[9, 40, 41]] = np.float16(3.5)  # tie across shards and within shard 1: index 9 wins
+    logits[[2, 50]] = np.float16("nan")
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = 30500 + (os.getpid() % 500)
+    procs = [ctx.Process(target=_key_worker, args=(r, 2, port, logits, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    toks = [q.get(timeout=120) for _ in procs]
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    assert toks == [9, 9]
