@@ -435,9 +435,16 @@ __device__ void stage_x(const LinArgs& a, __half* xp_s, float* xsum_s, float* co
       float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll 4
       for (int r = 0; r < a.tp_world; ++r) {
+        // 8 pairs = four 16-byte L2 loads; a pair not yet carrying this number is re-read alone
         const long long* p = a.tp_in + (int64_t)r * K + (int64_t)w * 8;
+        int4 q[4];
 #pragma unroll
-        for (int j = 0; j < 8; ++j) acc[j] += tp_read(p + j, num, a.err);
+        for (int j = 0; j < 4; ++j) q[j] = __ldcg(reinterpret_cast<const int4*>(p) + j);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          acc[2 * j] += q[j].y == num ? __int_as_float(q[j].x) : tp_read(p + 2 * j, num, a.err);
+          acc[2 * j + 1] += q[j].w == num ? __int_as_float(q[j].z) : tp_read(p + 2 * j + 1, num, a.err);
+        }
       }
       store_vec<__half, 8>(delta_s + (int64_t)w * 8, acc);
     }

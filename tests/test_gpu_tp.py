@@ -1,7 +1,8 @@
-"""Tensor-parallel decode on 2 GPUs (NCCL): the sharded MotifDecoder (GDA groups, MLP
-columns and the lm_head's vocabulary split over ranks; all-reduces after o_proj, down_proj,
-of the PolyNorm statistics and of the packed argmax keys) produces the same greedy tokens
-as the unsharded model built from the same seed. Skipped with fewer than 2 GPUs."""
+"""Tensor-parallel decode on 2, 4 and 8 GPUs: the sharded MotifDecoder (GDA groups, MLP
+columns and the lm_head's vocabulary split over ranks; the row-parallel outputs and the
+PolyNorm statistics exchanged through peer memory inside the GEMVs, or all-reduced by NCCL;
+the packed argmax keys combined by one all-reduce) produces the same greedy tokens as the
+unsharded model built from the same seed. Each case is skipped without enough GPUs."""
 
 from __future__ import annotations
 
@@ -49,16 +50,17 @@ def _worker(rank, world, port, q, nccl_only=False):
         dist.destroy_process_group()
 
 
-@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-@pytest.mark.parametrize("exchange", ["peer", "nccl"])
-def test_tp2_decode_equals_single_gpu(exchange):
+@pytest.mark.parametrize("world,exchange", [(2, "peer"), (2, "nccl"), (4, "peer"), (8, "peer")])
+def test_tp_decode_equals_single_gpu(world, exchange):
     """Peer-memory exchange inside the GEMVs (default) and the NCCL all-reduce path."""
     from mlx_motif.model import MotifDecoder
 
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    port = 29600 + (os.getpid() % 300) + (7 if exchange == "nccl" else 0)
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, q, exchange == "nccl")) for r in range(2)]
+    port = 29600 + (os.getpid() % 300) + 11 * world + (7 if exchange == "nccl" else 0)
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q, exchange == "nccl")) for r in range(world)]
     for p in procs:
         p.start()
     got = dict(q.get(timeout=300) for _ in procs)
@@ -66,6 +68,7 @@ def test_tp2_decode_equals_single_gpu(exchange):
         p.join(timeout=120)
         assert p.exitcode == 0
     ref = MotifDecoder.random(_args(), seed=5, std=0.05, max_seq=64, device="cuda:0").generate(PROMPT, N_TOKENS)
-    assert got[0] == got[1], "ranks disagree on the greedy tokens"
-    assert got[0][0] == ref, f"TP2 tokens {got[0][0]} != single-GPU tokens {ref}"
-    assert got[0][1] == ref, "TP2 tokens after reset() differ"
+    for r in range(1, world):
+        assert got[r] == got[0], f"rank {r} disagrees on the greedy tokens"
+    assert got[0][0] == ref, f"TP{world} tokens {got[0][0]} != single-GPU tokens {ref}"
+    assert got[0][1] == ref, f"TP{world} tokens after reset() differ"
