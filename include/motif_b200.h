@@ -188,6 +188,25 @@ MOTIF_API int motif_gda_decode_step(const void* qkv, const float* inv_freq, cons
                                     float lambda_init, float eps, void* out, void* workspace,
                                     size_t workspace_bytes, void* stream);
 
+/* The vanilla (ungrouped differential) decoder's attention step for one layer
+ * in ONE launch: MotifAttention._forward_vanilla (reference model.py:486-559)
+ * for batch 1, fp16. qkv: the fused projection row [q (2*H heads, q1/q2
+ * interleaved) | k (2*kv_heads, k1/k2 interleaved) | v (2*kv_heads, the
+ * projection's paired order v0_a, v0_b, v1_a, ...)], H = kv_heads*n_rep.
+ * The cache is the 4-slot layout with kv_heads heads per slot: k1, k2, the
+ * slab halves va and vb (cache.py:55-69). The new row is roped, written at
+ * pos_len[0], and the step attends over [0, pos_len[1]): q1 heads score on
+ * k1, q2 heads on k2, each against [va | vb]; then (o1 - lambda*o2), SubLN
+ * over 2*head_dim and the (1 - lambda_init) scale, with MLX's fp16 rounding
+ * at each op. out: (H, 2*head_dim) — the o_proj input. n_rep in {1, 2, 4},
+ * head_dim 128, lambda_full one value. workspace: as motif_gda_decode_step's
+ * with q_heads = 2*H; the same programmatic-dependent-launch precondition. */
+MOTIF_API int motif_vanilla_decode_step(const void* qkv, const float* inv_freq, const motif_kv4_slots* cache,
+                                        const int32_t* pos_len, float scale, int64_t kv_heads, int64_t n_rep,
+                                        const void* subln_w, const float* lambda_full, float lambda_init,
+                                        float eps, void* out, void* workspace, size_t workspace_bytes,
+                                        void* stream);
+
 /* ---- affine quantization ---------------------------------------------------
  * MLX-layout affine group quantization along the last axis (bits 4 or 8):
  * data (rows, dim*bits/32) uint32 little-endian, scales/biases

@@ -361,6 +361,60 @@ __device__ __forceinline__ void gda_merge_group(const float* __restrict__ ws, in
   }
 }
 
+// Merge split partials of one vanilla group (NP pairs of signal head 2j, noise head 2j+1) and
+// apply the differential combine of _forward_vanilla (model.py:553-557), rounding where the
+// reference's fp16 arrays round: p = fp16(fp16(λ)·o2), d = fp16(o1 − p), y = fp16(rms_norm(d)·w),
+// out = fp16(y·fp16(1 − λ_init)). Run by a CTA of 2D threads; out is (heads, 2D) of this group.
+template <int D, int NP>
+__device__ __forceinline__ void vanilla_merge_group(const float* __restrict__ ws, int nsplit, int n_active, int g,
+                                                    const __half* __restrict__ subln_w,
+                                                    const float* __restrict__ lam, float out_scale, float eps,
+                                                    __half* __restrict__ out) {
+  __shared__ float scratch[32 * NP];
+  __shared__ float f_s[2 * NP][kMaxSplits];
+  __shared__ float L_s[2 * NP];
+  const int ch = threadIdx.x;  // 0 .. 2D-1
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  constexpr int stride = 2 * D + 2;
+  if (warp < 2 * NP) {
+    const int head = 2 * (g * NP + (warp >> 1)) + (warp & 1);
+    split_weights(ws + (int64_t)head * nsplit * stride, n_active, stride, f_s[warp], &L_s[warp], lane);
+  }
+  __syncthreads();
+  const float* hb[2 * NP];
+  float acc[2 * NP];
+#pragma unroll
+  for (int j = 0; j < 2 * NP; ++j) {
+    hb[j] = ws + (int64_t)(2 * (g * NP + (j >> 1)) + (j & 1)) * nsplit * stride + 2 + ch;
+    acc[j] = 0.f;
+  }
+  for (int s = 0; s < n_active; ++s) {
+    float a[2 * NP];
+#pragma unroll
+    for (int j = 0; j < 2 * NP; ++j) a[j] = __ldcg(hb[j] + s * stride);
+#pragma unroll
+    for (int j = 0; j < 2 * NP; ++j) acc[j] += f_s[j][s] * a[j];
+  }
+  const float lam16 = __half2float(__float2half_rn(lam[0]));
+  float d[NP], ssq[NP];
+#pragma unroll
+  for (int j = 0; j < NP; ++j) {
+    const float o1 = round_through<__half>(L_s[2 * j] > 0.f ? acc[2 * j] / L_s[2 * j] : 0.f);
+    const float o2 = round_through<__half>(L_s[2 * j + 1] > 0.f ? acc[2 * j + 1] / L_s[2 * j + 1] : 0.f);
+    d[j] = round_through<__half>(o1 - round_through<__half>(lam16 * o2));
+    ssq[j] = d[j] * d[j];
+  }
+  block_sum<NP>(ssq, scratch);
+  const float w = __half2float(subln_w[ch]);
+  const float os16 = __half2float(__float2half_rn(out_scale));
+#pragma unroll
+  for (int j = 0; j < NP; ++j) {
+    const float inv = rsqrtf(ssq[j] / (float)(2 * D) + eps);
+    const float y = round_through<__half>(d[j] * inv * w);
+    out[(int64_t)(g * NP + j) * 2 * D + ch] = __float2half_rn(y * os16);
+  }
+}
+
 template <int D, int GR>
 __global__ void gda_combine_kernel(const float* __restrict__ ws, int nsplit, int kv_len_host,
                                    const int32_t* __restrict__ kv_len_dev, int q_origin,
@@ -405,9 +459,19 @@ struct FusedArgs {
   int* counters;  // [groups]
 };
 
-template <int BITS, int GR, int LPG>
+// Query heads of a group: NA signal heads on k1 and NB noise heads on k2. GDA (PAIRED false):
+// signal heads g·NA + j (origin-first), one noise head q_origin + g. Vanilla (PAIRED true,
+// NB == NA): the stripes interleave, signal head 2·(g·NA + j) and its noise head right after.
+template <int NA, int NB, bool PAIRED>
+__device__ __forceinline__ int fused_head(int g, int h, int q_origin) {
+  if (PAIRED) return 2 * (g * NA + (h < NA ? h : h - NA)) + (h < NA ? 0 : 1);
+  return h < NA ? g * NA + h : q_origin + g;
+}
+
+template <int BITS, int NA, int NB, bool PAIRED, int PPW, int LPG>
 __global__ void __launch_bounds__(kAttnThreads) gda_fused_kernel(FusedArgs f) {
-  constexpr int D = 128, CPL = D / 32, NH = GR + 1, half = D / 2;
+  constexpr int D = 128, CPL = D / 32, NH = NA + NB, half = D / 2;
+  constexpr int kPosPerWarp = PPW, kRoundPositions = kAttnWarps * PPW;
   __shared__ float s_row[4][D];
   __shared__ float s_cs[half], s_sn[half];
   __shared__ int s_last;
@@ -498,7 +562,7 @@ __global__ void __launch_bounds__(kAttnThreads) gda_fused_kernel(FusedArgs f) {
   float q[NH][CPL];
 #pragma unroll
   for (int h = 0; h < NH; ++h) {
-    const int head = h < GR ? g * GR + h : f.q_origin + g;
+    const int head = fused_head<NA, NB, PAIRED>(g, h, f.q_origin);
     const __half* src = f.qkv + (int64_t)head * D;
 #pragma unroll
     for (int j = 0; j < CPL; ++j) {
@@ -523,17 +587,11 @@ __global__ void __launch_bounds__(kAttnThreads) gda_fused_kernel(FusedArgs f) {
       if (base + u >= p1) break;
       float s[NH];
 #pragma unroll
-      for (int h = 0; h < GR; ++h) {
+      for (int h = 0; h < NH; ++h) {  // signal heads score on k1, noise heads on k2
         float t = 0.f;
 #pragma unroll
-        for (int c = 0; c < CPL; ++c) t += q[h][c] * ka[u][c];
+        for (int c = 0; c < CPL; ++c) t += q[h][c] * (h < NA ? ka[u][c] : kb[u][c]);
         s[h] = t;
-      }
-      {
-        float t = 0.f;
-#pragma unroll
-        for (int c = 0; c < CPL; ++c) t += q[GR][c] * kb[u][c];
-        s[GR] = t;
       }
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) {
@@ -594,7 +652,7 @@ __global__ void __launch_bounds__(kAttnThreads) gda_fused_kernel(FusedArgs f) {
         O += sm_o[(int64_t)(w * NH + h) * 2 * D + ch] * fw;
       }
     }
-    const int hh = h < GR ? g * GR + h : f.q_origin + g;
+    const int hh = fused_head<NA, NB, PAIRED>(g, h, f.q_origin);
     float* p = f.ws + ((int64_t)hh * nsplit + split) * (2 * D + 2);
     p[2 + ch] = O;
     if (ch == 0) {
@@ -610,8 +668,11 @@ __global__ void __launch_bounds__(kAttnThreads) gda_fused_kernel(FusedArgs f) {
   __syncthreads();
   if (!s_last) return;
   __threadfence();  // acquire the other CTAs' partials
-  gda_merge_group<D, GR>(f.ws, nsplit, n_active, g, f.q_origin, f.subln_w, f.lam, f.lam_mode, f.out_scale, f.eps,
-                         f.out);
+  if constexpr (PAIRED)
+    vanilla_merge_group<D, NA>(f.ws, nsplit, n_active, g, f.subln_w, f.lam, f.out_scale, f.eps, f.out);
+  else
+    gda_merge_group<D, NA>(f.ws, nsplit, n_active, g, f.q_origin, f.subln_w, f.lam, f.lam_mode, f.out_scale, f.eps,
+                           f.out);
   if (threadIdx.x == 0) f.counters[g] = 0;  // ready for the next launch
 }
 
@@ -884,6 +945,67 @@ int motif_gda_decode_attention(const void* q, const motif_kv4_slots* cache, floa
   return check_launch("gda decode attention");
 }
 
+}  // extern "C"
+
+namespace motif {
+namespace {
+
+template <int NA, int NB, bool PAIRED, int PPW, int BITS, int LPG>
+cudaError_t launch_fused_one(const FusedArgs& f, dim3 grid, cudaStream_t st) {
+  auto kern = gda_fused_kernel<BITS, NA, NB, PAIRED, PPW, LPG>;
+  const size_t smem = sizeof(float) * (size_t)kAttnWarps * (NA + NB) * (2 + 2 * 128);
+  static bool configured = false;  // one attribute call per instantiation
+  if (!configured) {
+    const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    configured = true;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(kAttnThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, f);
+}
+
+// The one-launch attention step for one head layout, dispatched over the cache's bits and group size.
+template <int NA, int NB, bool PAIRED, int PPW>
+cudaError_t launch_fused(const FusedArgs& f, dim3 grid, int bits, int gs, cudaStream_t st) {
+  if (bits == 16) return launch_fused_one<NA, NB, PAIRED, PPW, 16, 8>(f, grid, st);
+  if (gs == 32) return bits == 4 ? launch_fused_one<NA, NB, PAIRED, PPW, 4, 4>(f, grid, st)
+                                 : launch_fused_one<NA, NB, PAIRED, PPW, 8, 4>(f, grid, st);
+  if (gs == 64) return bits == 4 ? launch_fused_one<NA, NB, PAIRED, PPW, 4, 8>(f, grid, st)
+                                 : launch_fused_one<NA, NB, PAIRED, PPW, 8, 8>(f, grid, st);
+  return bits == 4 ? launch_fused_one<NA, NB, PAIRED, PPW, 4, 16>(f, grid, st)
+                   : launch_fused_one<NA, NB, PAIRED, PPW, 8, 16>(f, grid, st);
+}
+
+int check_fused_cache(const motif_kv4_slots& c, int64_t groups, const char* who) {
+  for (int i = 0; i < 4; ++i) MOTIF_REQUIRE(c.data[i], MOTIF_ERR_NULL, "%s: slot %d null", who, i);
+  MOTIF_REQUIRE(c.batch == 1 && c.head_dim == 128, MOTIF_ERR_BAD_CONTRACT, "%s: batch 1, head_dim 128 only", who);
+  MOTIF_REQUIRE(c.heads == groups && groups > 0, MOTIF_ERR_BAD_CONTRACT,
+                "%s: kv heads per slot (%lld) must equal the groups (%lld)", who, (long long)c.heads,
+                (long long)groups);
+  MOTIF_REQUIRE(c.capacity > 0 && c.capacity < (1ll << 31), MOTIF_ERR_BAD_SHAPE, "%s: capacity", who);
+  const int bits = c.bits;
+  MOTIF_REQUIRE(bits == 16 || ((bits == 4 || bits == 8) && c.scales[0] && c.biases[0] && c.scales[1] && c.biases[1] &&
+                               c.scales[2] && c.biases[2] && c.scales[3] && c.biases[3] &&
+                               (c.group_size == 32 || c.group_size == 64 || c.group_size == 128)),
+                MOTIF_ERR_BAD_CONTRACT, "%s: cache bits/group_size", who);
+  MOTIF_REQUIRE(groups * sizeof(int) <= kFusedCtlBytes, MOTIF_ERR_BAD_SHAPE, "%s: too many groups", who);
+  return MOTIF_OK;
+}
+
+}  // namespace
+}  // namespace motif
+
+extern "C" {
+
 size_t motif_gda_decode_step_workspace_bytes(int64_t q_heads, int64_t head_dim, int64_t max_splits) {
   if (q_heads <= 0 || head_dim <= 0 || max_splits <= 0) return 0;
   return kFusedCtlBytes + partial_bytes(q_heads, head_dim, max_splits < kMaxSplits ? max_splits : kMaxSplits);
@@ -940,49 +1062,53 @@ int motif_gda_decode_step(const void* qkv, const float* inv_freq, const motif_kv
   f.counters = static_cast<int*>(workspace);
   f.ws = reinterpret_cast<float*>(static_cast<char*>(workspace) + kFusedCtlBytes);
   cudaStream_t st = as_stream(stream);
-  dim3 grid(nsplit, (unsigned)q_groups);
-  cudaError_t e = cudaSuccess;
-#define MOTIF_FUSED_LAUNCH(BITS, GR, LPG)                                                              \
-  {                                                                                                     \
-    auto kern = gda_fused_kernel<BITS, GR, LPG>;                                                        \
-    const size_t smem = sizeof(float) * (size_t)kAttnWarps * (GR + 1) * (2 + 2 * 128);                 \
-    static bool configured = false;                                                                     \
-    if (!configured) {                                                                                  \
-      e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);           \
-      configured = e == cudaSuccess;                                                                    \
-    }                                                                                                   \
-    if (e == cudaSuccess) {                                                                             \
-      cudaLaunchConfig_t cfg = {};                                                                      \
-      cfg.gridDim = grid;                                                                               \
-      cfg.blockDim = dim3(kAttnThreads);                                                                \
-      cfg.dynamicSmemBytes = smem;                                                                      \
-      cfg.stream = st;                                                                                  \
-      cudaLaunchAttribute attr[1];                                                                      \
-      attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;                                  \
-      attr[0].val.programmaticStreamSerializationAllowed = 1;                                           \
-      cfg.attrs = attr;                                                                                 \
-      cfg.numAttrs = 1;                                                                                 \
-      e = cudaLaunchKernelEx(&cfg, kern, f);                                                            \
-    }                                                                                                   \
-  }
-#define MOTIF_FUSED_BITS(GR)                                                    \
-  if (bits == 16) MOTIF_FUSED_LAUNCH(16, GR, 8)                                 \
-  else if (c.group_size == 32) {                                                \
-    if (bits == 4) MOTIF_FUSED_LAUNCH(4, GR, 4) else MOTIF_FUSED_LAUNCH(8, GR, 4) \
-  } else if (c.group_size == 64) {                                              \
-    if (bits == 4) MOTIF_FUSED_LAUNCH(4, GR, 8) else MOTIF_FUSED_LAUNCH(8, GR, 8) \
-  } else {                                                                      \
-    if (bits == 4) MOTIF_FUSED_LAUNCH(4, GR, 16) else MOTIF_FUSED_LAUNCH(8, GR, 16) \
-  }
-  if (gr == 3) {
-    MOTIF_FUSED_BITS(3)
-  } else {
-    MOTIF_FUSED_BITS(4)
-  }
-#undef MOTIF_FUSED_BITS
-#undef MOTIF_FUSED_LAUNCH
+  const dim3 grid(nsplit, (unsigned)q_groups);
+  const cudaError_t e = gr == 3 ? launch_fused<3, 1, false, 4>(f, grid, c.bits, c.group_size, st)
+                                : launch_fused<4, 1, false, 4>(f, grid, c.bits, c.group_size, st);
   if (e != cudaSuccess) return fail(MOTIF_ERR_CUDA, "gda_decode_step: launch: %s", cudaGetErrorString(e));
   return check_launch("gda decode step");
+}
+
+int motif_vanilla_decode_step(const void* qkv, const float* inv_freq, const motif_kv4_slots* cache,
+                              const int32_t* pos_len, float scale, int64_t kv_heads, int64_t n_rep,
+                              const void* subln_w, const float* lambda_full, float lambda_init, float eps,
+                              void* out, void* workspace, size_t workspace_bytes, void* stream) {
+  MOTIF_REQUIRE(qkv && inv_freq && cache && pos_len && subln_w && lambda_full && out && workspace, MOTIF_ERR_NULL,
+                "vanilla_decode_step: null pointer");
+  MOTIF_REQUIRE(n_rep == 1 || n_rep == 2 || n_rep == 4, MOTIF_ERR_BAD_CONTRACT,
+                "vanilla_decode_step: n_rep=%lld not built (1, 2, 4)", (long long)n_rep);
+  const motif_kv4_slots& c = *cache;
+  if (int rc = check_fused_cache(c, kv_heads, "vanilla_decode_step")) return rc;
+  const int64_t q_heads = 2 * kv_heads * n_rep;  // interleaved q1/q2 stripes
+  MOTIF_REQUIRE(workspace_bytes > kFusedCtlBytes, MOTIF_ERR_WORKSPACE, "vanilla_decode_step: workspace too small");
+  const int64_t max_splits_ws = (workspace_bytes - kFusedCtlBytes) / partial_bytes(q_heads, 128, 1);
+  MOTIF_REQUIRE(max_splits_ws >= 1, MOTIF_ERR_WORKSPACE, "vanilla_decode_step: workspace too small");
+  const int nsplit = choose_splits(kv_heads, c.capacity, max_splits_ws);
+  FusedArgs f{};
+  f.qkv = static_cast<const __half*>(qkv);
+  f.inv_freq = inv_freq;
+  f.q_heads = (int)q_heads;
+  f.q_origin = 0;
+  f.groups = (int)kv_heads;
+  f.cache = c;
+  f.pos_len = pos_len;
+  f.scale_log2 = scale * kLog2e;
+  f.subln_w = static_cast<const __half*>(subln_w);
+  f.lam = lambda_full;
+  f.lam_mode = 0;
+  f.out_scale = 1.0f - lambda_init;
+  f.eps = eps;
+  f.out = static_cast<__half*>(out);
+  f.counters = static_cast<int*>(workspace);
+  f.ws = reinterpret_cast<float*>(static_cast<char*>(workspace) + kFusedCtlBytes);
+  cudaStream_t st = as_stream(stream);
+  const dim3 grid(nsplit, (unsigned)kv_heads);
+  cudaError_t e;
+  if (n_rep == 1) e = launch_fused<1, 1, true, 4>(f, grid, c.bits, c.group_size, st);
+  else if (n_rep == 2) e = launch_fused<2, 2, true, 4>(f, grid, c.bits, c.group_size, st);
+  else e = launch_fused<4, 4, true, 2>(f, grid, c.bits, c.group_size, st);
+  if (e != cudaSuccess) return fail(MOTIF_ERR_CUDA, "vanilla_decode_step: launch: %s", cudaGetErrorString(e));
+  return check_launch("vanilla decode step");
 }
 
 }  // extern "C"

@@ -7,7 +7,7 @@ in-tree C-ABI library ``libmotif_b200.so`` (``include/motif_b200.h``).
 """
 
 from . import _native  # noqa: F401  (loads the CUDA library; raises if it is missing)
-from .cache import MotifGroupedKVCache, MotifGroupedQuantizedKVCache  # noqa: F401
+from .cache import MotifGroupedKVCache, MotifGroupedQuantizedKVCache, MotifVanillaKVCache  # noqa: F401
 from .linear import QuantizedLinear, quantized_matmul  # noqa: F401
 from .quantization import dequantize, quantize  # noqa: F401
 

@@ -103,6 +103,10 @@ SIGNATURES = {
         _I,
         [_P, _P, _KV, _P, _F, _L, _L, _P, _P, _L, _F, _F, _P, _P, _S, _P],
     ),
+    "motif_vanilla_decode_step": (
+        _I,
+        [_P, _P, _KV, _P, _F, _L, _L, _P, _P, _F, _F, _P, _P, _S, _P],
+    ),
     "motif_gda_decode_attention": (
         _I,
         [_P, _KV, _F, _L, _L, _L, _P, _P, _P, _L, _F, _F, _P, _P, _S, _P],

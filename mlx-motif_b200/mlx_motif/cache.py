@@ -277,3 +277,113 @@ class MotifGroupedQuantizedKVCache(MotifGroupedKVCacheBase):
     @meta_state.setter
     def meta_state(self, v):
         self.offset, self.group_size, self.bits = map(int, v)
+
+
+# --------------------------------------------------------------------------- #
+# Vanilla (ungrouped) differential attention cache — cache.py:55-175
+# --------------------------------------------------------------------------- #
+
+
+def vanilla_v_paired_to_slab_perm(n_kv_heads: int) -> torch.Tensor:
+    """Head index of the projection's paired V order ``[v0_a, v0_b, v1_a, ...]`` that lands at slab
+    position p of ``[va_0 .. va_{H-1}, vb_0 .. vb_{H-1}]``: 2·(p mod H) + p div H (``cache.py:55-69``)."""
+    h = n_kv_heads
+    return torch.tensor([2 * (p % h) + (p // h) for p in range(2 * h)], dtype=torch.int64)
+
+
+def vanilla_v_slab_to_paired_perm(n_kv_heads: int) -> torch.Tensor:
+    """The inverse permutation, slab -> paired: (q mod 2)·H + q div 2 (``cache.py:72-82``)."""
+    h = n_kv_heads
+    return torch.tensor([(q % 2) * h + (q // 2) for q in range(2 * h)], dtype=torch.int64)
+
+
+class MotifVanillaKVCache(MotifGroupedKVCache):
+    """KV cache of the vanilla (2.6B-class) differential attention path (``cache.py:85-175``).
+
+    Reference view (mlx-lm ``KVCache`` semantics): ``keys`` (B, 2·Hk, offset, d) in the k
+    projection's stripe order [k1_0, k2_0, k1_1, ...] and ``values`` (B, 2·Hk, offset, d) in SLAB
+    order [va_0 .. va_{Hk-1}, vb_0 .. vb_{Hk-1}]; ``update_and_fetch(keys, values)`` takes the new
+    rows in those orders and returns the whole live cache. ``meta_state`` carries the "slab"
+    marker and a restore with another (or no) marker raises; ``hf_ordered_values`` gives V in
+    the paired order.
+
+    Device layout: the 4-slot form with Hk heads per slot — k1 (even k heads), k2 (odd), va, vb
+    — so the one-launch decode step (``motif_vanilla_decode_step``) reads each slot as a
+    row-contiguous (Hk, capacity, d) array. ``keys``/``values`` are gathered copies.
+    """
+
+    V_HEAD_ORDER = "slab"
+
+    def update_and_fetch(self, keys, values):
+        if keys.shape[1] % 2 or keys.shape[1] != values.shape[1]:
+            raise ValueError(f"vanilla cache: keys {tuple(keys.shape)} / values {tuple(values.shape)} need "
+                             "an even, equal head count (2·Hk)")
+        hk = keys.shape[1] // 2
+        self.update_and_fetch_4(keys[:, 0::2], keys[:, 1::2], values[:, :hk], values[:, hk:])
+        return self.keys, self.values
+
+    @property
+    def keys(self):
+        if self.k1 is None:
+            return None
+        o = self.offset
+        B, hk, _, D = self.k1.shape
+        return torch.stack([self.k1[:, :, :o], self.k2[:, :, :o]], dim=2).reshape(B, 2 * hk, o, D)
+
+    @property
+    def values(self):
+        if self.v1 is None:
+            return None
+        o = self.offset
+        return torch.cat([self.v1[:, :, :o], self.v2[:, :, :o]], dim=1)
+
+    def hf_ordered_values(self):
+        """The live V in the projection's paired order (a gathered copy), or None when empty."""
+        v = self.values
+        if v is None:
+            return None
+        return v[:, vanilla_v_slab_to_paired_perm(v.shape[1] // 2).to(v.device)]
+
+    @property
+    def state(self):
+        return self.keys, self.values
+
+    @state.setter
+    def state(self, v):
+        keys, values = v
+        B, h2, n, D = keys.shape
+        hk = h2 // 2
+        cap = max(n, self.max_size or 0)
+        self.k1, self.k2, self.v1, self.v2 = (
+            self._init_storage(B, hk, cap, D, keys.dtype, keys.device) for _ in range(4)
+        )
+        for dst, src in zip((self.k1, self.k2, self.v1, self.v2),
+                            (keys[:, 0::2], keys[:, 1::2], values[:, :hk], values[:, hk:])):
+            dst[:, :, :n].copy_(src)
+        self.offset = n
+
+    @property
+    def meta_state(self):
+        return (self.V_HEAD_ORDER,)
+
+    @meta_state.setter
+    def meta_state(self, v):
+        marker = None
+        if isinstance(v, (tuple, list)):
+            marker = v[0] if len(v) else None
+        elif v not in (None, ""):
+            marker = v
+        if marker is None:
+            raise ValueError("MotifVanillaKVCache.from_state: state carries no V head-order marker; the "
+                             f"vanilla path stores V in slab order (expected {self.V_HEAD_ORDER!r})")
+        if marker != self.V_HEAD_ORDER:
+            raise ValueError(f"MotifVanillaKVCache.from_state: V head-order marker mismatch — got {marker!r}, "
+                             f"expected {self.V_HEAD_ORDER!r}")
+
+    @classmethod
+    def from_state(cls, state, meta_state, max_size: int | None = None) -> "MotifVanillaKVCache":
+        """mlx-lm ``_BaseCache.from_state``: state first, then the marker check."""
+        c = cls(max_size=max_size)
+        c.state = state
+        c.meta_state = meta_state
+        return c

@@ -28,7 +28,7 @@ from dataclasses import dataclass
 import torch
 
 from ._native import check, lib, motif_linear_io, ptr, stream
-from .cache import MotifGroupedKVCache, MotifGroupedQuantizedKVCache
+from .cache import MotifGroupedKVCache, MotifGroupedQuantizedKVCache, MotifVanillaKVCache
 from .linear import QuantizedLinear
 from .quantization import quantize
 
@@ -112,21 +112,30 @@ class ModelArgs:
     def is_grouped(self) -> bool:
         return self.num_noise_heads is not None
 
-    # Derived grouped-attention dims (MotifAttention._init_grouped, model.py:424-447).
+    # Derived attention dims: grouped (MotifAttention._init_grouped, model.py:424-447) and
+    # vanilla (_init_vanilla, model.py:450-454: H = heads / 2, Hk = kv heads / 2).
     @property
     def d(self) -> int:
         return self.head_dim or self.hidden_size // self.num_attention_heads
 
     @property
     def grouped_ratio(self) -> int:
+        """Grouped: origin heads per noise head. Vanilla: q pairs per kv pair (n_rep = H / Hk)."""
+        if not self.is_grouped:
+            return self.num_attention_heads // self.num_key_value_heads
         return (self.num_attention_heads - self.num_noise_heads) // self.num_noise_heads
 
     @property
     def q_heads(self) -> int:
+        if not self.is_grouped:
+            return self.num_attention_heads
         return (self.grouped_ratio + 1) * self.num_noise_heads
 
     @property
     def q_origin(self) -> int:
+        """Rows of the attention output (each 2·d wide): gr·G grouped, H vanilla."""
+        if not self.is_grouped:
+            return self.num_attention_heads // 2
         return self.grouped_ratio * self.num_noise_heads
 
     @property
@@ -135,6 +144,8 @@ class ModelArgs:
 
     @property
     def kv_repeat(self) -> int:
+        if not self.is_grouped:
+            return 1
         return self.num_noise_heads // self.k_noise_heads
 
     @property
@@ -264,7 +275,12 @@ def _t(a, device, dtype=None) -> torch.Tensor:
 
 
 class MotifDecoder:
-    """Batch-1 greedy decoder of the grouped Motif model on one GPU (or one TP rank).
+    """Batch-1 greedy decoder of the Motif model on one GPU (or one TP rank).
+
+    Grouped configs (``num_noise_heads`` set) run ``_forward_grouped``'s DUAL_V /
+    QUANT_SDPA path; vanilla configs (``num_noise_heads`` None, the 2.6B class)
+    run ``_forward_vanilla`` (``model.py:486-559``) on a ``MotifVanillaKVCache``
+    (one GPU; its 4-slot form holds k1, k2 and the two V slabs).
 
     ``cache``: "fp16" (4-slot fp16 rows) or "q4"/"q8" (packed 4-slot cache,
     group 64). ``max_seq`` is the preallocated KV capacity. With a process
@@ -275,7 +291,14 @@ class MotifDecoder:
 
     def __init__(self, args: ModelArgs, weights: dict, cache: str = "fp16", max_seq: int = 4096,
                  device="cuda", tp_group=None):
-        if not args.is_grouped or args.k_ratio != 1 or args.kv_repeat != 1:
+        self.vanilla = not args.is_grouped
+        if self.vanilla:
+            if tp_group is not None:
+                raise ValueError("the vanilla decode path runs on one GPU (no tensor parallelism)")
+            if args.grouped_ratio not in (1, 2, 4) or args.d != 128:
+                raise ValueError(f"vanilla decode step built for n_rep 1, 2, 4 and head_dim 128 "
+                                 f"(got n_rep {args.grouped_ratio}, head_dim {args.d})")
+        elif args.k_ratio != 1 or args.kv_repeat != 1:
             raise ValueError("MotifDecoder runs the grouped DUAL_V/QUANT_SDPA decode path "
                              "(num_noise_heads set, k_ratio == 1, kv_repeat == 1)")
         self.args = args
@@ -283,11 +306,15 @@ class MotifDecoder:
         self.tp_group = tp_group
         self.tp = 1 if tp_group is None else torch.distributed.get_world_size(tp_group)
         a = args
-        self.q_groups = a.num_noise_heads // self.tp
-        self.gr = a.grouped_ratio
+        self.gr = a.grouped_ratio  # vanilla: n_rep, the q pairs of one kv pair
         self.d = a.d
         self.kv_heads = a.k_noise_heads // self.tp
-        self.q_heads = self.q_groups * (self.gr + 1)
+        if self.vanilla:
+            self.q_groups = self.kv_heads
+            self.q_heads = 2 * self.q_groups * self.gr  # q1/q2 stripes interleaved
+        else:
+            self.q_groups = a.num_noise_heads // self.tp
+            self.q_heads = self.q_groups * (self.gr + 1)
         self.q_origin = self.q_groups * self.gr
         self.inter = a.intermediate_size // self.tp
         self.H = a.hidden_size
@@ -330,7 +357,8 @@ class MotifDecoder:
 
         # KV caches: preallocated capacity (buffers never move; graph-safe).
         if cache == "fp16":
-            self.caches = [MotifGroupedKVCache(max_size=max_seq) for _ in self.layers]
+            kind = MotifVanillaKVCache if self.vanilla else MotifGroupedKVCache
+            self.caches = [kind(max_size=max_seq) for _ in self.layers]
         elif cache in ("q4", "q8"):
             bits = 4 if cache == "q4" else 8
             self.caches = [MotifGroupedQuantizedKVCache(64, bits, max_size=max_seq) for _ in self.layers]
@@ -373,7 +401,7 @@ class MotifDecoder:
             raise ValueError("intermediate size per rank must be a multiple of 16")
         self.lin_ws = torch.zeros(max(lin_ws, 16), dtype=torch.uint8, device=dev)
         # MOTIF_FUSED_ATTN=0 runs RoPE/append and the attention as two calls (for comparisons).
-        self.fused_attn = os.environ.get("MOTIF_FUSED_ATTN", "1") != "0"
+        self.fused_attn = self.vanilla or os.environ.get("MOTIF_FUSED_ATTN", "1") != "0"
         if self.fused_attn:
             self.attn_ws_bytes = lib.motif_gda_decode_step_workspace_bytes(self.q_heads, d, 64)
         else:
@@ -589,7 +617,13 @@ class MotifDecoder:
         for li, L in enumerate(self.layers):
             qkv_io, o_io, gu_io, dn_io = plan[li]
             self._linear(qkv_io, L["qkv"], self.qkv, st)
-            if self.fused_attn:
+            if self.vanilla:
+                check(lib.motif_vanilla_decode_step(ptr(self.qkv), ptr(self.inv_freq), self._slots[li], pos_p,
+                                                    self.scale, self.kv_heads, self.gr, ptr(L["subln"]),
+                                                    ptr(L["lambda_full"]), L["lambda_init"],
+                                                    self.args.attn_rms_norm_eps, ptr(self.attn), ptr(self.attn_ws),
+                                                    self.attn_ws_bytes, st), "vanilla_decode_step")
+            elif self.fused_attn:
                 check(lib.motif_gda_decode_step(ptr(self.qkv), ptr(self.inv_freq), self._slots[li], pos_p, self.scale,
                                                 self.q_groups, self.gr, ptr(L["subln"]), ptr(L["lambda_full"]),
                                                 L["lambda_full"].numel(), L["lambda_init"],
@@ -742,7 +776,6 @@ class MotifDecoder:
         f16 = torch.float16
         a = args
         H, I, d = a.hidden_size, a.intermediate_size, a.d
-        G, gr, Hk = a.num_noise_heads, a.grouped_ratio, a.k_noise_heads
 
         def randn(*shape):
             return (torch.randn(shape, generator=gen, device=dev, dtype=torch.float32) * std).to(f16)
@@ -753,7 +786,7 @@ class MotifDecoder:
         def norm_w(n):
             return (1.0 + 0.02 * torch.randn(n, generator=gen, device=dev)).to(f16)
 
-        plan = tp_shard_plan(args, rank, world)
+        plan = tp_shard_plan(args, rank, world) if world > 1 else None
         layers = []
         for li in range(a.num_hidden_layers):
             qkv = randn(a.qkv_out, H)

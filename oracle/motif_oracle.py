@@ -51,6 +51,13 @@ __all__ = [
     "make_synthetic_weights",
     "GroupedDecodeOracle",
     "shard_weights_tp",
+    "vanilla_v_paired_to_slab_perm",
+    "vanilla_v_slab_to_paired_perm",
+    "OracleVanillaKVCache",
+    "vanilla_attention_reference",
+    "OracleVanillaArgs",
+    "make_synthetic_weights_vanilla",
+    "VanillaDecodeOracle",
 ]
 
 
@@ -730,3 +737,221 @@ def shard_weights_tp(args: OracleArgs, weights: dict, rank: int, world: int) -> 
         )
     return dict(weights, layers=out_layers)
 
+
+# --------------------------------------------------------------------------- #
+# Vanilla decoder (2.6B-class, ungrouped differential attention) —
+# model.py:486-559 (_forward_vanilla), 450-454 (_init_vanilla), cache.py:55-175
+# --------------------------------------------------------------------------- #
+
+
+def vanilla_v_paired_to_slab_perm(n_kv_heads: int) -> np.ndarray:
+    """``cache.py:55-69``: head index of the paired V order [v0_a, v0_b, v1_a, ...] that lands
+    at slab position p of [va_0 .. va_{H-1}, vb_0 .. vb_{H-1}]: 2·(p mod H) + p div H."""
+    h = n_kv_heads
+    return np.array([2 * (p % h) + (p // h) for p in range(2 * h)], np.int64)
+
+
+def vanilla_v_slab_to_paired_perm(n_kv_heads: int) -> np.ndarray:
+    """``cache.py:72-82``: the inverse permutation, (q mod 2)·H + q div 2."""
+    h = n_kv_heads
+    return np.array([(q % 2) * h + (q // 2) for q in range(2 * h)], np.int64)
+
+
+class OracleVanillaKVCache:
+    """``MotifVanillaKVCache`` (``cache.py:85-175``) on mlx-lm ``KVCache`` semantics: keys in the
+    projection's stripe order, values in slab order, appended along the sequence axis;
+    ``update_and_fetch`` returns the whole live cache."""
+
+    V_HEAD_ORDER = "slab"
+
+    def __init__(self):
+        self.keys = None
+        self.values = None
+        self.offset = 0
+
+    def update_and_fetch(self, k, v):
+        if self.keys is None:
+            self.keys, self.values = np.array(k), np.array(v)
+        else:
+            self.keys = np.concatenate([self.keys, k], axis=2)
+            self.values = np.concatenate([self.values, v], axis=2)
+        self.offset += k.shape[2]
+        return self.keys, self.values
+
+    def hf_ordered_values(self):  # cache.py:160-175
+        if self.values is None:
+            return None
+        perm = vanilla_v_slab_to_paired_perm(self.values.shape[1] // 2)
+        return self.values[:, perm, : self.offset, :]
+
+    @property
+    def meta_state(self):
+        return (self.V_HEAD_ORDER,)
+
+
+def _gqa_sdpa(q, k, v, scale):
+    """``mx.fast.scaled_dot_product_attention`` with native GQA: q head i reads kv head i // n_rep."""
+    qf, kf, vf = _f64(q), _f64(k), _f64(v)
+    n_rep = qf.shape[1] // kf.shape[1]
+    if n_rep > 1:
+        kf = np.repeat(kf, n_rep, axis=1)
+        vf = np.repeat(vf, n_rep, axis=1)
+    return _sdpa(qf, kf, vf, scale)
+
+
+def vanilla_attention_reference(q, k, v_paired, cache, lam, lam_init, subln_w, eps=1e-5, kv_dtype=np.float16):
+    """``_forward_vanilla`` (``model.py:486-559``) from the roped projections to the o_proj input.
+
+    q (B, 2H, S, d) and k (B, 2Hk, S, d) after RoPE, v (B, 2Hk, S, d) in the projection's paired
+    order; ``cache`` an ``OracleVanillaKVCache``. V goes to slab order (line 514), the cache
+    appends (521), the stripes split (528-533), four SDPAs run (548-551), and
+    (o1 − λ·o2) per slab, SubLN and the (1 − λ_init) scale follow (553-557), each op
+    rounded to fp16 as MLX's fp16 arrays are. Returns (B, H, S, 2d) fp16. ``kv_dtype``: the
+    element type the cache holds (fp16; float32 for rows dequantized from a q4/q8 cache, whose
+    values the quantized SDPA reads in fp32).
+    """
+    f16 = np.float16
+    B, two_h, S, d = q.shape
+    H, Hk = two_h // 2, k.shape[1] // 2
+    v = np.asarray(v_paired)[:, vanilla_v_paired_to_slab_perm(Hk)]
+    K, V = cache.update_and_fetch(np.asarray(k, kv_dtype), np.asarray(v, kv_dtype))
+    kv = K.shape[2]
+    va, vb = V[:, :Hk], V[:, Hk:]
+    q_ = np.asarray(q).reshape(B, H, 2, S, d)
+    k_ = K.reshape(B, Hk, 2, kv, d)
+    q1, q2 = q_[:, :, 0], q_[:, :, 1]
+    k1, k2 = k_[:, :, 0], k_[:, :, 1]
+    scale = d ** -0.5
+    o1a, o1b = (_gqa_sdpa(q1, k1, vs, scale).astype(f16) for vs in (va, vb))
+    o2a, o2b = (_gqa_sdpa(q2, k2, vs, scale).astype(f16) for vs in (va, vb))
+    lam16 = np.float16(np.asarray(lam, np.float32).reshape(-1)[0])
+
+    def diff(o1, o2):  # fp16 ops: the product, then the difference, each rounded
+        return (o1.astype(np.float32) - (lam16.astype(np.float32) * o2.astype(np.float32)).astype(f16)).astype(f16)
+
+    out = np.concatenate([diff(o1a, o2a), diff(o1b, o2b)], axis=-1)
+    out = rms_norm(out, subln_w, eps).astype(f16)
+    scale_out = np.float16(1.0 - lam_init)  # a Python float meets an fp16 array: cast to fp16
+    return (out.astype(np.float32) * np.float32(scale_out)).astype(f16)
+
+
+@dataclass
+class OracleVanillaArgs:
+    """Shape of a vanilla (2.6B-class) Motif decoder; defaults are config[3]."""
+
+    hidden_size: int = 2048
+    num_hidden_layers: int = 32
+    intermediate_size: int = 8192
+    num_attention_heads: int = 16  # halved to 8 effective differential heads
+    num_key_value_heads: int = 4  # halved to 2
+    head_dim: int = 128
+    vocab_size: int = 219520
+    rms_norm_eps: float = 1e-6
+    attn_rms_norm_eps: float = 1e-5
+    rope_theta: float = 10000.0
+    group_size: int = 64
+    bits: int = 4
+
+    @property
+    def H(self):  # model.py:452
+        return self.num_attention_heads // 2
+
+    @property
+    def Hk(self):  # model.py:453
+        return self.num_key_value_heads // 2
+
+    @property
+    def qkv_out(self):
+        d = self.head_dim
+        return 2 * self.H * d + 2 * self.Hk * d + 2 * self.Hk * d
+
+
+def make_synthetic_weights_vanilla(args: OracleVanillaArgs, seed: int = 0, std: float = 0.02) -> dict:
+    """Random-init vanilla weights: per layer one fused [q | k | v] linear (rows of q_proj,
+    k_proj and v_proj stacked; v in the projection's paired order), o (hidden, 2H·d), the
+    PolyNorm MLP, SubLN over 2d and one λ per layer."""
+    rng = np.random.default_rng(seed)
+    g, b = args.group_size, args.bits
+    Hd, I, d = args.hidden_size, args.intermediate_size, args.head_dim
+    f16 = np.float16
+
+    def norm_w(n):
+        return (1.0 + 0.02 * rng.standard_normal(n)).astype(f16)
+
+    layers = []
+    for li in range(args.num_hidden_layers):
+        lam_init = lambda_init_for_layer(li)
+        lp = [rng.standard_normal(d).astype(np.float32) * 0.1 for _ in range(4)]
+        layers.append(
+            dict(
+                input_norm=norm_w(Hd),
+                post_norm=norm_w(Hd),
+                qkv=_q_linear(rng, args.qkv_out, Hd, std, g, b),
+                o=_q_linear(rng, Hd, 2 * args.H * d, std, g, b),
+                gate=_q_linear(rng, I, Hd, std, g, b),
+                up=_q_linear(rng, I, Hd, std, g, b),
+                down=_q_linear(rng, Hd, I, std, g, b),
+                subln=norm_w(2 * d),
+                lambda_init=lam_init,
+                lambda_full=np.array([lambda_full(*lp, lam_init)], np.float32),
+                polynorm_w=np.array([1 / 3, 1 / 3, 1 / 3], f16),
+                polynorm_b=np.zeros((1,), f16),
+            )
+        )
+    return dict(
+        embed=(rng.standard_normal((args.vocab_size, Hd), dtype=np.float32) * std).astype(f16),
+        final_norm=norm_w(Hd),
+        lm_head=_q_linear(rng, args.vocab_size, Hd, std, g, b),
+        layers=layers,
+    )
+
+
+class VanillaDecodeOracle:
+    """Batch-1 decode of the vanilla model: ``MotifDecoderLayer`` (``model.py:845-855``) with
+    ``_forward_vanilla`` (486-559) on an ``OracleVanillaKVCache``, the PolyNorm MLP (267-268),
+    final norm and lm_head (858-905); every op rounded to fp16."""
+
+    def __init__(self, args: OracleVanillaArgs, weights: dict):
+        self.args = args
+        self.w = weights
+        self.caches = [OracleVanillaKVCache() for _ in range(args.num_hidden_layers)]
+        self.inv_freq = rope_inv_freq(args.head_dim, args.rope_theta)
+
+    def _lin(self, x, triple):
+        a = self.args
+        return quantized_matmul(x, *triple, group_size=a.group_size, bits=a.bits).astype(np.float16)
+
+    def layer(self, li: int, h: np.ndarray) -> np.ndarray:
+        a = self.args
+        L = self.w["layers"][li]
+        f16 = np.float16
+        d, H, Hk = a.head_dim, a.H, a.Hk
+        cache = self.caches[li]
+        x = rms_norm(h, L["input_norm"], a.rms_norm_eps).astype(f16)
+        qkv = self._lin(x, L["qkv"])
+        qd, kd = 2 * H * d, 2 * Hk * d
+        q = qkv[..., :qd].reshape(1, 1, 2 * H, d).transpose(0, 2, 1, 3)
+        k = qkv[..., qd : qd + kd].reshape(1, 1, 2 * Hk, d).transpose(0, 2, 1, 3)
+        v = qkv[..., qd + kd :].reshape(1, 1, 2 * Hk, d).transpose(0, 2, 1, 3)
+        off = cache.offset
+        q = rope(q, off, inv_freq=self.inv_freq).astype(f16)
+        k = rope(k, off, inv_freq=self.inv_freq).astype(f16)
+        out = vanilla_attention_reference(q, k, v, cache, L["lambda_full"], L["lambda_init"], L["subln"],
+                                          a.attn_rms_norm_eps)
+        out = out.transpose(0, 2, 1, 3).reshape(1, -1)
+        o = self._lin(out, L["o"])
+        h = (h.astype(np.float32) + o.astype(np.float32)).astype(f16)
+        x2 = rms_norm(h, L["post_norm"], a.rms_norm_eps).astype(f16)
+        act = polynorm_mul_reference(self._lin(x2, L["gate"]), self._lin(x2, L["up"]), L["polynorm_w"],
+                                     L["polynorm_b"], 1e-6)
+        dn = self._lin(act, L["down"])
+        return (h.astype(np.float32) + dn.astype(np.float32)).astype(f16)
+
+    def step(self, token: int):
+        """One decode step -> (logits fp16 (V,), argmax token)."""
+        h = self.w["embed"][int(token)][None, :].astype(np.float16)
+        for li in range(self.args.num_hidden_layers):
+            h = self.layer(li, h)
+        hn = rms_norm(h, self.w["final_norm"], self.args.rms_norm_eps).astype(np.float16)
+        logits = self._lin(hn, self.w["lm_head"])[0]
+        return logits, int(np.argmax(logits.astype(np.float32)))
