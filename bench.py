@@ -18,6 +18,8 @@ Also reported in the same line:
   extra.p16k_*  config[2]: decode at a 16000-token context (KV cache filled
                 with synthetic N(0,1)·0.5 rows), q4 and fp16 4-slot caches,
                 with the attention kernels' HBM GB/s.
+  extra.vanilla_2p6b_p3204  config[3] decode: the 2.6B-class vanilla model at a
+                3204-row context (synthetic cache rows), one GPU.
   cpu_baseline  the CPU oracle (numpy restatement of the reference path) on
                 one full-size layer, scaled to a token.
 
@@ -61,6 +63,7 @@ def parse_args():
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--cache", choices=["fp16", "q4", "q8"], default="fp16")
     ap.add_argument("--no-long", action="store_true", help="skip the p16k extras")
+    ap.add_argument("--no-vanilla", action="store_true", help="skip the config[3] 2.6B vanilla extra")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--layers", type=int, default=48, help="(debug) model depth; 48 is the benchmark")
     ap.add_argument("--prompt", type=int, default=164, help="prompt length (164 = config[1])")
@@ -407,6 +410,7 @@ def run_b200(a) -> None:
     ms = max_over_ranks(e0.elapsed_time(e1), world)
     clocks = sampler.stop() if sampler else None
     value = a.steps / (ms / 1e3)
+    launches = model_launches(model) * a.steps
     kv_mid = PROMPT_LEN + a.warmup + a.steps // 2
     bytes_per_step = model.weight_bytes * world + model.kv_bytes_per_token(kv_mid) * world
 
@@ -472,6 +476,41 @@ def run_b200(a) -> None:
             del m
             torch.cuda.empty_cache()
 
+    # ---- config[3]: the 2.6B-class vanilla decoder (one GPU: the vanilla path has no TP) ----
+    if world == 1 and not a.no_vanilla:
+        if model is not None:
+            model._graphs.clear()
+            del model
+            model = None
+            torch.cuda.empty_cache()
+        van = ModelArgs(hidden_size=2048, num_hidden_layers=32, intermediate_size=8192, num_attention_heads=16,
+                        num_key_value_heads=4, num_noise_heads=None, vocab_size=a.vocab)
+        ctx = 3204
+        m = MotifDecoder.random(van, seed=0, cache="fp16", max_seq=ctx + a.warmup + a.steps + 8, device=dev)
+        m.fill_cache_synthetic(ctx, seed=2)
+        m.token.fill_(1)
+        for _ in range(a.warmup):
+            m.step_device()
+        torch.cuda.synchronize()
+        e0.record(st)
+        for _ in range(a.steps):
+            m.step_device()
+        e1.record(st)
+        torch.cuda.synchronize()
+        vms = e0.elapsed_time(e1)
+        vb = m.weight_bytes + m.kv_bytes_per_token(ctx + a.warmup + a.steps // 2)
+        extra["vanilla_2p6b_p3204"] = {
+            "workload": "config[3] decode: 2.6B-class vanilla q4 (32L, H2048, 16 q / 4 kv heads, I8192, V219520), "
+                        "fp16 4-slot cache holding 3204 synthetic N(0,1)*0.5 rows, greedy decode",
+            "tok_s": round(a.steps / (vms / 1e3), 2), "ms_per_step": round(vms / a.steps, 4),
+            "weights_gb": round(m.weight_bytes / 1e9, 3),
+            "step_hbm_gbs": round(vb / (vms / a.steps / 1e3) / 1e9, 1),
+            "kernels_per_step": model_launches(m),
+        }
+        m._graphs.clear()
+        del m
+        torch.cuda.empty_cache()
+
     cpu = None
     if rank == 0 and world == 1 and not a.no_cpu_baseline:
         cpu = cpu_baseline(threads=1)
@@ -487,7 +526,7 @@ def run_b200(a) -> None:
                        "model": "motif-12.7B-class (48L, H4096, 24+8 q heads, 8 kv/slot, I14336, V219520)",
                        "global_batch": 1, "seq_len": PROMPT_LEN, "parallelism": f"tp{world}" if world > 1 else "single",
                        "l2": "inputs larger than L2: 6.85 GB of weights stream from HBM every step"},
-            "e2e": e2e, "gpu_launches": model_launches(model) * a.steps,
+            "e2e": e2e, "gpu_launches": launches,
             "roofline": roofline, "cpu_baseline": cpu, "clocks": clocks, "extra": extra,
         }
         print(json.dumps(line), flush=True)

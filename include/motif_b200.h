@@ -251,7 +251,9 @@ MOTIF_API int motif_rope(int dtype, const void* x, int64_t batch, int64_t heads,
  * mx.quantized_matmul behind nn.QuantizedLinear (every linear of the decoder,
  * model.py:437-442, 262-264, 894; fused qkv 1017-1079). Fast path: bits 4,
  * group 64, fp16, k % 128 == 0 (persistent stream-K GEMV; rows of x run one
- * after another); other bits/groups/dtypes take a CUDA-core path. The
+ * after another); m >= 128 rows with n % 128 == 0 and k % 512 == 0 take the
+ * tensor-core GEMM (motif_q4_gemm); other bits/groups/dtypes take a
+ * CUDA-core path. The
  * workspace (motif_quantized_linear_workspace_bytes) must be zero-filled
  * before its first use; the kernel leaves it zeroed. */
 MOTIF_API size_t motif_quantized_linear_workspace_bytes(int64_t m, int64_t n, int64_t k, int bits,
@@ -260,6 +262,19 @@ MOTIF_API int motif_quantized_linear(int dtype, int bits, int group_size, const 
                            int64_t k, const uint32_t* w, const void* scales, const void* biases,
                            int64_t n, void* y, void* workspace, size_t workspace_bytes,
                            void* stream);
+
+/* Prompt-length q4 linear on the tcgen05 tensor cores: y (m, n) = x (m, k) ·
+ * dequant(W)ᵀ [+ residual], fp16 x / y / residual row-major, W q4 group 64 in
+ * the nn.QuantizedLinear layout (reference: mx.quantized_matmul behind every
+ * nn.QuantizedLinear of a prompt forward, model.py:1047-1079). Weight tiles
+ * are dequantized to fp16 in shared memory and multiplied with fp32
+ * accumulation in tensor memory; y is rounded to fp16 once, then (with
+ * residual) added in fp16 like the reference's h + linear(x). Needs
+ * m >= 128, n % 128 == 0, k % 512 == 0 and 16-byte aligned operands. err
+ * (optional, device int): set to 1 if a pipeline wait timed out. */
+MOTIF_API int motif_q4_gemm(const void* x, int64_t m, int64_t k, const uint32_t* w, const void* scales,
+                            const void* biases, int64_t n, void* y, const void* residual, int* err,
+                            void* stream);
 
 /* Fused decode linear: the q4 GEMV of motif_quantized_linear (bits 4, group 64,
  * fp16, one input row) with the input vector built in its prologue and an

@@ -1121,6 +1121,18 @@ int launch_q4(LinArgs& a, void* workspace, size_t ws_bytes, cudaStream_t st) {
 bool al16(const void* p) { return p == nullptr || (reinterpret_cast<uintptr_t>(p) % 16) == 0; }
 
 }  // namespace
+
+bool q4_gemm_supported(int dtype, int bits, int group_size, int64_t m, int64_t n, int64_t k, const void* x,
+                       const void* w, const void* sc, const void* bi, const void* y);
+int q4_gemm(const void* x, int64_t m, int64_t k, const uint32_t* w, const void* scales, const void* biases, int64_t n,
+            void* y, const void* residual, int* err, cudaStream_t st);
+
+bool encode_tma_rows(CUtensorMap* m, const void* base, uint64_t inner_bytes, uint64_t rows, uint32_t box_inner,
+                     uint32_t box_rows, bool swizzle128) {
+  return encode_rows(m, base, inner_bytes, rows, box_inner, box_rows,
+                     swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE);
+}
+
 }  // namespace motif
 
 using namespace motif;
@@ -1146,6 +1158,9 @@ int motif_quantized_linear(int dtype, int bits, int group_size, const void* x, i
                 "quantized_linear: m=%lld n=%lld k=%lld", (long long)m, (long long)n, (long long)k);
   if (m == 0) return MOTIF_OK;
   cudaStream_t st = as_stream(stream);
+  // prompt-length inputs: the tcgen05 GEMM (dequantized weight tiles on the tensor cores)
+  if (q4_gemm_supported(dtype, bits, group_size, m, n, k, x, w, scales, biases, y))
+    return q4_gemm(x, m, k, w, scales, biases, n, y, nullptr, nullptr, st);
   if (fast_path_ok(dtype, bits, group_size, k, x, w, scales, biases)) {
     for (int64_t i = 0; i < m; ++i) {
       LinArgs a{};

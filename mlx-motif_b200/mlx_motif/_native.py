@@ -103,6 +103,7 @@ SIGNATURES = {
         _I,
         [_P, _P, _KV, _P, _F, _L, _L, _P, _P, _L, _F, _F, _P, _P, _S, _P],
     ),
+    "motif_q4_gemm": (_I, [_P, _L, _L, _P, _P, _P, _L, _P, _P, _P, _P]),
     "motif_vanilla_decode_step": (
         _I,
         [_P, _P, _KV, _P, _F, _L, _L, _P, _P, _F, _F, _P, _P, _S, _P],
