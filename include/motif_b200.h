@@ -239,6 +239,17 @@ MOTIF_API int motif_rope_qkv_append(const void* qkv, const float* inv_freq, int6
                           const motif_kv4_slots* cache, const int32_t* pos_dev, void* q_out,
                           void* stream);
 
+/* The same for a block of `seq` prompt rows: qkv (seq, q_heads + 4*kv2 heads
+ * of 128), row s at position offset + s (offset = *offset_dev when
+ * offset_dev is non-NULL); q is written head-major, q_out (q_heads, seq, 128)
+ * (the layout motif_prefill_attention reads); k/v rows go to cache rows
+ * [offset, offset + seq), quantized per row for a q4/q8 cache (bit-identical
+ * to appending the rows one by one). Reference: the prompt branch of
+ * _forward_grouped / _forward_vanilla (model.py:580-657, 486-521). */
+MOTIF_API int motif_rope_qkv_append_rows(const void* qkv, int64_t seq, const float* inv_freq, int64_t q_heads,
+                                         const motif_kv4_slots* cache, int64_t offset, const int32_t* offset_dev,
+                                         void* q_out, void* stream);
+
 /* Non-traditional RoPE on x (B, H, S, D) at positions offset + s (mlx-lm
  * initialize_rope, traditional=False, as used at model.py:414-420,589-594). */
 MOTIF_API int motif_rope(int dtype, const void* x, int64_t batch, int64_t heads, int64_t seq, int64_t dim,
@@ -275,6 +286,35 @@ MOTIF_API int motif_quantized_linear(int dtype, int bits, int group_size, const 
 MOTIF_API int motif_q4_gemm(const void* x, int64_t m, int64_t k, const uint32_t* w, const void* scales,
                             const void* biases, int64_t n, void* y, const void* residual, int* err,
                             void* stream);
+
+/* ---- prompt (prefill) attention -------------------------------------------
+ * Causal attention of `seq` prompt rows at positions [offset, offset + seq)
+ * over cache rows [0, offset + seq) of an fp16 4-slot cache (the rows already
+ * appended), on the tcgen05 tensor cores with fp32 accumulation. Per query
+ * head: o = softmax(q·kᵀ·scale, causal)·[v1 | v2] (256 wide), with
+ *   mode 0 (grouped): q_heads = kv2*(gr+1) origin-first; origin head h reads
+ *     k1 of group h/gr, noise head q_origin+g reads k2 of group g — the four
+ *     per-slab SDPAs of _forward_grouped's prompt path (model.py:769-807);
+ *   mode 1 (vanilla): q_heads = 2*kv2*gr (gr = n_rep), q1/q2 interleaved;
+ *     head h reads k1 (even h) or k2 (odd h) of kv head (h/2)/gr — the
+ *     per-slab SDPAs of _forward_vanilla (model.py:486-559).
+ * q: head-major (q_heads, seq, 128) fp16; out: (seq, q_heads, 256) fp16, each
+ * SDPA output rounded to fp16 as the reference's are. err (optional device
+ * int) is set to 1 if a pipeline wait timed out. */
+MOTIF_API int motif_prefill_attention(const void* q, int64_t seq, int64_t q_heads, const motif_kv4_slots* cache,
+                                      int64_t offset, int mode, int64_t gr, float scale, void* out, int* err,
+                                      void* stream);
+
+/* The differential combine over prompt rows: o (seq, q_heads, 256) from
+ * motif_prefill_attention -> y (seq, out_heads, 256), the o_proj input.
+ * mode 0: gda_post_split (kernels/gda.py:223-282) of each group's gr origin
+ * heads against its noise head; lambda_len 1, groups or groups*gr.
+ * mode 1: the vanilla (o1 - lambda*o2), SubLN, (1 - lambda_init) of each
+ * q1/q2 pair with fp16 rounding after each op (model.py:553-557);
+ * lambda_len 1. */
+MOTIF_API int motif_prefill_post(const void* o, int64_t seq, int64_t q_heads, int mode, int64_t groups, int64_t gr,
+                                 const void* subln_w, const float* lambda_full, int64_t lambda_len,
+                                 float lambda_init, float eps, void* y, void* stream);
 
 /* Fused decode linear: the q4 GEMV of motif_quantized_linear (bits 4, group 64,
  * fp16, one input row) with the input vector built in its prologue and an

@@ -171,22 +171,25 @@ __global__ void rope_kernel(const T* __restrict__ x, int64_t rows, int S, int D,
   y[row * D + k + half] = from_f<T>(__fadd_rn(__fmul_rn(x1, sn), __fmul_rn(x2, cs)));
 }
 
-// ---- decode prologue: RoPE(q), RoPE(k), 4-slot append ------------------------
-// One CTA per head of the fused qkv row: [q heads | k heads (k1,k2 pairs) |
-// v heads (v1,v2 pairs)]. D threads per CTA, thread c owns channel c.
+// ---- RoPE(q), RoPE(k), 4-slot append ------------------------------------------
+// One CTA per (head, row) of the fused qkv rows: [q heads | k heads (k1,k2 pairs) |
+// v heads (v1,v2 pairs)]. D threads per CTA, thread c owns channel c. Row s sits at
+// position pos0 + s (pos0 = *pos_dev when given); q is written head-major (q_heads, seq, D),
+// which for one row is the plain (q_heads, D) of the decode step.
 template <int D, int LPG>
 __global__ void rope_qkv_append_kernel(const __half* __restrict__ qkv,
                                        const float* __restrict__ inv_freq, int q_heads,
                                        int kv2, motif_kv4_slots cache,
-                                       const int32_t* __restrict__ pos_dev,
-                                       __half* __restrict__ q_out) {
+                                       const int32_t* __restrict__ pos_dev, int64_t pos_host, int seq,
+                                       int64_t qkv_stride, __half* __restrict__ q_out) {
   __shared__ float vals[D];
   pdl_trigger();
   const int head = blockIdx.x;
+  const int srow = blockIdx.y;
   const int c = threadIdx.x;
   const int half = D / 2;
-  const int pos = *pos_dev;
-  const __half* src = qkv + (int64_t)head * D;
+  const int pos = (pos_dev ? *pos_dev : (int)pos_host) + srow;
+  const __half* src = qkv + srow * qkv_stride + (int64_t)head * D;
   const bool is_q = head < q_heads;
   const bool is_k = !is_q && head < q_heads + 2 * kv2;
   float v;
@@ -197,7 +200,7 @@ __global__ void rope_qkv_append_kernel(const __half* __restrict__ qkv,
   }
   const __half hv = __float2half_rn(v);
   if (is_q) {
-    q_out[(int64_t)head * D + c] = hv;
+    q_out[((int64_t)head * seq + srow) * D + c] = hv;
     return;
   }
   const int kvh = is_k ? head - q_heads : head - q_heads - 2 * kv2;
@@ -362,33 +365,53 @@ int motif_rope(int dtype, const void* x, int64_t batch, int64_t heads, int64_t s
   return check_launch("rope");
 }
 
-int motif_rope_qkv_append(const void* qkv, const float* inv_freq, int64_t q_heads,
-                          const motif_kv4_slots* cache, const int32_t* pos_dev, void* q_out,
-                          void* stream) {
-  MOTIF_REQUIRE(qkv && inv_freq && cache && pos_dev && q_out, MOTIF_ERR_NULL, "rope_qkv_append: null pointer");
+static int rope_qkv_append_launch(const void* qkv, int64_t seq, const float* inv_freq, int64_t q_heads,
+                                  const motif_kv4_slots* cache, int64_t pos_host, const int32_t* pos_dev,
+                                  void* q_out, void* stream) {
+  MOTIF_REQUIRE(qkv && inv_freq && cache && q_out, MOTIF_ERR_NULL, "rope_qkv_append: null pointer");
   const motif_kv4_slots& c = *cache;
   MOTIF_REQUIRE(c.batch == 1 && c.head_dim == 128, MOTIF_ERR_BAD_CONTRACT,
                 "rope_qkv_append: batch 1 and head_dim 128 only (got %lld, %lld)", (long long)c.batch,
                 (long long)c.head_dim);
+  MOTIF_REQUIRE(seq >= 1 && seq < 65536 && q_heads >= 1, MOTIF_ERR_BAD_SHAPE, "rope_qkv_append: seq=%lld",
+                (long long)seq);
+  MOTIF_REQUIRE(pos_dev || (pos_host >= 0 && pos_host + seq <= c.capacity), MOTIF_ERR_BAD_SHAPE,
+                "rope_qkv_append: rows [%lld, %lld) outside capacity %lld", (long long)pos_host,
+                (long long)(pos_host + seq), (long long)c.capacity);
   for (int i = 0; i < 4; ++i) MOTIF_REQUIRE(c.data[i], MOTIF_ERR_NULL, "rope_qkv_append: slot %d null", i);
-  const int blocks = (int)(q_heads + 4 * c.heads);
+  const dim3 grid((unsigned)(q_heads + 4 * c.heads), (unsigned)seq);
+  const int64_t stride = (q_heads + 4 * c.heads) * 128;
   cudaStream_t st = as_stream(stream);
   auto qkv_p = static_cast<const __half*>(qkv);
   auto q_p = static_cast<__half*>(q_out);
+  const int qh = (int)q_heads, kv2 = (int)c.heads, S = (int)seq;
   if (c.bits == 16) {
-    rope_qkv_append_kernel<128, 8><<<blocks, 128, 0, st>>>(qkv_p, inv_freq, (int)q_heads, (int)c.heads, c, pos_dev, q_p);
+    rope_qkv_append_kernel<128, 8><<<grid, 128, 0, st>>>(qkv_p, inv_freq, qh, kv2, c, pos_dev, pos_host, S, stride, q_p);
   } else {
     MOTIF_REQUIRE(c.bits == 4 || c.bits == 8, MOTIF_ERR_DTYPE, "rope_qkv_append: bits=%d", c.bits);
     for (int i = 0; i < 4; ++i)
       MOTIF_REQUIRE(c.scales[i] && c.biases[i], MOTIF_ERR_NULL, "rope_qkv_append: slot %d scales/biases null", i);
     switch (c.group_size) {
-      case 32: rope_qkv_append_kernel<128, 4><<<blocks, 128, 0, st>>>(qkv_p, inv_freq, (int)q_heads, (int)c.heads, c, pos_dev, q_p); break;
-      case 64: rope_qkv_append_kernel<128, 8><<<blocks, 128, 0, st>>>(qkv_p, inv_freq, (int)q_heads, (int)c.heads, c, pos_dev, q_p); break;
-      case 128: rope_qkv_append_kernel<128, 16><<<blocks, 128, 0, st>>>(qkv_p, inv_freq, (int)q_heads, (int)c.heads, c, pos_dev, q_p); break;
+      case 32: rope_qkv_append_kernel<128, 4><<<grid, 128, 0, st>>>(qkv_p, inv_freq, qh, kv2, c, pos_dev, pos_host, S, stride, q_p); break;
+      case 64: rope_qkv_append_kernel<128, 8><<<grid, 128, 0, st>>>(qkv_p, inv_freq, qh, kv2, c, pos_dev, pos_host, S, stride, q_p); break;
+      case 128: rope_qkv_append_kernel<128, 16><<<grid, 128, 0, st>>>(qkv_p, inv_freq, qh, kv2, c, pos_dev, pos_host, S, stride, q_p); break;
       default: return fail(MOTIF_ERR_BAD_CONTRACT, "rope_qkv_append: group_size %d", c.group_size);
     }
   }
   return check_launch("rope_qkv_append");
+}
+
+int motif_rope_qkv_append(const void* qkv, const float* inv_freq, int64_t q_heads,
+                          const motif_kv4_slots* cache, const int32_t* pos_dev, void* q_out,
+                          void* stream) {
+  MOTIF_REQUIRE(pos_dev, MOTIF_ERR_NULL, "rope_qkv_append: null pointer");
+  return rope_qkv_append_launch(qkv, 1, inv_freq, q_heads, cache, 0, pos_dev, q_out, stream);
+}
+
+int motif_rope_qkv_append_rows(const void* qkv, int64_t seq, const float* inv_freq, int64_t q_heads,
+                               const motif_kv4_slots* cache, int64_t offset, const int32_t* offset_dev,
+                               void* q_out, void* stream) {
+  return rope_qkv_append_launch(qkv, seq, inv_freq, q_heads, cache, offset, offset_dev, q_out, stream);
 }
 
 }  // extern "C"

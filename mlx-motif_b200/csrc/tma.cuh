@@ -112,6 +112,17 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
         "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
       : "r"(taddr));
 }
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+      "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};\n" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+      "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]),
+      "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]),
+      "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+}
+__device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;\n" ::: "memory"); }
 __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory"); }
 
 // Shared-memory matrix descriptor of a K-major tile in the 128-byte swizzle layout: rows of
@@ -127,10 +138,25 @@ __device__ __forceinline__ uint64_t desc_kmajor_sw128(uint32_t saddr) {
   return d;
 }
 
-// Instruction descriptor of kind::f16 with fp16 A and B (both K-major), fp32 accumulator.
-__host__ __device__ constexpr uint32_t idesc_f16_f32(int M, int N) {
+// Descriptor of an MN-major tile in the 128-byte swizzle layout: each K row holds 64 fp16 of
+// the M/N dimension in 128 bytes, 8-row atoms are `sbo` bytes apart along K, and successive
+// 64-element chunks of M/N are `lbo` bytes apart. Advancing K by 8·j rows adds j·sbo bytes.
+__device__ __forceinline__ uint64_t desc_mnmajor_sw128(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr >> 4) & 0x3FFF);
+  d |= (uint64_t)((lbo >> 4) & 0x3FFF) << 16;
+  d |= (uint64_t)((sbo >> 4) & 0x3FFF) << 32;
+  d |= (uint64_t)1 << 46;
+  d |= (uint64_t)2 << 61;
+  return d;
+}
+
+// Instruction descriptor of kind::f16 with fp16 A and B, fp32 accumulator; A K-major, B K-major
+// (b_mn_major false) or MN-major.
+__host__ __device__ constexpr uint32_t idesc_f16_f32(int M, int N, bool b_mn_major = false) {
   return (1u << 4)                           // D format f32
          | (0u << 7) | (0u << 10)            // A, B format f16
+         | ((b_mn_major ? 1u : 0u) << 16)    // B major-ness
          | ((uint32_t)(N >> 3) << 17)        // N / 8
          | ((uint32_t)(M >> 4) << 24);       // M / 16
 }

@@ -35,6 +35,8 @@ __all__ = [
     "gda_post_split_reference",
     "gda_post_reference",
     "sdpa_dual_v_reference",
+    "causal_gqa_sdpa",
+    "grouped_prompt_attention_reference",
     "sdpa_dual_v_q4_reference",
     "dequantize",
     "quantize",
@@ -170,6 +172,43 @@ def _sdpa(q, k, v, scale):
     p = np.exp(s)
     p = p / p.sum(axis=-1, keepdims=True)
     return np.einsum("bhsn,bhnd->bhsd", p, v)
+
+
+def _sdpa_causal(q, k, v, scale, offset):
+    """``mx.fast.scaled_dot_product_attention`` with mlx-lm's causal mask for a prompt block
+    (``create_causal_mask``: query i sits at position offset + i and sees keys 0 .. offset + i),
+    float64; q (B,H,S,D), k/v (B,H,N,D)."""
+    S, N = q.shape[2], k.shape[2]
+    s = np.einsum("bhsd,bhnd->bhsn", q, k) * scale
+    mask = np.arange(N)[None, :] <= (offset + np.arange(S))[:, None]
+    s = np.where(mask[None, None], s, -np.inf)
+    s = s - s.max(axis=-1, keepdims=True)
+    p = np.exp(s)
+    p = p / p.sum(axis=-1, keepdims=True)
+    return np.einsum("bhsn,bhnd->bhsd", p, v)
+
+
+def causal_gqa_sdpa(q, k, v, scale, offset):
+    """Native-GQA causal SDPA (q head i reads kv head i // (Hq // Hkv)), float64."""
+    qf, kf, vf = _f64(q), _f64(k), _f64(v)
+    rep = qf.shape[1] // kf.shape[1]
+    if rep > 1:
+        kf = np.repeat(kf, rep, axis=1)
+        vf = np.repeat(vf, rep, axis=1)
+    return _sdpa_causal(qf, kf, vf, scale, offset)
+
+
+def grouped_prompt_attention_reference(q_origin, q_noise, k1, k2, v1, v2, scale, offset):
+    """The prompt branch of ``_forward_grouped`` (``model.py:769-807``): four per-slab causal
+    SDPAs, each rounded to fp16 (MLX materialises fp16 arrays), concatenated on the channel
+    axis: attn_origin = [SDPA(q1,k1,v1) | SDPA(q1,k1,v2)], attn_noise the same with (q2, k2).
+    q_* (B, H, S, D); k/v (B, G, N, D) holding the cache rows [0, offset + S)."""
+    f16 = np.float16
+
+    def pair(q, k):
+        return np.concatenate([causal_gqa_sdpa(q, k, v, scale, offset).astype(f16) for v in (v1, v2)], axis=-1)
+
+    return pair(q_origin, k1), pair(q_noise, k2)
 
 
 def sdpa_dual_v_reference(q, k, v1, v2, scale, kv_len=None):
@@ -790,13 +829,10 @@ class OracleVanillaKVCache:
 
 
 def _gqa_sdpa(q, k, v, scale):
-    """``mx.fast.scaled_dot_product_attention`` with native GQA: q head i reads kv head i // n_rep."""
-    qf, kf, vf = _f64(q), _f64(k), _f64(v)
-    n_rep = qf.shape[1] // kf.shape[1]
-    if n_rep > 1:
-        kf = np.repeat(kf, n_rep, axis=1)
-        vf = np.repeat(vf, n_rep, axis=1)
-    return _sdpa(qf, kf, vf, scale)
+    """``mx.fast.scaled_dot_product_attention`` with native GQA: q head i reads kv head i // n_rep;
+    a block of S > 1 queries (the last S cache positions) gets the causal mask."""
+    S, N = np.asarray(q).shape[2], np.asarray(k).shape[2]
+    return causal_gqa_sdpa(q, k, v, scale, N - S)
 
 
 def vanilla_attention_reference(q, k, v_paired, cache, lam, lam_init, subln_w, eps=1e-5, kv_dtype=np.float16):

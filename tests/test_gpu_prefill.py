@@ -84,3 +84,120 @@ def test_q4_gemm_rejects_outside_contract(cuda):
     assert N_.lib.motif_q4_gemm(p, 64, 512, p, p, p, 256, p, None, None, N_.stream()) == N_.ERR_BAD_CONTRACT
     assert N_.lib.motif_q4_gemm(p, 128, 576, p, p, p, 256, p, None, None, N_.stream()) == N_.ERR_BAD_CONTRACT
     assert N_.lib.motif_q4_gemm(p, 128, 512, p, p, p, 200, p, None, None, N_.stream()) == N_.ERR_BAD_CONTRACT
+
+
+# ---------------------------------------------------------------- batched RoPE + append
+@pytest.mark.parametrize("bits", [16, 4])
+def test_rope_qkv_append_rows_equals_row_by_row(cuda, bits):
+    """motif_rope_qkv_append_rows over a block of rows == motif_rope_qkv_append one row at a time,
+    bit for bit: q (head-major) and every cache slot (codes, scales and biases for q4)."""
+    from mlx_motif import _native as N_
+    from mlx_motif.cache import MotifGroupedKVCache, MotifGroupedQuantizedKVCache
+    from mlx_motif.model import rope_inv_freq
+
+    G, qh, d, S, off, cap = 2, 8, 128, 37, 5, 128
+    rng = np.random.default_rng(bits)
+    qkv = up(rounded(rng.standard_normal((S, (qh + 4 * G) * d)), "float16"))
+    inv = rope_inv_freq(d, 10000.0, cuda)
+
+    def make():
+        c = MotifGroupedKVCache(max_size=cap) if bits == 16 else MotifGroupedQuantizedKVCache(64, 4, max_size=cap)
+        c._grow(1, G, 1, d, torch.float16, cuda)
+        return c
+
+    ca, cb = make(), make()
+    qa = torch.empty((qh, S, d), dtype=torch.float16, device=cuda)
+    N_.check(N_.lib.motif_rope_qkv_append_rows(qkv.data_ptr(), S, inv.data_ptr(), qh, ca.slots_struct(), off, None,
+                                               qa.data_ptr(), N_.stream()), "rope rows")
+    qb = torch.empty((qh, S, d), dtype=torch.float16, device=cuda)
+    row_q = torch.empty((qh, d), dtype=torch.float16, device=cuda)
+    for s in range(S):
+        pos = torch.tensor([off + s], dtype=torch.int32, device=cuda)
+        N_.check(N_.lib.motif_rope_qkv_append(qkv[s].data_ptr(), inv.data_ptr(), qh, cb.slots_struct(),
+                                              pos.data_ptr(), row_q.data_ptr(), N_.stream()))
+        qb[:, s].copy_(row_q)
+    torch.cuda.synchronize()
+    assert torch.equal(qa, qb)
+    for n in ("k1", "k2", "v1", "v2"):
+        a, b = getattr(ca, n), getattr(cb, n)
+        for x, y in (zip(a, b) if isinstance(a, tuple) else [(a, b)]):
+            assert torch.equal(x, y), f"slot {n} differs"
+
+
+# ---------------------------------------------------------------- prompt attention
+def _filled_cache(rng, G, n, cap, dev):
+    from mlx_motif.cache import MotifGroupedKVCache
+
+    c = MotifGroupedKVCache(max_size=cap)
+    rows = [rounded(rng.standard_normal((1, G, n, 128)) * 0.5, "float16") for _ in range(4)]
+    c.update_and_fetch_4(*(up(r) for r in rows))
+    return c, rows
+
+
+@pytest.mark.parametrize("S,off", [(1, 0), (100, 0), (300, 0), (130, 77), (64, 1000)])
+def test_prefill_attention_grouped_matches_oracle(cuda, S, off):
+    """motif_prefill_attention (tcgen05, mode 0) == the four per-slab causal SDPAs of
+    _forward_grouped's prompt branch (model.py:769-807), and motif_prefill_post ==
+    gda_post_split over every row."""
+    from mlx_motif import _native as N_
+
+    G, gr, d = 2, 3, 128
+    qh = G * (gr + 1)
+    rng = np.random.default_rng(S + off)
+    cache, (k1, k2, v1, v2) = _filled_cache(rng, G, off + S, 2048, cuda)
+    q = rounded(rng.standard_normal((qh, S, d)), "float16")  # head-major, origin-first
+    tq = up(q)
+    o = torch.full((S, qh, 2 * d), float("nan"), dtype=torch.float16, device=cuda)
+    err = torch.zeros(1, dtype=torch.int32, device=cuda)
+    N_.check(N_.lib.motif_prefill_attention(tq.data_ptr(), S, qh, cache.slots_struct(), off, 0, gr, d ** -0.5,
+                                            o.data_ptr(), err.data_ptr(), N_.stream()), "prefill_attention")
+    subln = rounded(1 + 0.02 * rng.standard_normal(2 * d), "float16")
+    lam = np.array([0.37], np.float32)
+    y = torch.empty((S, G * gr, 2 * d), dtype=torch.float16, device=cuda)
+    t_sub, t_lam = up(subln), torch.tensor(lam, device=cuda)
+    N_.check(N_.lib.motif_prefill_post(o.data_ptr(), S, qh, 0, G, gr, t_sub.data_ptr(), t_lam.data_ptr(), 1, 0.8,
+                                       1e-5, y.data_ptr(), N_.stream()), "prefill_post")
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    ao, an = O.grouped_prompt_attention_reference(q[None, : G * gr], q[None, G * gr:], k1, k2, v1, v2, d ** -0.5, off)
+    got = down(o).transpose(1, 0, 2)[None]  # (1, qh, S, 256)
+    assert_close(got[:, : G * gr], ao.astype(np.float64), "float16", what="origin heads")
+    assert_close(got[:, G * gr:], an.astype(np.float64), "float16", what="noise heads")
+    # the post on the kernel's own attention rows
+    ref = O.gda_post_split_reference(got[:, : G * gr], got[:, G * gr:], subln, lam, 0.8, gr, 1e-5)
+    assert_close(down(y).transpose(1, 0, 2)[None], ref.astype(np.float16).astype(np.float64), "float16",
+                 what="gda post rows")
+
+
+@pytest.mark.parametrize("n_rep,S,off", [(4, 200, 0), (4, 129, 300), (2, 64, 0), (1, 257, 5)])
+def test_prefill_attention_vanilla_matches_oracle(cuda, n_rep, S, off):
+    """mode 1 + the vanilla combine == _forward_vanilla's prompt attention (model.py:486-559):
+    four per-slab causal SDPAs with native GQA, (o1 − λ·o2), SubLN, (1 − λ_init)."""
+    from mlx_motif import _native as N_
+
+    Hk, d = 2, 128
+    H = Hk * n_rep
+    qh = 2 * H
+    rng = np.random.default_rng(10 * n_rep + S)
+    cache, (k1, k2, va, vb) = _filled_cache(rng, Hk, off + S, 1024, cuda)
+    q = rounded(rng.standard_normal((qh, S, d)), "float16")
+    tq = up(q)
+    o = torch.empty((S, qh, 2 * d), dtype=torch.float16, device=cuda)
+    N_.check(N_.lib.motif_prefill_attention(tq.data_ptr(), S, qh, cache.slots_struct(), off, 1, n_rep, d ** -0.5,
+                                            o.data_ptr(), None, N_.stream()), "prefill_attention")
+    subln = rounded(1 + 0.02 * rng.standard_normal(2 * d), "float16")
+    lam, lam_init = np.array([0.41], np.float32), 0.35
+    y = torch.empty((S, H, 2 * d), dtype=torch.float16, device=cuda)
+    N_.check(N_.lib.motif_prefill_post(o.data_ptr(), S, qh, 1, Hk, n_rep, up(subln).data_ptr(),
+                                       torch.tensor(lam, device=cuda).data_ptr(), 1, lam_init, 1e-5, y.data_ptr(),
+                                       N_.stream()), "prefill_post")
+    torch.cuda.synchronize()
+    # oracle: keys in stripe order, values in the projection's paired order, the new rows last
+    K = np.stack([k1, k2], axis=2).reshape(1, 2 * Hk, off + S, d)
+    V_paired = np.concatenate([va, vb], axis=1)[:, O.vanilla_v_slab_to_paired_perm(Hk)]
+    oc = O.OracleVanillaKVCache()
+    if off:
+        oc.update_and_fetch(K[:, :, :off].astype(np.float16),
+                            np.concatenate([va, vb], axis=1)[:, :, :off].astype(np.float16))
+    ref = O.vanilla_attention_reference(q[None], K[:, :, off:], V_paired[:, :, off:], oc, lam, lam_init, subln, 1e-5)
+    assert_close(down(y), ref[0].transpose(1, 0, 2).astype(np.float64), "float16", what="vanilla prompt attention")
