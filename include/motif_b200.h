@@ -428,6 +428,11 @@ MOTIF_API int motif_add_rms_norm(int dtype, void* h, const void* delta, const vo
 /* h = table[*token_dev] (nn.Embedding, model.py:862/872), y = rms_norm(h) * w. */
 MOTIF_API int motif_embed_rms_norm(int dtype, const int32_t* token_dev, const void* table, int64_t vocab,
                          int64_t dim, const void* w, float eps, void* h, void* y, void* stream);
+/* The same for a block of prompt rows: h (rows, dim) = table[tokens_dev[r]],
+ * y = rms_norm(h) * w (the prompt forward's embedding and first input norm). */
+MOTIF_API int motif_embed_rms_norm_rows(int dtype, const int32_t* tokens_dev, int64_t rows, const void* table,
+                                        int64_t vocab, int64_t dim, const void* w, float eps, void* h, void* y,
+                                        void* stream);
 /* Greedy sampler: first index of the maximum of logits (n,) -> *out_index
  * (argmax at temperature 0 in mlx_lm generate_step). */
 MOTIF_API size_t motif_argmax_workspace_bytes(int64_t n);

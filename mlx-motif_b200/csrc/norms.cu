@@ -333,6 +333,16 @@ int motif_embed_rms_norm(int dtype, const int32_t* token_dev, const void* table,
   return MOTIF_OK;
 }
 
+int motif_embed_rms_norm_rows(int dtype, const int32_t* tokens_dev, int64_t rows, const void* table, int64_t vocab,
+                              int64_t dim, const void* w, float eps, void* h, void* y, void* stream) {
+  MOTIF_REQUIRE(tokens_dev && table && w && h && y, MOTIF_ERR_NULL, "embed_rms_norm_rows: null pointer");
+  MOTIF_REQUIRE(rows >= 0 && rows < (1ll << 31) && vocab > 0 && dim > 0 && dim < (1ll << 31), MOTIF_ERR_BAD_SHAPE,
+                "embed_rms_norm_rows: bad shape");
+  if (rows == 0) return MOTIF_OK;
+  MOTIF_DISPATCH_FLOAT(dtype, T, return launch_rms<T>(2, table, h, nullptr, tokens_dev, vocab, w, eps, rows, dim, y, as_stream(stream)));
+  return MOTIF_OK;
+}
+
 static int gda_common(int dtype, const void* o_base, int64_t o_bstride, const void* n_base,
                       int64_t n_bstride, const void* subln_w, const float* lam, int64_t lam_len,
                       float lambda_init, int64_t B, int64_t q_groups, int64_t gr, int64_t S,

@@ -708,12 +708,137 @@ class MotifDecoder:
         self._launch_step(with_head)
         self._bump_host()
 
-    def prefill(self, ids) -> None:
-        """Feed prompt tokens through the decode path (causal, one position at a time)."""
+    # Row blocks of at least this many prompt rows go through the tensor-core prefill.
+    min_block_rows = 128
+
+    def prefill(self, ids, chunk: int | None = None, batched: bool | None = None) -> None:
+        """Ingest a prompt. All rows but the last run as blocks of up to ``chunk`` rows
+        (default 2048, mlx-lm's prefill step) through the tensor-core prompt path (q4 GEMMs,
+        causal prompt attention); the last token, and a remainder shorter than
+        ``min_block_rows``, take the decode step, which also yields the first greedy token.
+        ``batched=False`` (or MOTIF_BATCHED_PREFILL=0, or tensor parallelism) runs every row
+        through the decode step."""
         ids_d = torch.as_tensor(ids, dtype=torch.int32).reshape(-1).to(self.device)
-        for i in range(ids_d.numel()):
-            self.token.copy_(ids_d[i : i + 1])
-            self.step_device(with_head=(i == ids_d.numel() - 1))
+        n = ids_d.numel()
+        if batched is None:
+            batched = os.environ.get("MOTIF_BATCHED_PREFILL", "1") != "0"
+        batched = batched and self.tp_group is None and self._block_ok()
+        chunk = chunk or 2048
+        i = 0
+        if batched:
+            while n - 1 - i >= self.min_block_rows:
+                S = min(chunk, n - 1 - i)
+                self._prefill_block(ids_d[i : i + S])
+                i += S
+        for j in range(i, n):
+            self.token.copy_(ids_d[j : j + 1])
+            self.step_device(with_head=(j == n - 1))
+
+    def _block_ok(self) -> bool:
+        """The prompt path's contracts: q4 GEMM shapes (k % 512, n % 128) and head_dim 128."""
+        lins = [L[k] for L in self.layers for k in ("qkv", "o", "gate_up", "down")]
+        return self.d == 128 and all(ql.in_dim % 512 == 0 and ql.out_dim % 128 == 0 for ql in lins)
+
+    def _block_buffers(self, S: int) -> dict:
+        b = getattr(self, "_blk", None)
+        if b is not None and b["S"] >= S:
+            return b
+        f16, dev, d = torch.float16, self.device, self.d
+        L0 = self.layers[0]
+        b = dict(
+            S=S,
+            h=torch.empty((S, self.H), dtype=f16, device=dev),
+            x=torch.empty((S, self.H), dtype=f16, device=dev),
+            qkv=torch.empty((S, L0["qkv"].out_dim), dtype=f16, device=dev),
+            q=torch.empty((self.q_heads, S, d), dtype=f16, device=dev),
+            o=torch.empty((S, self.q_heads, 2 * d), dtype=f16, device=dev),
+            attn=torch.empty((S, self.q_origin * 2 * d), dtype=f16, device=dev),
+            gu=torch.empty((S, 2 * self.inter), dtype=f16, device=dev),
+            act=torch.empty((S, self.inter), dtype=f16, device=dev),
+            err=torch.zeros(1, dtype=torch.int32, device=dev),
+        )
+        self._blk = b
+        return b
+
+    def _attn_slots(self, li: int, rows: int):
+        """The fp16 4-slot view the prompt attention reads: the cache itself, or (q4/q8 cache) its
+        rows [0, rows) dequantized into a scratch fp16 cache — the reference's prompt path also
+        attends over the dequantized fetch (cache.py:448-465)."""
+        if self.cache_kind == "fp16":
+            return self._slots[li]
+        from .cache import _slots_struct
+
+        c = self.caches[li]
+        G, d = self.kv_heads, self.d
+        cap = ((rows + 63) // 64) * 64
+        sc = getattr(self, "_deq_scratch", None)
+        if sc is None or sc[0].shape[2] < cap:
+            sc = [torch.zeros((1, G, cap, d), dtype=torch.float16, device=self.device) for _ in range(4)]
+            self._deq_scratch = sc
+        cap = sc[0].shape[2]
+        st = stream(self.device)
+        el = 32 // c.bits
+        for i, slot in enumerate((c.k1, c.k2, c.v1, c.v2)):
+            data, scales, biases = slot
+            ccap = data.shape[2]
+            for g in range(G):
+                check(lib.motif_dequantize(0, c.bits, c.group_size, data.data_ptr() + g * ccap * (d // el) * 4,
+                                           scales.data_ptr() + g * ccap * (d // c.group_size) * 2,
+                                           biases.data_ptr() + g * ccap * (d // c.group_size) * 2, rows, d,
+                                           sc[i].data_ptr() + g * cap * d * 2, st), "dequantize")
+        return _slots_struct(sc, 16, 64, 1, G, cap, d)
+
+    def _prefill_block(self, ids_d: torch.Tensor) -> None:
+        """One block of S prompt rows at positions [offset, offset + S): per layer input norm, qkv
+        GEMM, RoPE + cache append, causal prompt attention + combine, o_proj GEMM (+ residual),
+        post norm, gate|up GEMM, PolyNorm·up, down GEMM (+ residual) — ``MotifDecoderLayer``
+        (model.py:845-855) over the block. The block's hidden rows are not needed afterwards:
+        only its K/V rows stay (in the cache)."""
+        S = ids_d.numel()
+        off = self.offset
+        if off + S + 1 > self.max_seq:
+            raise ValueError(f"KV capacity {self.max_seq} exhausted by a {S}-row prompt block at {off}")
+        b = self._block_buffers(S)
+        a = self.args
+        st = stream(self.device)
+        H, d, I = self.H, self.d, self.inter
+        eps = a.rms_norm_eps
+        h, x = b["h"][:S], b["x"][:S]
+        qkv, o, attn = b["qkv"][:S], b["o"][:S], b["attn"][:S]
+        q = b["q"].view(-1)[: self.q_heads * S * d].view(self.q_heads, S, d)  # head-major, contiguous
+        gu, act, err = b["gu"][:S], b["act"][:S], b["err"]
+        mode = 1 if self.vanilla else 0
+
+        def gemm(xin, ql, out, residual=None):
+            check(lib.motif_q4_gemm(ptr(xin), S, ql.in_dim, ptr(ql.weight), ptr(ql.scales), ptr(ql.biases),
+                                    ql.out_dim, ptr(out), ptr(residual) if residual is not None else None,
+                                    ptr(err), st), "q4_gemm")
+
+        for li, L in enumerate(self.layers):
+            if li == 0:
+                check(lib.motif_embed_rms_norm_rows(0, ptr(ids_d), S, ptr(self.embed), self.V, H,
+                                                    ptr(L["input_norm"]), eps, ptr(h), ptr(x), st), "embed rows")
+            else:
+                check(lib.motif_rms_norm(0, ptr(h), ptr(L["input_norm"]), eps, S, H, ptr(x), st), "rms_norm")
+            gemm(x, L["qkv"], qkv)
+            check(lib.motif_rope_qkv_append_rows(ptr(qkv), S, ptr(self.inv_freq), self.q_heads, self._slots[li],
+                                                 off, None, ptr(q), st), "rope rows")
+            slots = self._attn_slots(li, off + S)
+            check(lib.motif_prefill_attention(ptr(q), S, self.q_heads, slots, off, mode, self.gr, self.scale,
+                                              ptr(o), ptr(err), st), "prefill_attention")
+            check(lib.motif_prefill_post(ptr(o), S, self.q_heads, mode, self.q_groups, self.gr, ptr(L["subln"]),
+                                         ptr(L["lambda_full"]), L["lambda_full"].numel(), L["lambda_init"],
+                                         a.attn_rms_norm_eps, ptr(attn), st), "prefill_post")
+            gemm(attn, L["o"], h, residual=h)
+            check(lib.motif_rms_norm(0, ptr(h), ptr(L["post_norm"]), eps, S, H, ptr(x), st), "rms_norm")
+            gemm(x, L["gate_up"], gu)
+            check(lib.motif_polynorm_mul(0, ptr(gu), ptr(gu) + 2 * I, 2 * I, ptr(L["polynorm_w"]),
+                                         ptr(L["polynorm_b"]), 1e-6, S, I, ptr(act), st), "polynorm_mul")
+            gemm(act, L["down"], h, residual=h)
+        self._bump_host(S)
+        self.pos_len.copy_(torch.tensor([self.offset, self.offset + 1], dtype=torch.int32))
+        if int(err.item()) != 0:
+            raise RuntimeError("prompt block: a tensor-core pipeline wait timed out")
 
     def decode_host(self, token: int) -> int:
         """Public per-token API with host buffers: H2D token, one graph replay, D2H argmax, sync."""

@@ -201,3 +201,87 @@ def test_prefill_attention_vanilla_matches_oracle(cuda, n_rep, S, off):
                             np.concatenate([va, vb], axis=1)[:, :, :off].astype(np.float16))
     ref = O.vanilla_attention_reference(q[None], K[:, :, off:], V_paired[:, :, off:], oc, lam, lam_init, subln, 1e-5)
     assert_close(down(y), ref[0].transpose(1, 0, 2).astype(np.float64), "float16", what="vanilla prompt attention")
+
+
+# ---------------------------------------------------------------- whole-model prompt ingestion
+def _grouped_model(cache, seed=0):
+    from mlx_motif.model import ModelArgs, MotifDecoder
+
+    a = ModelArgs(hidden_size=512, num_hidden_layers=3, intermediate_size=1024, num_attention_heads=32,
+                  num_key_value_heads=16, num_noise_heads=8, vocab_size=1024)
+    return MotifDecoder.random(a, seed=seed, std=0.05, cache=cache, max_seq=1024)
+
+
+def _vanilla_model(n_rep, seed=0):
+    from mlx_motif.model import ModelArgs, MotifDecoder
+
+    heads = 8 if n_rep == 4 else 4
+    a = ModelArgs(hidden_size=heads * 128, num_hidden_layers=3, intermediate_size=1024, num_attention_heads=heads,
+                  num_key_value_heads=heads // n_rep, num_noise_heads=None, vocab_size=1024)
+    return MotifDecoder.random(a, seed=seed, std=0.05, cache="fp16", max_seq=1024)
+
+
+@pytest.mark.parametrize("kind", ["grouped-fp16", "grouped-q4", "grouped-q8", "vanilla-4", "vanilla-1"])
+def test_batched_prefill_matches_stepwise(cuda, kind):
+    """A prompt ingested in tensor-core row blocks (chunks of 128, so several blocks with a
+    nonzero cache offset, the chunked-prefill case) leaves the same cache and greedy
+    continuation as feeding it through the decode step one token at a time: K/V rows within
+    fp16 tolerance, identical greedy tokens, close final logits."""
+    def make():
+        if kind.startswith("grouped"):
+            return _grouped_model(kind.split("-")[1], seed=3)
+        return _vanilla_model(int(kind.split("-")[1]), seed=3)
+
+    prompt = np.random.default_rng(1).integers(0, 1024, 300).tolist()
+    a, b = make(), make()
+    assert a._block_ok()
+    a.prefill(prompt, chunk=128, batched=True)
+    b.prefill(prompt, batched=False)
+    assert a.offset == b.offset == len(prompt)
+    assert int(a.token.item()) == int(b.token.item())
+    # A q4 cache flips a code wherever a row sits on a rounding boundary; the flip (one
+    # quantization step, range/15) then propagates through the later layers.
+    lt = {"q4": 0.15, "q8": 0.05}.get(kind.split("-")[1], 2e-2)
+    assert_close(down(a.logits), down(b.logits), "float16", atol=lt, rtol=2e-2, what="first-token logits")
+    ca, cb = a.caches[-1], b.caches[-1]
+    for n in ("k1", "k2", "v1", "v2"):
+        x, y = getattr(ca, n), getattr(cb, n)
+        if isinstance(x, tuple):  # quantized: the rows agree but for boundary flips of single codes
+            from mlx_motif.quantization import dequantize
+
+            dx = dequantize(*(t[..., :300, :].contiguous() for t in x), group_size=64, bits=ca.bits).float()
+            dy = dequantize(*(t[..., :300, :].contiguous() for t in y), group_size=64, bits=cb.bits).float()
+            rel = ((dx - dy).abs().mean() / dy.abs().mean()).item()
+            assert rel <= 0.05, f"last-layer {n}: mean |difference| is {rel:.3f} of mean |value|"
+        else:
+            assert_close(down(x[..., :300, :]), down(y[..., :300, :]), "float16", atol=2e-2, rtol=2e-2,
+                         what=f"last-layer {n} rows")
+    ta = [int(a.token.item())]
+    tb = [int(b.token.item())]
+    for _ in range(6):
+        a.step_device()
+        b.step_device()
+        ta.append(int(a.token.item()))
+        tb.append(int(b.token.item()))
+    assert ta == tb
+
+
+def test_batched_prefill_vanilla_matches_oracle(cuda):
+    """Vanilla prompt of 140 tokens through one 139-row tensor-core block + the decode step ==
+    the oracle's token-by-token _forward_vanilla: the same first greedy token, logits within
+    tolerance."""
+    from mlx_motif.model import ModelArgs, MotifDecoder
+
+    a = O.OracleVanillaArgs(hidden_size=1024, num_hidden_layers=2, intermediate_size=512, num_attention_heads=8,
+                            num_key_value_heads=2, head_dim=128, vocab_size=512)
+    w = O.make_synthetic_weights_vanilla(a, seed=4, std=0.05)
+    ma = ModelArgs(hidden_size=1024, num_hidden_layers=2, intermediate_size=512, num_attention_heads=8,
+                   num_key_value_heads=2, vocab_size=512, num_noise_heads=None)
+    dec = MotifDecoder(ma, w, cache="fp16", max_seq=256, device=cuda)
+    prompt = np.random.default_rng(2).integers(0, 512, 140).tolist()
+    dec.prefill(prompt, batched=True)
+    orc = O.VanillaDecodeOracle(a, w)
+    for t in prompt:
+        logits, tok = orc.step(t)
+    assert int(dec.token.item()) == tok
+    assert_close(down(dec.logits), logits.astype(np.float64), "float16", atol=2e-2, rtol=2e-2, what="logits")
