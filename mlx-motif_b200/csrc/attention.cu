@@ -20,6 +20,7 @@
 
 #include "common.cuh"
 #include "kvquant.cuh"
+#include "tma.cuh"
 
 namespace motif {
 namespace {
@@ -676,6 +677,326 @@ __global__ void __launch_bounds__(kAttnThreads) gda_fused_kernel(FusedArgs f) {
   if (threadIdx.x == 0) f.counters[g] = 0;  // ready for the next launch
 }
 
+// ---- long-context decode step on the tensor cores (fp16 4-slot cache) ----------------------
+//
+// Same contract as gda_fused_kernel (RoPE + append of the new row, split-KV attention over the
+// cache, last-CTA merge with the differential combine), for caches long enough that the
+// per-position CUDA-core work limits gda_fused_kernel. Cache positions are the MMA's M
+// dimension: per 128-position tile
+//   S1ᵀ = K1·Q_sigᵀ and S2ᵀ = K2·Q_noiseᵀ      (M 128 positions, N 16 padded heads, K 128)
+//   O1ᵀ += V1ᵀ·Pᵀ and O2ᵀ += V2ᵀ·Pᵀ            (M 128 channels, N 16 heads, K 128 positions;
+//                                               V read MN-major straight from the cache rows)
+// with S and O in tensor memory. Warp 0 streams (k1, k2) and (v1, v2) tile pairs with TMA
+// into a three-entry ring of 64 KB; warp 1 issues the MMAs one tile ahead; warps 2..5 (one
+// thread per position, then per channel) run the online softmax — per-head maxima through
+// shuffles and shared memory, the running maximum re-based only when it grows by more than
+// 2^8 (O's columns rescaled in tensor memory), P written as fp16 — and finally store the
+// split's partial (m, l, O) in the layout the merge reads.
+constexpr int kLongThreads = 256;
+constexpr int kLT = 128;       // cache positions per tile
+constexpr int kLRing = 3;      // 64 KB ring entries
+constexpr int kLOffQ = kLRing * 65536;   // Q_sig, Q_noise: 2 × 4 KB (16 rows × 256 B, two K chunks)
+constexpr int kLOffP = kLOffQ + 8192;    // Pᵀ: 2 buffers × 4 KB
+constexpr int kLOffRed = kLOffP + 8192;  // softmax scratch: [2][4 warps][16] maxima + [4][16] sums
+constexpr int kLOffRow = kLOffRed + 1024;  // append scratch: 4 × 128 floats
+constexpr int kLOffBar = kLOffRow + 2048;
+constexpr int kLNumBars = 2 * kLRing + 6;  // full[3], free[3], s_full[2], p_full[2], o_bar, drain
+constexpr int kLSmem = kLOffBar + kLNumBars * 8 + 16 + 1024;
+constexpr int kLErrSlot = 63;  // control word set to 1 when a wait timed out
+
+struct LongMaps {
+  CUtensorMap slot[4];  // k1, k2, v1, v2: (heads·cap) rows × 256 B, box 128 B × 128 rows, 128-byte swizzle
+};
+
+// Byte offset of element (row, col) in a K-major tile of 16 rows × 128 fp16 (two 64-column
+// chunks of 16 rows × 128 B, 128-byte swizzle).
+__device__ __forceinline__ uint32_t kmaj16_off(int row, int col) {
+  return (uint32_t)((col >> 6) * 2048 + row * 128 + ((((col & 63) >> 3) ^ (row & 7)) << 4) + (col & 7) * 2);
+}
+
+template <int NA, int NB, bool PAIRED>
+__global__ void __launch_bounds__(kLongThreads, 1) gda_long_kernel(FusedArgs f, const __grid_constant__ LongMaps tm) {
+  constexpr int D = 128, NH = NA + NB, half = D / 2;
+  static_assert(NA <= 16 && NB <= 16, "heads per group");
+  __shared__ float s_cs[half], s_sn[half];
+  __shared__ int s_last;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const uint32_t sb = tc::smem_addr(smem);
+  const uint32_t bar = sb + kLOffBar;
+  auto full = [&](int e) { return bar + 8u * e; };
+  auto freeb = [&](int e) { return bar + 8u * (kLRing + e); };
+  auto s_full = [&](int b) { return bar + 8u * (2 * kLRing + b); };
+  auto p_full = [&](int b) { return bar + 8u * (2 * kLRing + 2 + b); };
+  const uint32_t o_bar = bar + 8u * (2 * kLRing + 4);
+  const uint32_t drain = bar + 8u * (2 * kLRing + 5);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kLOffBar + kLNumBars * 8);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  float* red = reinterpret_cast<float*>(smem + kLOffRed);
+  float* s_row = reinterpret_cast<float*>(smem + kLOffRow);
+
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int split = blockIdx.x, nsplit = gridDim.x, g = blockIdx.y;
+  const int64_t cap = f.cache.capacity;
+  // every read below may depend on the previous kernel (the qkv projection)
+  asm volatile("griddepcontrol.wait;\n" ::: "memory");
+  const int pos = f.pos_len[0], kv_len = max(0, min(f.pos_len[1], (int)cap));
+  int p0, p1, n_active;
+  split_range(kv_len, nsplit, split, p0, p1, n_active);
+  if (n_active < 1) n_active = 1;
+  if (split >= n_active) return;
+  const bool append = pos >= 0 && pos < cap && ((pos >= p0 && pos < p1) || (split == 0 && pos >= kv_len));
+  const int nt = p1 > p0 ? (p1 - p0 + kLT - 1) / kLT : 0;
+
+  if (threadIdx.x < half) rope_angle(threadIdx.x, pos, f.inv_freq, s_cs[threadIdx.x], s_sn[threadIdx.x]);
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kLNumBars; ++i) tc::mbar_init(bar + 8u * i, (i == 2 * kLRing + 2 || i == 2 * kLRing + 3) ? 4 : 1);
+    *abort_flag = 0;
+    tc::mbar_fence_init();
+  }
+  if (warp == 1) {
+    tc::tmem_alloc(tc::smem_addr(tmem_slot), 128);  // S: 2 × 32 columns, O1/O2: 2 × 16
+    tc::tmem_relinquish();
+  }
+  // zero the Q and Pᵀ tiles (rows past NH stay zero: padded heads)
+  for (int i = threadIdx.x; i < 16384 / 16; i += kLongThreads)
+    reinterpret_cast<uint4*>(smem + kLOffQ)[i] = make_uint4(0, 0, 0, 0);
+  tc::tc_fence_before();
+  __syncthreads();
+  tc::tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  // ---- the new row (k1, k2 with RoPE, v1, v2) of this group, by warps 0..3 ----
+  if (append && warp < 4) {
+    const int head = warp < 2 ? f.q_heads + 2 * g + warp : f.q_heads + 2 * f.groups + 2 * g + (warp - 2);
+    const __half* src = f.qkv + (int64_t)head * D;
+    __half* dst = static_cast<__half*>(f.cache.data[warp]) + ((int64_t)g * cap + pos) * D + lane * 4;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int c = lane * 4 + j, k = c < half ? c : c - half;
+      dst[j] = __float2half_rn(warp < 2 ? rope_rotate(src, c, half, s_cs[k], s_sn[k]) : __half2float(src[c]));
+    }
+    asm volatile("fence.proxy.async.global;\n" ::: "memory");  // the TMA loads below read this row
+  }
+  // ---- rotated q of the group's heads, fp16, into the K-major Q tiles ----
+  for (int i = threadIdx.x; i < NH * D; i += kLongThreads) {
+    const int h = i / D, c = i - h * D, k = c < half ? c : c - half;
+    const __half* src = f.qkv + (int64_t)fused_head<NA, NB, PAIRED>(g, h, f.q_origin) * D;
+    const __half v = __float2half_rn(rope_rotate(src, c, half, s_cs[k], s_sn[k]));
+    const int tile = h < NA ? 0 : 1, row = h < NA ? h : h - NA;
+    *reinterpret_cast<__half*>(smem + kLOffQ + tile * 4096 + kmaj16_off(row, c)) = v;
+  }
+  tc::fence_proxy_async_smem();
+  __syncthreads();
+
+  float m_ref[NH], L[NH];
+  if (warp == 0) {
+    if (lane == 0) {  // ---- TMA producer: (k1,k2) then (v1,v2) per tile ----
+      int issued = 0;
+      for (int u = 0; u < 2 * nt; ++u) {
+        const int e = u % kLRing, r = u / kLRing;
+        if (u >= kLRing && !tc::mbar_wait(freeb(e), (r - 1) & 1)) { *abort_flag = 1; break; }
+        if (*abort_flag) break;
+        const int j = u >> 1, sl = (u & 1) * 2;
+        const int row = (int)((int64_t)g * cap + p0 + j * kLT);
+        const uint32_t dst = sb + e * 65536;
+        tc::mbar_expect_tx(full(e), 65536);
+        tc::tma_load_2d(dst, &tm.slot[sl], 0, row, full(e));
+        tc::tma_load_2d(dst + 16384, &tm.slot[sl], 128, row, full(e));
+        tc::tma_load_2d(dst + 32768, &tm.slot[sl + 1], 0, row, full(e));
+        tc::tma_load_2d(dst + 49152, &tm.slot[sl + 1], 128, row, full(e));
+        issued = u + 1;
+      }
+      for (int u = issued > kLRing ? issued - kLRing : 0; u < issued; ++u)
+        if (!tc::mbar_wait(full(u % kLRing), (u / kLRing) & 1)) *abort_flag = 1;
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {  // ---- MMA issuer ----
+      constexpr uint32_t idesc_qk = tc::idesc_f16_f32(kLT, 16);
+      constexpr uint32_t idesc_pv = tc::idesc_f16_f32(kLT, 16, false, true);
+      const uint32_t qs = sb + kLOffQ, qn = sb + kLOffQ + 4096;
+      auto issue_qk = [&](int j) -> bool {
+        const int u = 2 * j, e = u % kLRing;
+        if (!tc::mbar_wait(full(e), (u / kLRing) & 1)) return false;
+        tc::tc_fence_after();
+        const uint32_t kb = sb + e * 65536;
+        const uint32_t col = (j & 1) * 32;
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          const uint32_t ko = (kk >> 2) * 16384 + (kk & 3) * 32, qo = (kk >> 2) * 2048 + (kk & 3) * 32;
+          tc::mma_f16(tmem + col, tc::desc_kmajor_sw128(kb + ko), tc::desc_kmajor_sw128(qs + qo), idesc_qk, kk > 0);
+          tc::mma_f16(tmem + col + 16, tc::desc_kmajor_sw128(kb + 32768 + ko), tc::desc_kmajor_sw128(qn + qo),
+                      idesc_qk, kk > 0);
+        }
+        tc::mma_commit(s_full(j & 1));
+        tc::mma_commit(freeb(e));
+        return true;
+      };
+      bool ok = nt == 0 || issue_qk(0);
+      for (int j = 0; ok && j < nt; ++j) {
+        if (*abort_flag) { ok = false; break; }
+        if (j + 1 < nt && !issue_qk(j + 1)) { ok = false; break; }
+        const int u = 2 * j + 1, e = u % kLRing;
+        if (!tc::mbar_wait(p_full(j & 1), (j >> 1) & 1) || !tc::mbar_wait(full(e), (u / kLRing) & 1)) {
+          ok = false;
+          break;
+        }
+        tc::tc_fence_after();
+        const uint32_t vb = sb + e * 65536, pb = sb + kLOffP + (j & 1) * 4096;
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          const uint64_t bdesc = tc::desc_kmajor_sw128(pb + (kk >> 2) * 2048 + (kk & 3) * 32);
+          tc::mma_f16(tmem + 64, tc::desc_mnmajor_sw128(vb + kk * 2048, 16384, 1024), bdesc, idesc_pv, (j | kk) != 0);
+          tc::mma_f16(tmem + 80, tc::desc_mnmajor_sw128(vb + 32768 + kk * 2048, 16384, 1024), bdesc, idesc_pv,
+                      (j | kk) != 0);
+        }
+        tc::mma_commit(o_bar);
+        tc::mma_commit(freeb(e));
+      }
+      if (!ok) *abort_flag = 1;
+      tc::mma_commit(drain);
+      if (!tc::mbar_wait(drain, 0)) *abort_flag = 1;
+    }
+    __syncwarp();
+  } else if (warp < 6) {  // ---- softmax: thread = position of the tile, later = channel ----
+    const int sw = warp - 2, q = warp & 3, r = q * 32 + lane;
+    const uint32_t trow = tmem + ((uint32_t)(q * 32) << 16);
+#pragma unroll
+    for (int h = 0; h < NH; ++h) {
+      m_ref[h] = -INFINITY;
+      L[h] = 0.f;
+    }
+    int o_seen = 0;
+    bool alive = true;
+    auto observe = [&](int upto) -> bool {  // PV(0 .. upto-1) complete, phases in order
+      while (o_seen < upto) {
+        if (!tc::mbar_wait(o_bar, o_seen & 1)) return false;
+        ++o_seen;
+      }
+      return true;
+    };
+    for (int j = 0; j < nt; ++j) {
+      const bool got = tc::mbar_wait(s_full(j & 1), (j >> 1) & 1);
+      tc::tc_fence_after();
+      uint32_t s1[16], s2[16];
+      tc::tmem_ld16(trow + (j & 1) * 32, s1);
+      tc::tmem_ld16(trow + (j & 1) * 32 + 16, s2);
+      tc::tmem_ld_wait();
+      const bool valid = p0 + j * kLT + r < p1;
+      float x[NH], mt[NH];
+#pragma unroll
+      for (int h = 0; h < NH; ++h) {
+        x[h] = valid ? __uint_as_float(h < NA ? s1[h] : s2[h - NA]) * f.scale_log2 : -INFINITY;
+        mt[h] = warp_max(x[h]);
+      }
+      float* rb = red + (j & 1) * 64;
+      if (lane == 0)
+#pragma unroll
+        for (int h = 0; h < NH; ++h) rb[sw * 16 + h] = mt[h];
+      // the four warps leave together when a wait gave up anywhere
+      if (tc::named_sync_or(1, 128, !got || *abort_flag)) {
+        *abort_flag = 1;
+        alive = false;
+        break;
+      }
+      bool any_need = false;
+      float factor[NH];
+#pragma unroll
+      for (int h = 0; h < NH; ++h) {
+        const float m = fmaxf(fmaxf(rb[h], rb[16 + h]), fmaxf(rb[32 + h], rb[48 + h]));
+        factor[h] = 1.f;
+        if (m > m_ref[h] + 8.f) {
+          factor[h] = exp2f(m_ref[h] - m);  // 0 while nothing was accumulated (m_ref = -inf)
+          m_ref[h] = m;
+          any_need = true;
+        }
+        L[h] *= factor[h];
+      }
+      __half pv[NH];
+#pragma unroll
+      for (int h = 0; h < NH; ++h) {
+        pv[h] = __float2half_rn(x[h] == -INFINITY ? 0.f : exp2f(x[h] - m_ref[h]));
+        L[h] += __half2float(pv[h]);
+      }
+      // Pᵀ buffer (j mod 2) was read by PV(j-2); a rescale of O needs PV(j-1) finished
+      bool okw = observe(j - 1);
+      if (okw && any_need && j > 0) {
+        okw = observe(j);
+        if (__all_sync(0xffffffffu, okw)) {
+          tc::tc_fence_after();
+#pragma unroll
+          for (int oc = 0; oc < 2; ++oc) {
+            uint32_t ov[16];
+            tc::tmem_ld16(trow + 64 + oc * 16, ov);
+            tc::tmem_ld_wait();
+#pragma unroll
+            for (int h = 0; h < NH; ++h) ov[h] = __float_as_uint(__uint_as_float(ov[h]) * factor[h]);
+            tc::tmem_st16(trow + 64 + oc * 16, ov);
+          }
+          tc::tmem_st_wait();
+        }
+      }
+      if (!okw) *abort_flag = 1;  // caught by the next tile's barrier (or the final wait)
+      uint8_t* pt = smem + kLOffP + (j & 1) * 4096;
+#pragma unroll
+      for (int h = 0; h < NH; ++h) *reinterpret_cast<__half*>(pt + kmaj16_off(h, r)) = pv[h];
+      tc::fence_proxy_async_smem();
+      tc::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) tc::mbar_arrive(p_full(j & 1));
+    }
+    // ---- the split's partial: O columns per channel r, m and l per head ----
+    const bool fin = alive && __all_sync(0xffffffffu, observe(nt));
+    if (!fin) *abort_flag = 1;
+    tc::tc_fence_after();
+    uint32_t o1[16], o2[16];
+    tc::tmem_ld16(trow + 64, o1);
+    tc::tmem_ld16(trow + 80, o2);
+    tc::tmem_ld_wait();
+    float* lred = red + 128;
+#pragma unroll
+    for (int h = 0; h < NH; ++h) {
+      const float t = warp_sum(L[h]);
+      if (lane == 0) lred[sw * 16 + h] = t;
+    }
+    tc::named_sync(1, 128);
+    constexpr int stride = 2 * D + 2;
+#pragma unroll
+    for (int h = 0; h < NH; ++h) {
+      float* base = f.ws + ((int64_t)fused_head<NA, NB, PAIRED>(g, h, f.q_origin) * nsplit + split) * stride;
+      const bool any = nt > 0 && fin;
+      base[2 + r] = any ? __uint_as_float(o1[h]) : 0.f;
+      base[2 + D + r] = any ? __uint_as_float(o2[h]) : 0.f;
+      if (r == 0) {
+        base[0] = any ? m_ref[h] : -INFINITY;
+        base[1] = any ? (lred[h] + lred[16 + h]) + (lred[32 + h] + lred[48 + h]) : 0.f;
+      }
+    }
+  }
+
+  tc::tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc::tc_fence_after();
+    tc::tmem_dealloc(tmem, 128);
+  }
+  pdl_trigger();
+  if (threadIdx.x == 0 && *abort_flag) atomicExch(f.counters + kLErrSlot, 1);
+  // ---- the last CTA of the group merges the splits ----
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) s_last = atomicAdd(f.counters + g, 1) == n_active - 1;
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  if constexpr (PAIRED)
+    vanilla_merge_group<D, NA>(f.ws, nsplit, n_active, g, f.subln_w, f.lam, f.out_scale, f.eps, f.out);
+  else
+    gda_merge_group<D, NA>(f.ws, nsplit, n_active, g, f.q_origin, f.subln_w, f.lam, f.lam_mode, f.out_scale, f.eps,
+                           f.out);
+  if (threadIdx.x == 0) f.counters[g] = 0;
+}
+
 template <typename T, int D, int BITS, int MAXA, int NB>
 int launch_split(const AttnArgs& a, int nsplit, int batch, cudaStream_t st) {
   constexpr int NH = MAXA + NB;
@@ -985,6 +1306,65 @@ cudaError_t launch_fused(const FusedArgs& f, dim3 grid, int bits, int gs, cudaSt
                    : launch_fused_one<NA, NB, PAIRED, PPW, 8, 16>(f, grid, st);
 }
 
+template <int NA, int NB, bool PAIRED>
+cudaError_t launch_long_one(const FusedArgs& f, const LongMaps& m, dim3 grid, cudaStream_t st) {
+  auto kern = gda_long_kernel<NA, NB, PAIRED>;
+  static bool configured = false;
+  if (!configured) {
+    const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kLSmem);
+    if (e != cudaSuccess) return e;
+    configured = true;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(kLongThreads);
+  cfg.dynamicSmemBytes = kLSmem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, f, m);
+}
+
+// Caches at least this long (capacity, fp16) take the tensor-core step; MOTIF_LONG_ATTN_MIN_CAP
+// overrides it (0 = always, a huge value = never).
+int64_t long_min_cap() {
+  const char* v = getenv("MOTIF_LONG_ATTN_MIN_CAP");
+  return v ? atoll(v) : 2048;
+}
+
+// The tensor-core step's maps over the four fp16 slots, or false when the cache does not fit it.
+bool long_maps(const motif_kv4_slots& c, LongMaps& m) {
+  if (c.bits != 16 || c.capacity < long_min_cap() || c.heads >= kLErrSlot || c.heads * c.capacity >= (1ll << 31))
+    return false;
+  for (int i = 0; i < 4; ++i) {
+    if (reinterpret_cast<uintptr_t>(c.data[i]) % 16) return false;
+    if (!encode_tma_rows(&m.slot[i], c.data[i], 256, (uint64_t)(c.heads * c.capacity), 128, kLT, true)) return false;
+  }
+  return true;
+}
+
+int sm_count() {
+  static int n = 0;
+  if (!n) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
+        n <= 0)
+      n = 148;
+  }
+  return n;
+}
+
+// One CTA per SM (the ring takes ~210 KB of shared memory), all in one wave.
+int long_splits(int64_t groups, int64_t max_splits_ws) {
+  int64_t n = sm_count() / (groups < 1 ? 1 : groups);
+  if (n > max_splits_ws) n = max_splits_ws;
+  if (n > kMaxSplits) n = kMaxSplits;
+  return (int)(n < 1 ? 1 : n);
+}
+
 int check_fused_cache(const motif_kv4_slots& c, int64_t groups, const char* who) {
   for (int i = 0; i < 4; ++i) MOTIF_REQUIRE(c.data[i], MOTIF_ERR_NULL, "%s: slot %d null", who, i);
   MOTIF_REQUIRE(c.batch == 1 && c.head_dim == 128, MOTIF_ERR_BAD_CONTRACT, "%s: batch 1, head_dim 128 only", who);
@@ -1062,9 +1442,16 @@ int motif_gda_decode_step(const void* qkv, const float* inv_freq, const motif_kv
   f.counters = static_cast<int*>(workspace);
   f.ws = reinterpret_cast<float*>(static_cast<char*>(workspace) + kFusedCtlBytes);
   cudaStream_t st = as_stream(stream);
-  const dim3 grid(nsplit, (unsigned)q_groups);
-  const cudaError_t e = gr == 3 ? launch_fused<3, 1, false, 4>(f, grid, c.bits, c.group_size, st)
-                                : launch_fused<4, 1, false, 4>(f, grid, c.bits, c.group_size, st);
+  cudaError_t e;
+  LongMaps lm;
+  if (long_maps(c, lm)) {
+    const dim3 grid(long_splits(q_groups, max_splits_ws), (unsigned)q_groups);
+    e = gr == 3 ? launch_long_one<3, 1, false>(f, lm, grid, st) : launch_long_one<4, 1, false>(f, lm, grid, st);
+  } else {
+    const dim3 grid(nsplit, (unsigned)q_groups);
+    e = gr == 3 ? launch_fused<3, 1, false, 4>(f, grid, c.bits, c.group_size, st)
+                : launch_fused<4, 1, false, 4>(f, grid, c.bits, c.group_size, st);
+  }
   if (e != cudaSuccess) return fail(MOTIF_ERR_CUDA, "gda_decode_step: launch: %s", cudaGetErrorString(e));
   return check_launch("gda decode step");
 }
@@ -1102,11 +1489,19 @@ int motif_vanilla_decode_step(const void* qkv, const float* inv_freq, const moti
   f.counters = static_cast<int*>(workspace);
   f.ws = reinterpret_cast<float*>(static_cast<char*>(workspace) + kFusedCtlBytes);
   cudaStream_t st = as_stream(stream);
-  const dim3 grid(nsplit, (unsigned)kv_heads);
   cudaError_t e;
-  if (n_rep == 1) e = launch_fused<1, 1, true, 4>(f, grid, c.bits, c.group_size, st);
-  else if (n_rep == 2) e = launch_fused<2, 2, true, 4>(f, grid, c.bits, c.group_size, st);
-  else e = launch_fused<4, 4, true, 2>(f, grid, c.bits, c.group_size, st);
+  LongMaps lm;
+  if (long_maps(c, lm)) {
+    const dim3 grid(long_splits(kv_heads, max_splits_ws), (unsigned)kv_heads);
+    if (n_rep == 1) e = launch_long_one<1, 1, true>(f, lm, grid, st);
+    else if (n_rep == 2) e = launch_long_one<2, 2, true>(f, lm, grid, st);
+    else e = launch_long_one<4, 4, true>(f, lm, grid, st);
+  } else {
+    const dim3 grid(nsplit, (unsigned)kv_heads);
+    if (n_rep == 1) e = launch_fused<1, 1, true, 4>(f, grid, c.bits, c.group_size, st);
+    else if (n_rep == 2) e = launch_fused<2, 2, true, 4>(f, grid, c.bits, c.group_size, st);
+    else e = launch_fused<4, 4, true, 2>(f, grid, c.bits, c.group_size, st);
+  }
   if (e != cudaSuccess) return fail(MOTIF_ERR_CUDA, "vanilla_decode_step: launch: %s", cudaGetErrorString(e));
   return check_launch("vanilla decode step");
 }
