@@ -311,7 +311,8 @@ __device__ __forceinline__ void gda_merge_group(const float* __restrict__ ws, in
   __shared__ float scratch[32 * GR];
   __shared__ float f_s[GR + 1][kMaxSplits];
   __shared__ float L_s[GR + 1];
-  const int ch = threadIdx.x;  // 0 .. 2D-1
+  const bool act = threadIdx.x < 2 * D;  // threads past 2D (wider blocks) only join the barriers
+  const int ch = act ? threadIdx.x : 0;  // 0 .. 2D-1
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   constexpr int stride = 2 * D + 2;
   if (warp <= GR) {
@@ -351,14 +352,14 @@ __device__ __forceinline__ void gda_merge_group(const float* __restrict__ ws, in
     const int h_o = g * GR + j;
     const float l = lam[lam_mode == 0 ? 0 : (lam_mode == 1 ? g : h_o)];
     d[j] = val[j] - l * val[GR];
-    ssq[j] = d[j] * d[j];
+    ssq[j] = act ? d[j] * d[j] : 0.f;
   }
   block_sum<GR>(ssq, scratch);
   const float w = __half2float(subln_w[ch]);
 #pragma unroll
   for (int j = 0; j < GR; ++j) {
     const float inv = rsqrtf(ssq[j] / (float)(2 * D) + eps);
-    out[(int64_t)(g * GR + j) * 2 * D + ch] = __float2half_rn(d[j] * inv * w * out_scale);
+    if (act) out[(int64_t)(g * GR + j) * 2 * D + ch] = __float2half_rn(d[j] * inv * w * out_scale);
   }
 }
 
@@ -374,7 +375,8 @@ __device__ __forceinline__ void vanilla_merge_group(const float* __restrict__ ws
   __shared__ float scratch[32 * NP];
   __shared__ float f_s[2 * NP][kMaxSplits];
   __shared__ float L_s[2 * NP];
-  const int ch = threadIdx.x;  // 0 .. 2D-1
+  const bool act = threadIdx.x < 2 * D;  // threads past 2D (wider blocks) only join the barriers
+  const int ch = act ? threadIdx.x : 0;  // 0 .. 2D-1
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   constexpr int stride = 2 * D + 2;
   if (warp < 2 * NP) {
@@ -403,7 +405,7 @@ __device__ __forceinline__ void vanilla_merge_group(const float* __restrict__ ws
     const float o1 = round_through<__half>(L_s[2 * j] > 0.f ? acc[2 * j] / L_s[2 * j] : 0.f);
     const float o2 = round_through<__half>(L_s[2 * j + 1] > 0.f ? acc[2 * j + 1] / L_s[2 * j + 1] : 0.f);
     d[j] = round_through<__half>(o1 - round_through<__half>(lam16 * o2));
-    ssq[j] = d[j] * d[j];
+    ssq[j] = act ? d[j] * d[j] : 0.f;
   }
   block_sum<NP>(ssq, scratch);
   const float w = __half2float(subln_w[ch]);
@@ -412,7 +414,7 @@ __device__ __forceinline__ void vanilla_merge_group(const float* __restrict__ ws
   for (int j = 0; j < NP; ++j) {
     const float inv = rsqrtf(ssq[j] / (float)(2 * D) + eps);
     const float y = round_through<__half>(d[j] * inv * w);
-    out[(int64_t)(g * NP + j) * 2 * D + ch] = __float2half_rn(y * os16);
+    if (act) out[(int64_t)(g * NP + j) * 2 * D + ch] = __float2half_rn(y * os16);
   }
 }
 
@@ -677,7 +679,7 @@ __global__ void __launch_bounds__(kAttnThreads) gda_fused_kernel(FusedArgs f) {
   if (threadIdx.x == 0) f.counters[g] = 0;  // ready for the next launch
 }
 
-// ---- long-context decode step on the tensor cores (fp16 4-slot cache) ----------------------
+// ---- long-context decode step on the tensor cores ------------------------------------------
 //
 // Same contract as gda_fused_kernel (RoPE + append of the new row, split-KV attention over the
 // cache, last-CTA merge with the differential combine), for caches long enough that the
@@ -685,27 +687,56 @@ __global__ void __launch_bounds__(kAttnThreads) gda_fused_kernel(FusedArgs f) {
 // dimension: per 128-position tile
 //   S1ᵀ = K1·Q_sigᵀ and S2ᵀ = K2·Q_noiseᵀ      (M 128 positions, N 16 padded heads, K 128)
 //   O1ᵀ += V1ᵀ·Pᵀ and O2ᵀ += V2ᵀ·Pᵀ            (M 128 channels, N 16 heads, K 128 positions;
-//                                               V read MN-major straight from the cache rows)
-// with S and O in tensor memory. Warp 0 streams (k1, k2) and (v1, v2) tile pairs with TMA
-// into a three-entry ring of 64 KB; warp 1 issues the MMAs one tile ahead; warps 2..5 (one
-// thread per position, then per channel) run the online softmax — per-head maxima through
-// shuffles and shared memory, the running maximum re-based only when it grows by more than
-// 2^8 (O's columns rescaled in tensor memory), P written as fp16 — and finally store the
-// split's partial (m, l, O) in the layout the merge reads.
-constexpr int kLongThreads = 256;
-constexpr int kLT = 128;       // cache positions per tile
-constexpr int kLRing = 3;      // 64 KB ring entries
-constexpr int kLOffQ = kLRing * 65536;   // Q_sig, Q_noise: 2 × 4 KB (16 rows × 256 B, two K chunks)
-constexpr int kLOffP = kLOffQ + 8192;    // Pᵀ: 2 buffers × 4 KB
-constexpr int kLOffRed = kLOffP + 8192;  // softmax scratch: [2][4 warps][16] maxima + [4][16] sums
-constexpr int kLOffRow = kLOffRed + 1024;  // append scratch: 4 × 128 floats
-constexpr int kLOffBar = kLOffRow + 2048;
-constexpr int kLNumBars = 2 * kLRing + 6;  // full[3], free[3], s_full[2], p_full[2], o_bar, drain
-constexpr int kLSmem = kLOffBar + kLNumBars * 8 + 16 + 1024;
+//                                               V read MN-major: the cache rows as stored)
+// with S and O in tensor memory. Warps 2..5 (one thread per position, then per channel) run
+// the online softmax — per-head maxima through shuffles and a barrier, the running maximum
+// re-based only when it grows by more than 2^8 (O's columns rescaled in tensor memory), P
+// written as fp16 — and store the split's partial (m, l, O) in the layout the merge reads.
+//   fp16 cache (BITS 16): warp 0 streams (k1, k2) and (v1, v2) tile pairs with TMA straight
+//     into a three-entry ring of 64 KB operand tiles (128-byte swizzle); warp 1 issues QK one
+//     tile ahead of PV.
+//   q4 cache (BITS 4, group 64): warp 0 streams the packed rows (codes, scales, biases of the
+//     four slots: 36 KB a tile) into a two-entry ring; warps 6..13 dequantize them (1024 + q
+//     exponent trick, one fused multiply-add with scale and bias) into two fp16 operand
+//     entries (K, V) in the same swizzled layout; warp 1 issues PV(j) then QK(j+1).
+// Splits start on multiples of 128 positions (the packed-scale view needs 4-row alignment).
+constexpr int kLT = 128;  // cache positions per tile
 constexpr int kLErrSlot = 63;  // control word set to 1 when a wait timed out
 
+template <int BITS>
+struct LongCfg;
+template <>
+struct LongCfg<16> {
+  static constexpr int kThreads = 256;
+  static constexpr int kRing = 3;                 // 64 KB operand entries
+  static constexpr int kOffQ = kRing * 65536;     // Q_sig, Q_noise: 2 × 4 KB
+  static constexpr int kOffP = kOffQ + 8192;      // Pᵀ: 2 × 4 KB
+  static constexpr int kOffRed = kOffP + 8192;    // softmax scratch (768 B)
+  static constexpr int kOffRow = kOffRed + 1024;  // append scratch (unused for fp16)
+  static constexpr int kOffBar = kOffRow;
+  static constexpr int kBars = 2 * kRing + 6;     // full[3], free[3], s_full[2], p_full[2], o_bar, drain
+};
+template <>
+struct LongCfg<4> {
+  static constexpr int kThreads = 448;
+  static constexpr int kPacked = 36864;            // codes 4 × 8 KB, scales 4 × 512 B, biases 4 × 512 B
+  static constexpr int kOffPk = 131072;            // after the two 64 KB operand entries
+  static constexpr int kOffQ = kOffPk + 2 * kPacked;
+  static constexpr int kOffP = kOffQ + 8192;
+  static constexpr int kOffRed = kOffP + 8192;
+  static constexpr int kOffRow = kOffPk + kPacked;  // append scratch aliases packed entry 1 (free then)
+  static constexpr int kOffBar = kOffRed + 1024;
+  static constexpr int kBars = 14;  // ofull[2], ofree[2], pfull[2], pfree[2], s_full[2], p_full[2], o_bar, drain
+};
+template <int BITS>
+constexpr int long_smem() {
+  return LongCfg<BITS>::kOffBar + LongCfg<BITS>::kBars * 8 + 16 + 1024;
+}
+
 struct LongMaps {
-  CUtensorMap slot[4];  // k1, k2, v1, v2: (heads·cap) rows × 256 B, box 128 B × 128 rows, 128-byte swizzle
+  CUtensorMap slot[4];  // fp16: rows × 256 B, box 128 B × 128, swizzled; q4: codes rows × 64 B, box 64 B × 128
+  CUtensorMap sc[4];    // q4 scales / biases as 16-byte lines (4 rows each), box 16 B × 32
+  CUtensorMap bi[4];
 };
 
 // Byte offset of element (row, col) in a K-major tile of 16 rows × 128 fp16 (two 64-column
@@ -714,26 +745,59 @@ __device__ __forceinline__ uint32_t kmaj16_off(int row, int col) {
   return (uint32_t)((col >> 6) * 2048 + row * 128 + ((((col & 63) >> 3) ^ (row & 7)) << 4) + (col & 7) * 2);
 }
 
-template <int NA, int NB, bool PAIRED>
-__global__ void __launch_bounds__(kLongThreads, 1) gda_long_kernel(FusedArgs f, const __grid_constant__ LongMaps tm) {
+// Split ranges of the tensor-core step: chunks rounded up to whole tiles.
+__device__ __forceinline__ void long_split_range(int kv_len, int nsplit, int split, int& p0, int& p1, int& n_active) {
+  int chunk = (kv_len + nsplit - 1) / nsplit;
+  chunk = ((chunk + kLT - 1) / kLT) * kLT;
+  if (chunk < kLT) chunk = kLT;
+  n_active = (kv_len + chunk - 1) / chunk;
+  p0 = split * chunk;
+  p1 = min(kv_len, p0 + chunk);
+}
+
+__device__ __forceinline__ uint32_t dq_half2(uint32_t p, __half2 s2, __half2 b2) {
+  const __half2 k1024 = __half2half2(__ushort_as_half(0x6400));
+  __half2 h = *reinterpret_cast<__half2*>(&p);
+  h = __hfma2(__hsub2(h, k1024), s2, b2);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+
+// Eight nibbles (element e at bits 4e..4e+3) -> eight fp16 values in element order.
+__device__ __forceinline__ uint4 dq_word(uint32_t w, __half2 s2, __half2 b2) {
+  const uint32_t t0 = (w & 0x000F000Fu) | 0x64006400u;
+  const uint32_t t1 = ((w >> 4) & 0x000F000Fu) | 0x64006400u;
+  const uint32_t t2 = ((w >> 8) & 0x000F000Fu) | 0x64006400u;
+  const uint32_t t3 = ((w >> 12) & 0x000F000Fu) | 0x64006400u;
+  uint4 o;
+  o.x = dq_half2(__byte_perm(t0, t1, 0x5410), s2, b2);
+  o.y = dq_half2(__byte_perm(t2, t3, 0x5410), s2, b2);
+  o.z = dq_half2(__byte_perm(t0, t1, 0x7632), s2, b2);
+  o.w = dq_half2(__byte_perm(t2, t3, 0x7632), s2, b2);
+  return o;
+}
+
+template <int NA, int NB, bool PAIRED, int BITS>
+__global__ void __launch_bounds__(LongCfg<BITS>::kThreads, 1)
+    gda_long_kernel(FusedArgs f, const __grid_constant__ LongMaps tm) {
+  using C = LongCfg<BITS>;
   constexpr int D = 128, NH = NA + NB, half = D / 2;
+  constexpr bool Q4 = BITS == 4;
   static_assert(NA <= 16 && NB <= 16, "heads per group");
   __shared__ float s_cs[half], s_sn[half];
   __shared__ int s_last;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const uint32_t sb = tc::smem_addr(smem);
-  const uint32_t bar = sb + kLOffBar;
-  auto full = [&](int e) { return bar + 8u * e; };
-  auto freeb = [&](int e) { return bar + 8u * (kLRing + e); };
-  auto s_full = [&](int b) { return bar + 8u * (2 * kLRing + b); };
-  auto p_full = [&](int b) { return bar + 8u * (2 * kLRing + 2 + b); };
-  const uint32_t o_bar = bar + 8u * (2 * kLRing + 4);
-  const uint32_t drain = bar + 8u * (2 * kLRing + 5);
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kLOffBar + kLNumBars * 8);
+  const uint32_t bar = sb + C::kOffBar;
+  // barrier map: fp16 full[e] 0..2, free[e] 3..5; q4 ofull[2] 0..1, ofree[2] 2..3, pfull[2] 4..5, pfree[2] 6..7
+  constexpr int kS = Q4 ? 8 : 6;
+  auto s_full = [&](int b) { return bar + 8u * (kS + b); };
+  auto p_full = [&](int b) { return bar + 8u * (kS + 2 + b); };
+  const uint32_t o_bar = bar + 8u * (kS + 4);
+  const uint32_t drain = bar + 8u * (kS + 5);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::kOffBar + C::kBars * 8);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  float* red = reinterpret_cast<float*>(smem + kLOffRed);
-  float* s_row = reinterpret_cast<float*>(smem + kLOffRow);
+  float* red = reinterpret_cast<float*>(smem + C::kOffRed);
 
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int split = blockIdx.x, nsplit = gridDim.x, g = blockIdx.y;
@@ -742,7 +806,7 @@ __global__ void __launch_bounds__(kLongThreads, 1) gda_long_kernel(FusedArgs f, 
   asm volatile("griddepcontrol.wait;\n" ::: "memory");
   const int pos = f.pos_len[0], kv_len = max(0, min(f.pos_len[1], (int)cap));
   int p0, p1, n_active;
-  split_range(kv_len, nsplit, split, p0, p1, n_active);
+  long_split_range(kv_len, nsplit, split, p0, p1, n_active);
   if (n_active < 1) n_active = 1;
   if (split >= n_active) return;
   const bool append = pos >= 0 && pos < cap && ((pos >= p0 && pos < p1) || (split == 0 && pos >= kv_len));
@@ -750,7 +814,12 @@ __global__ void __launch_bounds__(kLongThreads, 1) gda_long_kernel(FusedArgs f, 
 
   if (threadIdx.x < half) rope_angle(threadIdx.x, pos, f.inv_freq, s_cs[threadIdx.x], s_sn[threadIdx.x]);
   if (threadIdx.x == 0) {
-    for (int i = 0; i < kLNumBars; ++i) tc::mbar_init(bar + 8u * i, (i == 2 * kLRing + 2 || i == 2 * kLRing + 3) ? 4 : 1);
+    for (int i = 0; i < C::kBars; ++i) {
+      int cnt = 1;
+      if (i == kS + 2 || i == kS + 3) cnt = 4;                     // p_full: the four softmax warps
+      if (Q4 && (i <= 1 || i == 6 || i == 7)) cnt = 8;             // ofull, pfree: the dequant warps
+      tc::mbar_init(bar + 8u * i, cnt);
+    }
     *abort_flag = 0;
     tc::mbar_fence_init();
   }
@@ -759,8 +828,8 @@ __global__ void __launch_bounds__(kLongThreads, 1) gda_long_kernel(FusedArgs f, 
     tc::tmem_relinquish();
   }
   // zero the Q and Pᵀ tiles (rows past NH stay zero: padded heads)
-  for (int i = threadIdx.x; i < 16384 / 16; i += kLongThreads)
-    reinterpret_cast<uint4*>(smem + kLOffQ)[i] = make_uint4(0, 0, 0, 0);
+  for (int i = threadIdx.x; i < 16384 / 16; i += C::kThreads)
+    reinterpret_cast<uint4*>(smem + C::kOffQ)[i] = make_uint4(0, 0, 0, 0);
   tc::tc_fence_before();
   __syncthreads();
   tc::tc_fence_after();
@@ -770,57 +839,115 @@ __global__ void __launch_bounds__(kLongThreads, 1) gda_long_kernel(FusedArgs f, 
   if (append && warp < 4) {
     const int head = warp < 2 ? f.q_heads + 2 * g + warp : f.q_heads + 2 * f.groups + 2 * g + (warp - 2);
     const __half* src = f.qkv + (int64_t)head * D;
-    __half* dst = static_cast<__half*>(f.cache.data[warp]) + ((int64_t)g * cap + pos) * D + lane * 4;
+    const int64_t row = (int64_t)g * cap + pos;
+    __half hv[4];
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       const int c = lane * 4 + j, k = c < half ? c : c - half;
-      dst[j] = __float2half_rn(warp < 2 ? rope_rotate(src, c, half, s_cs[k], s_sn[k]) : __half2float(src[c]));
+      hv[j] = __float2half_rn(warp < 2 ? rope_rotate(src, c, half, s_cs[k], s_sn[k]) : __half2float(src[c]));
+    }
+    if constexpr (!Q4) {
+      __half* dst = static_cast<__half*>(f.cache.data[warp]) + row * D + lane * 4;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) dst[j] = hv[j];
+    } else {
+      float* s_row = reinterpret_cast<float*>(smem + C::kOffRow) + warp * D;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) s_row[lane * 4 + j] = __half2float(hv[j]);
+      __syncwarp();
+      const bool act = lane < D / 8;
+      float x8[8];
+#pragma unroll
+      for (int t = 0; t < 8; ++t) x8[t] = act ? s_row[lane * 8 + t] : 0.f;
+      uint32_t words[2];
+      float scv, biv;
+      quant_group<8>(x8, 4, words, scv, biv);
+      if (act) {
+        static_cast<uint32_t*>(f.cache.data[warp])[row * (D / 8) + lane] = words[0];
+        if ((lane * 8) % 64 == 0) {
+          const int64_t gi = row * (D / 64) + (lane * 8) / 64;
+          static_cast<__half*>(f.cache.scales[warp])[gi] = __float2half_rn(scv);
+          static_cast<__half*>(f.cache.biases[warp])[gi] = __float2half_rn(biv);
+        }
+      }
     }
     asm volatile("fence.proxy.async.global;\n" ::: "memory");  // the TMA loads below read this row
   }
   // ---- rotated q of the group's heads, fp16, into the K-major Q tiles ----
-  for (int i = threadIdx.x; i < NH * D; i += kLongThreads) {
+  for (int i = threadIdx.x; i < NH * D; i += C::kThreads) {
     const int h = i / D, c = i - h * D, k = c < half ? c : c - half;
     const __half* src = f.qkv + (int64_t)fused_head<NA, NB, PAIRED>(g, h, f.q_origin) * D;
     const __half v = __float2half_rn(rope_rotate(src, c, half, s_cs[k], s_sn[k]));
     const int tile = h < NA ? 0 : 1, row = h < NA ? h : h - NA;
-    *reinterpret_cast<__half*>(smem + kLOffQ + tile * 4096 + kmaj16_off(row, c)) = v;
+    *reinterpret_cast<__half*>(smem + C::kOffQ + tile * 4096 + kmaj16_off(row, c)) = v;
   }
   tc::fence_proxy_async_smem();
   __syncthreads();
 
-  float m_ref[NH], L[NH];
+  const int64_t row0 = (int64_t)g * cap + p0;
   if (warp == 0) {
-    if (lane == 0) {  // ---- TMA producer: (k1,k2) then (v1,v2) per tile ----
-      int issued = 0;
-      for (int u = 0; u < 2 * nt; ++u) {
-        const int e = u % kLRing, r = u / kLRing;
-        if (u >= kLRing && !tc::mbar_wait(freeb(e), (r - 1) & 1)) { *abort_flag = 1; break; }
-        if (*abort_flag) break;
-        const int j = u >> 1, sl = (u & 1) * 2;
-        const int row = (int)((int64_t)g * cap + p0 + j * kLT);
-        const uint32_t dst = sb + e * 65536;
-        tc::mbar_expect_tx(full(e), 65536);
-        tc::tma_load_2d(dst, &tm.slot[sl], 0, row, full(e));
-        tc::tma_load_2d(dst + 16384, &tm.slot[sl], 128, row, full(e));
-        tc::tma_load_2d(dst + 32768, &tm.slot[sl + 1], 0, row, full(e));
-        tc::tma_load_2d(dst + 49152, &tm.slot[sl + 1], 128, row, full(e));
-        issued = u + 1;
+    if (lane == 0) {  // ---- TMA producer ----
+      if constexpr (!Q4) {  // (k1,k2) then (v1,v2) operand tiles per tile
+        auto full = [&](int e) { return bar + 8u * e; };
+        auto freeb = [&](int e) { return bar + 8u * (C::kRing + e); };
+        int issued = 0;
+        for (int u = 0; u < 2 * nt; ++u) {
+          const int e = u % C::kRing, r = u / C::kRing;
+          if (u >= C::kRing && !tc::mbar_wait(freeb(e), (r - 1) & 1)) { *abort_flag = 1; break; }
+          if (*abort_flag) break;
+          const int jj = u >> 1, sl = (u & 1) * 2;
+          const int row = (int)(row0 + jj * kLT);
+          const uint32_t dst = sb + e * 65536;
+          tc::mbar_expect_tx(full(e), 65536);
+          tc::tma_load_2d(dst, &tm.slot[sl], 0, row, full(e));
+          tc::tma_load_2d(dst + 16384, &tm.slot[sl], 128, row, full(e));
+          tc::tma_load_2d(dst + 32768, &tm.slot[sl + 1], 0, row, full(e));
+          tc::tma_load_2d(dst + 49152, &tm.slot[sl + 1], 128, row, full(e));
+          issued = u + 1;
+        }
+        for (int u = issued > C::kRing ? issued - C::kRing : 0; u < issued; ++u)
+          if (!tc::mbar_wait(full(u % C::kRing), (u / C::kRing) & 1)) *abort_flag = 1;
+      } else {  // packed rows of the four slots per tile
+        auto pfull = [&](int e) { return bar + 8u * (4 + e); };
+        auto pfree = [&](int e) { return bar + 8u * (6 + e); };
+        int issued = 0;
+        for (int jj = 0; jj < nt; ++jj) {
+          const int e = jj & 1;
+          if (jj >= 2 && !tc::mbar_wait(pfree(e), ((jj >> 1) - 1) & 1)) { *abort_flag = 1; break; }
+          if (*abort_flag) break;
+          const int row = (int)(row0 + jj * kLT);
+          const uint32_t dst = sb + C::kOffPk + e * C::kPacked;
+          tc::mbar_expect_tx(pfull(e), C::kPacked);
+#pragma unroll
+          for (int sl = 0; sl < 4; ++sl) {
+            tc::tma_load_2d(dst + sl * 8192, &tm.slot[sl], 0, row, pfull(e));
+            tc::tma_load_2d(dst + 32768 + sl * 512, &tm.sc[sl], 0, row / 4, pfull(e));
+            tc::tma_load_2d(dst + 34816 + sl * 512, &tm.bi[sl], 0, row / 4, pfull(e));
+          }
+          issued = jj + 1;
+        }
+        for (int jj = issued > 2 ? issued - 2 : 0; jj < issued; ++jj)
+          if (!tc::mbar_wait(pfull(jj & 1), (jj >> 1) & 1)) *abort_flag = 1;
       }
-      for (int u = issued > kLRing ? issued - kLRing : 0; u < issued; ++u)
-        if (!tc::mbar_wait(full(u % kLRing), (u / kLRing) & 1)) *abort_flag = 1;
     }
   } else if (warp == 1) {
     if (lane == 0) {  // ---- MMA issuer ----
       constexpr uint32_t idesc_qk = tc::idesc_f16_f32(kLT, 16);
       constexpr uint32_t idesc_pv = tc::idesc_f16_f32(kLT, 16, false, true);
-      const uint32_t qs = sb + kLOffQ, qn = sb + kLOffQ + 4096;
-      auto issue_qk = [&](int j) -> bool {
-        const int u = 2 * j, e = u % kLRing;
-        if (!tc::mbar_wait(full(e), (u / kLRing) & 1)) return false;
+      const uint32_t qs = sb + C::kOffQ, qn = sb + C::kOffQ + 4096;
+      // operand entry holding K(j) / V(j), the barrier saying it is ready, and the one to free
+      auto k_entry = [&](int jj) { return Q4 ? 0 : (2 * jj) % 3; };
+      auto v_entry = [&](int jj) { return Q4 ? 1 : (2 * jj + 1) % 3; };
+      auto ready = [&](int e, int use) -> bool {  // `use`: how many times this entry was filled before
+        return tc::mbar_wait(bar + 8u * e, use & 1);
+      };
+      auto freebar = [&](int e) { return bar + 8u * ((Q4 ? 2 : 3) + e); };
+      auto issue_qk = [&](int jj) -> bool {
+        const int e = k_entry(jj);
+        if (!ready(e, Q4 ? jj : (2 * jj) / 3)) return false;
         tc::tc_fence_after();
         const uint32_t kb = sb + e * 65536;
-        const uint32_t col = (j & 1) * 32;
+        const uint32_t col = (jj & 1) * 32;
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
           const uint32_t ko = (kk >> 2) * 16384 + (kk & 3) * 32, qo = (kk >> 2) * 2048 + (kk & 3) * 32;
@@ -828,30 +955,37 @@ __global__ void __launch_bounds__(kLongThreads, 1) gda_long_kernel(FusedArgs f, 
           tc::mma_f16(tmem + col + 16, tc::desc_kmajor_sw128(kb + 32768 + ko), tc::desc_kmajor_sw128(qn + qo),
                       idesc_qk, kk > 0);
         }
-        tc::mma_commit(s_full(j & 1));
-        tc::mma_commit(freeb(e));
+        tc::mma_commit(s_full(jj & 1));
+        tc::mma_commit(freebar(e));
         return true;
       };
-      bool ok = nt == 0 || issue_qk(0);
-      for (int j = 0; ok && j < nt; ++j) {
-        if (*abort_flag) { ok = false; break; }
-        if (j + 1 < nt && !issue_qk(j + 1)) { ok = false; break; }
-        const int u = 2 * j + 1, e = u % kLRing;
-        if (!tc::mbar_wait(p_full(j & 1), (j >> 1) & 1) || !tc::mbar_wait(full(e), (u / kLRing) & 1)) {
-          ok = false;
-          break;
-        }
+      auto issue_pv = [&](int jj) -> bool {
+        const int e = v_entry(jj);
+        if (!tc::mbar_wait(p_full(jj & 1), (jj >> 1) & 1) || !ready(e, Q4 ? jj : (2 * jj + 1) / 3)) return false;
         tc::tc_fence_after();
-        const uint32_t vb = sb + e * 65536, pb = sb + kLOffP + (j & 1) * 4096;
+        const uint32_t vb = sb + e * 65536, pb = sb + C::kOffP + (jj & 1) * 4096;
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
           const uint64_t bdesc = tc::desc_kmajor_sw128(pb + (kk >> 2) * 2048 + (kk & 3) * 32);
-          tc::mma_f16(tmem + 64, tc::desc_mnmajor_sw128(vb + kk * 2048, 16384, 1024), bdesc, idesc_pv, (j | kk) != 0);
+          tc::mma_f16(tmem + 64, tc::desc_mnmajor_sw128(vb + kk * 2048, 16384, 1024), bdesc, idesc_pv,
+                      (jj | kk) != 0);
           tc::mma_f16(tmem + 80, tc::desc_mnmajor_sw128(vb + 32768 + kk * 2048, 16384, 1024), bdesc, idesc_pv,
-                      (j | kk) != 0);
+                      (jj | kk) != 0);
         }
         tc::mma_commit(o_bar);
-        tc::mma_commit(freeb(e));
+        tc::mma_commit(freebar(e));
+        return true;
+      };
+      bool ok = nt == 0 || issue_qk(0);
+      for (int jj = 0; ok && jj < nt; ++jj) {
+        if (*abort_flag) { ok = false; break; }
+        if constexpr (!Q4) {  // QK one tile ahead: its K tile is already in the ring
+          if (jj + 1 < nt && !issue_qk(jj + 1)) { ok = false; break; }
+          if (!issue_pv(jj)) { ok = false; break; }
+        } else {  // K(j+1) is dequantized into the one K entry after QK(j): PV(j) first
+          if (!issue_pv(jj)) { ok = false; break; }
+          if (jj + 1 < nt && !issue_qk(jj + 1)) { ok = false; break; }
+        }
       }
       if (!ok) *abort_flag = 1;
       tc::mma_commit(drain);
@@ -861,6 +995,7 @@ __global__ void __launch_bounds__(kLongThreads, 1) gda_long_kernel(FusedArgs f, 
   } else if (warp < 6) {  // ---- softmax: thread = position of the tile, later = channel ----
     const int sw = warp - 2, q = warp & 3, r = q * 32 + lane;
     const uint32_t trow = tmem + ((uint32_t)(q * 32) << 16);
+    float m_ref[NH], L[NH];
 #pragma unroll
     for (int h = 0; h < NH; ++h) {
       m_ref[h] = -INFINITY;
@@ -918,10 +1053,11 @@ __global__ void __launch_bounds__(kLongThreads, 1) gda_long_kernel(FusedArgs f, 
         pv[h] = __float2half_rn(x[h] == -INFINITY ? 0.f : exp2f(x[h] - m_ref[h]));
         L[h] += __half2float(pv[h]);
       }
-      // Pᵀ buffer (j mod 2) was read by PV(j-2); a rescale of O needs PV(j-1) finished
-      bool okw = observe(j - 1);
+      // PV(0 .. j-1) observed in order before P(j) is written: PV(j) cannot complete before that,
+      // so no o_bar wait ever has two completed phases behind it (its parity stays unambiguous);
+      // O is then also stable for the rescale.
+      const bool okw = observe(j);
       if (okw && any_need && j > 0) {
-        okw = observe(j);
         if (__all_sync(0xffffffffu, okw)) {
           tc::tc_fence_after();
 #pragma unroll
@@ -937,7 +1073,7 @@ __global__ void __launch_bounds__(kLongThreads, 1) gda_long_kernel(FusedArgs f, 
         }
       }
       if (!okw) *abort_flag = 1;  // caught by the next tile's barrier (or the final wait)
-      uint8_t* pt = smem + kLOffP + (j & 1) * 4096;
+      uint8_t* pt = smem + C::kOffP + (j & 1) * 4096;
 #pragma unroll
       for (int h = 0; h < NH; ++h) *reinterpret_cast<__half*>(pt + kmaj16_off(h, r)) = pv[h];
       tc::fence_proxy_async_smem();
@@ -961,15 +1097,56 @@ __global__ void __launch_bounds__(kLongThreads, 1) gda_long_kernel(FusedArgs f, 
     }
     tc::named_sync(1, 128);
     constexpr int stride = 2 * D + 2;
+    const bool any = nt > 0 && fin;
 #pragma unroll
     for (int h = 0; h < NH; ++h) {
       float* base = f.ws + ((int64_t)fused_head<NA, NB, PAIRED>(g, h, f.q_origin) * nsplit + split) * stride;
-      const bool any = nt > 0 && fin;
       base[2 + r] = any ? __uint_as_float(o1[h]) : 0.f;
       base[2 + D + r] = any ? __uint_as_float(o2[h]) : 0.f;
       if (r == 0) {
         base[0] = any ? m_ref[h] : -INFINITY;
         base[1] = any ? (lred[h] + lred[16 + h]) + (lred[32 + h] + lred[48 + h]) : 0.f;
+      }
+    }
+  } else if constexpr (Q4) {  // ---- dequantize packed tiles into the operand entries ----
+    const int t = threadIdx.x - 192;  // 0..255: slot (t >> 7) of the pair, row (t & 127)
+    const int sp = t >> 7, p = t & 127;
+    auto ofull = [&](int e) { return bar + 8u * e; };
+    auto ofree = [&](int e) { return bar + 8u * (2 + e); };
+    auto pfull = [&](int e) { return bar + 8u * (4 + e); };
+    auto pfree = [&](int e) { return bar + 8u * (6 + e); };
+    for (int u = 0; u < 2 * nt; ++u) {
+      const int jj = u >> 1, part = u & 1, e = jj & 1;
+      bool okd = true;
+      if (part == 0) okd = tc::mbar_wait(pfull(e), (jj >> 1) & 1);
+      if (okd && jj > 0) okd = tc::mbar_wait(ofree(part), (jj - 1) & 1);  // MMA done with this entry's last use
+      if (__any_sync(0xffffffffu, !okd || *abort_flag)) {
+        *abort_flag = 1;
+        break;
+      }
+      const int sl = part * 2 + sp;
+      const uint8_t* pk = smem + C::kOffPk + e * C::kPacked;
+      const uint4* codes = reinterpret_cast<const uint4*>(pk + sl * 8192 + p * 64);
+      const __half2 sc2 = *reinterpret_cast<const __half2*>(pk + 32768 + sl * 512 + p * 4);
+      const __half2 bi2 = *reinterpret_cast<const __half2*>(pk + 34816 + sl * 512 + p * 4);
+      uint8_t* dst = smem + part * 65536 + sp * 32768 + p * 128;
+#pragma unroll
+      for (int v = 0; v < 4; ++v) {
+        const uint4 cw = codes[v];
+        const uint32_t wv[4] = {cw.x, cw.y, cw.z, cw.w};
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const int w = v * 4 + k;  // channels 8w .. 8w+7, group w >> 3
+          const __half2 s2 = __half2half2(w < 8 ? __low2half(sc2) : __high2half(sc2));
+          const __half2 b2 = __half2half2(w < 8 ? __low2half(bi2) : __high2half(bi2));
+          *reinterpret_cast<uint4*>(dst + (w >> 3) * 16384 + (((w & 7) ^ (p & 7)) << 4)) = dq_word(wv[k], s2, b2);
+        }
+      }
+      tc::fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        tc::mbar_arrive(ofull(part));
+        if (part == 1) tc::mbar_arrive(pfree(e));
       }
     }
   }
@@ -1306,19 +1483,20 @@ cudaError_t launch_fused(const FusedArgs& f, dim3 grid, int bits, int gs, cudaSt
                    : launch_fused_one<NA, NB, PAIRED, PPW, 8, 16>(f, grid, st);
 }
 
-template <int NA, int NB, bool PAIRED>
-cudaError_t launch_long_one(const FusedArgs& f, const LongMaps& m, dim3 grid, cudaStream_t st) {
-  auto kern = gda_long_kernel<NA, NB, PAIRED>;
+template <int NA, int NB, bool PAIRED, int BITS>
+cudaError_t launch_long_bits(const FusedArgs& f, const LongMaps& m, dim3 grid, cudaStream_t st) {
+  auto kern = gda_long_kernel<NA, NB, PAIRED, BITS>;
+  constexpr int smem = long_smem<BITS>();
   static bool configured = false;
   if (!configured) {
-    const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kLSmem);
+    const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
     configured = true;
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
-  cfg.blockDim = dim3(kLongThreads);
-  cfg.dynamicSmemBytes = kLSmem;
+  cfg.blockDim = dim3(LongCfg<BITS>::kThreads);
+  cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -1328,6 +1506,12 @@ cudaError_t launch_long_one(const FusedArgs& f, const LongMaps& m, dim3 grid, cu
   return cudaLaunchKernelEx(&cfg, kern, f, m);
 }
 
+template <int NA, int NB, bool PAIRED>
+cudaError_t launch_long_one(const FusedArgs& f, const LongMaps& m, dim3 grid, cudaStream_t st) {
+  return f.cache.bits == 16 ? launch_long_bits<NA, NB, PAIRED, 16>(f, m, grid, st)
+                            : launch_long_bits<NA, NB, PAIRED, 4>(f, m, grid, st);
+}
+
 // Caches at least this long (capacity, fp16) take the tensor-core step; MOTIF_LONG_ATTN_MIN_CAP
 // overrides it (0 = always, a huge value = never).
 int64_t long_min_cap() {
@@ -1335,13 +1519,26 @@ int64_t long_min_cap() {
   return v ? atoll(v) : 2048;
 }
 
-// The tensor-core step's maps over the four fp16 slots, or false when the cache does not fit it.
+// The tensor-core step's maps over the four slots (fp16, or q4 group 64 with the capacity a
+// multiple of 4), or false when the cache does not fit it.
 bool long_maps(const motif_kv4_slots& c, LongMaps& m) {
-  if (c.bits != 16 || c.capacity < long_min_cap() || c.heads >= kLErrSlot || c.heads * c.capacity >= (1ll << 31))
-    return false;
+  if (c.capacity < long_min_cap() || c.heads >= kLErrSlot || c.heads * c.capacity >= (1ll << 31)) return false;
+  const bool q4 = c.bits == 4 && c.group_size == 64 && c.capacity % 4 == 0;
+  if (c.bits != 16 && !q4) return false;
+  const uint64_t rows = (uint64_t)(c.heads * c.capacity);
   for (int i = 0; i < 4; ++i) {
-    if (reinterpret_cast<uintptr_t>(c.data[i]) % 16) return false;
-    if (!encode_tma_rows(&m.slot[i], c.data[i], 256, (uint64_t)(c.heads * c.capacity), 128, kLT, true)) return false;
+    if (c.bits == 16) {
+      if (reinterpret_cast<uintptr_t>(c.data[i]) % 16) return false;
+      if (!encode_tma_rows(&m.slot[i], c.data[i], 256, rows, 128, kLT, true)) return false;
+    } else {
+      if ((reinterpret_cast<uintptr_t>(c.data[i]) | reinterpret_cast<uintptr_t>(c.scales[i]) |
+           reinterpret_cast<uintptr_t>(c.biases[i])) % 16)
+        return false;
+      if (!encode_tma_rows(&m.slot[i], c.data[i], 64, rows, 64, kLT, false) ||
+          !encode_tma_rows(&m.sc[i], c.scales[i], 16, rows / 4, 16, kLT / 4, false) ||
+          !encode_tma_rows(&m.bi[i], c.biases[i], 16, rows / 4, 16, kLT / 4, false))
+        return false;
+    }
   }
   return true;
 }

@@ -26,11 +26,12 @@ def _run_step(N, mode, tq, inv, slots, pos_t, d, G, gr, t_sub, t_lam, lam_len, o
                                            ws.data_ptr(), wb, N.stream())
 
 
+@pytest.mark.parametrize("kind", ["fp16", "q4"])
 @pytest.mark.parametrize("mode,gr", [("gda", 3), ("vanilla", 4), ("vanilla", 1)])
 @pytest.mark.parametrize("kv_len", [1, 130, 3000, 16000])
-def test_long_decode_step_matches_oracle_and_short_path(cuda, monkeypatch, mode, gr, kv_len):
+def test_long_decode_step_matches_oracle_and_short_path(cuda, monkeypatch, kind, mode, gr, kv_len):
     from mlx_motif import _native as N
-    from mlx_motif.cache import MotifGroupedKVCache
+    from mlx_motif.cache import MotifGroupedKVCache, MotifGroupedQuantizedKVCache
     from mlx_motif.model import rope_inv_freq
 
     d, cap = 128, 16384
@@ -43,10 +44,15 @@ def test_long_decode_step_matches_oracle_and_short_path(cuda, monkeypatch, mode,
     qkv = rounded(rng.standard_normal(qh * d + 4 * G * d), "float16")
 
     def make():
-        c = MotifGroupedKVCache(max_size=cap)
-        if pos:
-            c.update_and_fetch_4(*(up(h) for h in hist))
+        if kind == "fp16":
+            c = MotifGroupedKVCache(max_size=cap)
+            if pos:
+                c.update_and_fetch_4(*(up(h) for h in hist))
         else:
+            c = MotifGroupedQuantizedKVCache(64, 4, max_size=cap)
+            if pos:
+                c.update_and_fetch_4_quantized(*(up(h) for h in hist))
+        if not pos:
             c._grow(1, G, 1, d, torch.float16, cuda)
         return c
 
@@ -72,11 +78,22 @@ def test_long_decode_step_matches_oracle_and_short_path(cuda, monkeypatch, mode,
         assert torch.equal(ws[:256], torch.zeros(256, dtype=torch.uint8, device=cuda)), f"{path}: control words"
         outs[path], caches[path] = res[0], c
     for n in ("k1", "k2", "v1", "v2"):
-        assert torch.equal(getattr(caches["long"], n)[..., :kv_len, :], getattr(caches["short"], n)[..., :kv_len, :])
+        a, b = getattr(caches["long"], n), getattr(caches["short"], n)
+        for x, y in (zip(a, b) if isinstance(a, tuple) else [(a, b)]):
+            assert torch.equal(x[..., :kv_len, :], y[..., :kv_len, :]), f"cache slot {n} differs"
     assert_close(down(outs["long"]), down(outs["short"]), "float16", what="long vs short step")
-    # oracle on the stored rows
+    # oracle on the stored rows (dequantized in fp32 for q4, as the quantized SDPA reads them)
     c = caches["long"]
-    k1, k2, v1, v2 = (down(getattr(c, n)[..., :kv_len, :]) for n in ("k1", "k2", "v1", "v2"))
+
+    def rows(n):
+        t = getattr(c, n)
+        if kind == "fp16":
+            return down(t[..., :kv_len, :])
+        dd, ss, bb = (x[..., :kv_len, :].cpu() for x in t)
+        return O.dequantize(dd.numpy().view(np.uint32), ss.float().numpy(), bb.float().numpy(), 64, 4,
+                            out_dtype=np.float32)
+
+    k1, k2, v1, v2 = (rows(n) for n in ("k1", "k2", "v1", "v2"))
     if mode == "gda":
         q = qkv[: qh * d].reshape(1, qh, 1, d)
         qr = O.rope(q, pos).astype(np.float16)
@@ -88,5 +105,6 @@ def test_long_decode_step_matches_oracle_and_short_path(cuda, monkeypatch, mode,
         qr = O.rope(q, pos).astype(np.float16)
         K = np.stack([k1, k2], axis=2).reshape(1, 2 * G, kv_len, d)
         V_paired = np.concatenate([v1, v2], axis=1)[:, O.vanilla_v_slab_to_paired_perm(G)]
-        ref = O.vanilla_attention_reference(qr, K, V_paired, O.OracleVanillaKVCache(), lam, 0.35, subln, 1e-5)
+        ref = O.vanilla_attention_reference(qr, K, V_paired, O.OracleVanillaKVCache(), lam, 0.35, subln, 1e-5,
+                                            kv_dtype=np.float16 if kind == "fp16" else np.float32)
     assert_close(down(outs["long"]), ref.reshape(-1).astype(np.float64), "float16", what="long step vs oracle")
