@@ -433,6 +433,32 @@ MOTIF_API int motif_embed_rms_norm(int dtype, const int32_t* token_dev, const vo
 MOTIF_API int motif_embed_rms_norm_rows(int dtype, const int32_t* tokens_dev, int64_t rows, const void* table,
                                         int64_t vocab, int64_t dim, const void* w, float eps, void* h, void* y,
                                         void* stream);
+/* ---- sampling ------------------------------------------------------------
+ * Temperature sampling of `rows` logit rows (fp16, row_stride apart) by the
+ * Gumbel-max rule — token = argmax(l/T + g), g = -log(-log u), u from
+ * Philox-4x32-10 keyed by `seed` and counted by (element, position, row,
+ * stream_id) — which draws exactly from softmax(l/T) (top-p 1.0). T = 0 is the
+ * greedy argmax. position = *pos_dev when given (a replayed graph draws fresh
+ * numbers at every position), else pos_host. pos_len_inc (optional int32[2])
+ * is advanced by one after row 0, as the decode step's head does. Reference:
+ * mlx-lm generate_step's categorical sampler at temperature T. */
+MOTIF_API int motif_sample(const void* logits, int64_t rows, int64_t n, int64_t row_stride, float temperature,
+                           uint64_t seed, const int32_t* pos_dev, int64_t pos_host, uint32_t stream_id,
+                           int32_t* tokens, void* pos_len_inc, void* stream);
+
+/* Speculative acceptance of k draft tokens (rejection sampling, the reference's
+ * MotifSpeculativeDecoding): p_logits are the target's k+1 rows (positions of
+ * the draft tokens and the bonus position), q_logits the draft's k rows, both
+ * fp16 with row_stride. Draft token i is accepted with probability
+ * min(1, p_i(x_i)/q_i(x_i)); at the first rejection the next token is drawn
+ * from max(0, p_i - q_i) renormalised, after k acceptances from p_k. T = 0:
+ * accept while the draft equals the target's argmax, next token = that row's
+ * argmax (q_logits may be NULL). out: int32[2] = {accepted, next token}. */
+MOTIF_API int motif_speculative_accept(const void* p_logits, const void* q_logits, int64_t row_stride,
+                                       const int32_t* draft_tokens, int64_t k, int64_t n, float temperature,
+                                       uint64_t seed, const int32_t* pos_dev, int64_t pos_host, int32_t* out,
+                                       void* stream);
+
 /* Greedy sampler: first index of the maximum of logits (n,) -> *out_index
  * (argmax at temperature 0 in mlx_lm generate_step). */
 MOTIF_API size_t motif_argmax_workspace_bytes(int64_t n);

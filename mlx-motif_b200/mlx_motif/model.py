@@ -410,6 +410,10 @@ class MotifDecoder:
         self.argmax_ws_bytes = lib.motif_argmax_workspace_bytes(self.V_local)
         self.argmax_ws = torch.zeros(self.argmax_ws_bytes, dtype=torch.uint8, device=dev)
         self.offset = 0  # host mirror of pos_len[0]
+        # Sampling of the head: 0 = greedy (fused argmax); > 0 = temperature (set_sampling).
+        self.temperature = 0.0
+        self.seed = 0
+        self.stream_id = 0
         self._graphs: dict[bool, torch.cuda.CUDAGraph] = {}
         self.pinned_in = torch.zeros(1, dtype=torch.int32).pin_memory()
         self.pinned_out = torch.zeros(1, dtype=torch.int32).pin_memory()
@@ -579,7 +583,7 @@ class MotifDecoder:
             plan.append((qkv_io, o_io, gu_io, dn_io))
         # The lm_head GEMV also picks the greedy token and advances pos_len (MOTIF_FUSED_ARGMAX=0: separate
         # argmax launches).
-        self.fused_argmax = tp or os.environ.get("MOTIF_FUSED_ARGMAX", "1") != "0"
+        self.fused_argmax = tp or (os.environ.get("MOTIF_FUSED_ARGMAX", "1") != "0" and self.temperature == 0)
         if tp:  # this rank's key; the ranks' keys are combined by an all-reduce
             extra = dict(argmax_key_out=ptr(self.amax_key), argmax_row_offset=self.v0)
         elif self.fused_argmax:
@@ -661,6 +665,11 @@ class MotifDecoder:
                 return
             if self.fused_argmax:
                 return  # the GEMV wrote the token and advanced pos_len
+            if self.temperature > 0:  # Gumbel-max draw from softmax(logits / T); advances pos_len
+                check(lib.motif_sample(ptr(self.logits), 1, self.V_local, self.V_local, self.temperature, self.seed,
+                                       ptr(self.pos_len), 0, self.stream_id, ptr(self.token), ptr(self.pos_len), st),
+                      "sample")
+                return
             check(lib.motif_argmax(0, ptr(self.logits), self.V_local, ptr(self.token), ptr(self.argmax_ws),
                                    self.argmax_ws_bytes, st), "argmax")
         self.pos_len.add_(self._one_one)
@@ -681,6 +690,28 @@ class MotifDecoder:
                 self._launch_step(with_head)
             self._graphs[with_head] = g
         return g
+
+    def set_sampling(self, temperature: float, seed: int = 0, stream_id: int = 0) -> None:
+        """Head mode for the following steps: greedy (temperature 0) or a Gumbel-max draw from
+        softmax(logits / temperature), seeded and counted by position (``motif_sample``)."""
+        if temperature > 0 and self.tp_group is not None:
+            raise ValueError("temperature sampling runs on one GPU (the sharded head picks greedily)")
+        self.temperature = float(temperature)
+        self.seed = int(seed)
+        self.stream_id = int(stream_id)
+        self._plan = None
+        self._graphs.clear()
+
+    def rewind(self, offset: int) -> None:
+        """Drop cache rows at and after ``offset`` (the reference cache's ``trim``): the next step
+        writes position ``offset``."""
+        if not 0 <= offset <= self.offset:
+            raise ValueError(f"rewind to {offset} outside [0, {self.offset}]")
+        self.offset = offset
+        for c in self.caches:
+            c.offset = offset
+        self.pos_len.copy_(torch.tensor([offset, offset + 1], dtype=torch.int32))
+        self._tp_reset_flags()
 
     def reset(self) -> None:
         self.pos_len.copy_(torch.tensor([0, 1], dtype=torch.int32))
@@ -749,6 +780,7 @@ class MotifDecoder:
             S=S,
             h=torch.empty((S, self.H), dtype=f16, device=dev),
             x=torch.empty((S, self.H), dtype=f16, device=dev),
+            tmp=torch.empty((S, self.H), dtype=f16, device=dev),
             qkv=torch.empty((S, L0["qkv"].out_dim), dtype=f16, device=dev),
             q=torch.empty((self.q_heads, S, d), dtype=f16, device=dev),
             o=torch.empty((S, self.q_heads, 2 * d), dtype=f16, device=dev),
@@ -788,39 +820,55 @@ class MotifDecoder:
                                            sc[i].data_ptr() + g * cap * d * 2, st), "dequantize")
         return _slots_struct(sc, 16, 64, 1, G, cap, d)
 
-    def _prefill_block(self, ids_d: torch.Tensor) -> None:
-        """One block of S prompt rows at positions [offset, offset + S): per layer input norm, qkv
-        GEMM, RoPE + cache append, causal prompt attention + combine, o_proj GEMM (+ residual),
-        post norm, gate|up GEMM, PolyNorm·up, down GEMM (+ residual) — ``MotifDecoderLayer``
-        (model.py:845-855) over the block. The block's hidden rows are not needed afterwards:
-        only its K/V rows stay (in the cache)."""
+    def _prefill_block(self, ids_d: torch.Tensor, logits_out: torch.Tensor | None = None) -> None:
+        """One block of S rows at positions [offset, offset + S): per layer input norm, qkv linear,
+        RoPE + cache append, causal attention over the cache + combine, o_proj (+ residual), post
+        norm, gate|up, PolyNorm·up, down (+ residual) — ``MotifDecoderLayer`` (model.py:845-855)
+        over the block. Blocks of at least 128 rows run the tcgen05 GEMMs with the residual
+        fused; shorter blocks (the speculative verify) run the q4 GEMV per row and fold the
+        residual into the next norm. With ``logits_out`` (S, V) the final norm and lm_head run
+        for every row (model.py:858-905); otherwise only the K/V rows stay (in the cache)."""
         S = ids_d.numel()
         off = self.offset
         if off + S + 1 > self.max_seq:
-            raise ValueError(f"KV capacity {self.max_seq} exhausted by a {S}-row prompt block at {off}")
+            raise ValueError(f"KV capacity {self.max_seq} exhausted by a {S}-row block at {off}")
         b = self._block_buffers(S)
         a = self.args
         st = stream(self.device)
         H, d, I = self.H, self.d, self.inter
         eps = a.rms_norm_eps
-        h, x = b["h"][:S], b["x"][:S]
+        h, x, tmp = b["h"][:S], b["x"][:S], b["tmp"][:S]
         qkv, o, attn = b["qkv"][:S], b["o"][:S], b["attn"][:S]
         q = b["q"].view(-1)[: self.q_heads * S * d].view(self.q_heads, S, d)  # head-major, contiguous
         gu, act, err = b["gu"][:S], b["act"][:S], b["err"]
         mode = 1 if self.vanilla else 0
+        big = S >= self.min_block_rows and self._block_ok()
 
-        def gemm(xin, ql, out, residual=None):
-            check(lib.motif_q4_gemm(ptr(xin), S, ql.in_dim, ptr(ql.weight), ptr(ql.scales), ptr(ql.biases),
-                                    ql.out_dim, ptr(out), ptr(residual) if residual is not None else None,
-                                    ptr(err), st), "q4_gemm")
+        def lin(xin, ql, out, residual=None):
+            if big:
+                check(lib.motif_q4_gemm(ptr(xin), S, ql.in_dim, ptr(ql.weight), ptr(ql.scales), ptr(ql.biases),
+                                        ql.out_dim, ptr(out), ptr(residual) if residual is not None else None,
+                                        ptr(err), st), "q4_gemm")
+            else:
+                check(lib.motif_quantized_linear(0, 4, 64, ptr(xin), S, ql.in_dim, ptr(ql.weight), ptr(ql.scales),
+                                                 ptr(ql.biases), ql.out_dim, ptr(out), ptr(self.lin_ws),
+                                                 self.lin_ws.numel(), st), "quantized_linear")
+
+        def norm_after(residual_out, w):
+            # big: the residual was added in the GEMM epilogue; small: h += residual_out, then the norm
+            if big:
+                check(lib.motif_rms_norm(0, ptr(h), ptr(w), eps, S, H, ptr(x), st), "rms_norm")
+            else:
+                check(lib.motif_add_rms_norm(0, ptr(h), ptr(residual_out), ptr(w), eps, S, H, ptr(x), st),
+                      "add_rms_norm")
 
         for li, L in enumerate(self.layers):
             if li == 0:
                 check(lib.motif_embed_rms_norm_rows(0, ptr(ids_d), S, ptr(self.embed), self.V, H,
                                                     ptr(L["input_norm"]), eps, ptr(h), ptr(x), st), "embed rows")
             else:
-                check(lib.motif_rms_norm(0, ptr(h), ptr(L["input_norm"]), eps, S, H, ptr(x), st), "rms_norm")
-            gemm(x, L["qkv"], qkv)
+                norm_after(tmp, L["input_norm"])
+            lin(x, L["qkv"], qkv)
             check(lib.motif_rope_qkv_append_rows(ptr(qkv), S, ptr(self.inv_freq), self.q_heads, self._slots[li],
                                                  off, None, ptr(q), st), "rope rows")
             slots = self._attn_slots(li, off + S)
@@ -829,16 +877,48 @@ class MotifDecoder:
             check(lib.motif_prefill_post(ptr(o), S, self.q_heads, mode, self.q_groups, self.gr, ptr(L["subln"]),
                                          ptr(L["lambda_full"]), L["lambda_full"].numel(), L["lambda_init"],
                                          a.attn_rms_norm_eps, ptr(attn), st), "prefill_post")
-            gemm(attn, L["o"], h, residual=h)
-            check(lib.motif_rms_norm(0, ptr(h), ptr(L["post_norm"]), eps, S, H, ptr(x), st), "rms_norm")
-            gemm(x, L["gate_up"], gu)
+            lin(attn, L["o"], h if big else tmp, residual=h if big else None)
+            norm_after(tmp, L["post_norm"])
+            lin(x, L["gate_up"], gu)
             check(lib.motif_polynorm_mul(0, ptr(gu), ptr(gu) + 2 * I, 2 * I, ptr(L["polynorm_w"]),
                                          ptr(L["polynorm_b"]), 1e-6, S, I, ptr(act), st), "polynorm_mul")
-            gemm(act, L["down"], h, residual=h)
+            lin(act, L["down"], h if big else tmp, residual=h if big else None)
+        if logits_out is not None:
+            norm_after(tmp, self.final_norm)
+            ql = self.lm_head
+            check(lib.motif_quantized_linear(0, 4, 64, ptr(x), S, ql.in_dim, ptr(ql.weight), ptr(ql.scales),
+                                             ptr(ql.biases), ql.out_dim, ptr(logits_out), ptr(self.lin_ws),
+                                             self.lin_ws.numel(), st), "lm_head rows")
         self._bump_host(S)
         self.pos_len.copy_(torch.tensor([self.offset, self.offset + 1], dtype=torch.int32))
         if int(err.item()) != 0:
             raise RuntimeError("prompt block: a tensor-core pipeline wait timed out")
+
+    def forward_rows(self, ids, logits_out: torch.Tensor | None = None) -> torch.Tensor:
+        """Feed a block of tokens at the current position and return their logits (S, V) fp16: the
+        batched ``[1, S]`` forward of a speculative verify (one GPU). The cache advances by S."""
+        if self.tp_group is not None:
+            raise ValueError("the row-block forward runs on one GPU")
+        ids_d = torch.as_tensor(ids, dtype=torch.int32).reshape(-1).to(self.device)
+        S = ids_d.numel()
+        if logits_out is None:
+            logits_out = torch.empty((S, self.V_local), dtype=torch.float16, device=self.device)
+        self._prefill_block(ids_d, logits_out)
+        return logits_out
+
+    def ingest(self, ids) -> None:
+        """Append tokens to the cache without producing a next token (blocks of ``min_block_rows``
+        or more on the tensor cores, the rest through the decode step without its head)."""
+        ids_d = torch.as_tensor(ids, dtype=torch.int32).reshape(-1).to(self.device)
+        n, i = ids_d.numel(), 0
+        if self.tp_group is None and self._block_ok():
+            while n - i >= self.min_block_rows:
+                S = min(2048, n - i)
+                self._prefill_block(ids_d[i : i + S])
+                i += S
+        for j in range(i, n):
+            self.token.copy_(ids_d[j : j + 1])
+            self.step_device(with_head=False)
 
     def decode_host(self, token: int) -> int:
         """Public per-token API with host buffers: H2D token, one graph replay, D2H argmax, sync."""
