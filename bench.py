@@ -18,8 +18,11 @@ Also reported in the same line:
   extra.p16k_*  config[2]: decode at a 16000-token context (KV cache filled
                 with synthetic N(0,1)·0.5 rows), q4 and fp16 4-slot caches,
                 with the attention kernels' HBM GB/s.
-  extra.vanilla_2p6b_p3204  config[3] decode: the 2.6B-class vanilla model at a
-                3204-row context (synthetic cache rows), one GPU.
+  extra.vanilla_2p6b_p3204  config[3]: the 2.6B-class vanilla model ingests a
+                3204-token prompt (tensor-core blocks), then greedy decode, one GPU.
+  extra.speculative  config[4]: that model drafts K=4 tokens per cycle for the
+                12.7B-class target (one [1, K+1] verify forward per cycle,
+                rejection sampling at T=0.7), 800-token prompt, 256 tokens.
   cpu_baseline  the CPU oracle (numpy restatement of the reference path) on
                 one full-size layer, scaled to a token.
 
@@ -64,6 +67,7 @@ def parse_args():
     ap.add_argument("--cache", choices=["fp16", "q4", "q8"], default="fp16")
     ap.add_argument("--no-long", action="store_true", help="skip the p16k extras")
     ap.add_argument("--no-vanilla", action="store_true", help="skip the config[3] 2.6B vanilla extra")
+    ap.add_argument("--no-spec", action="store_true", help="skip the config[4] speculative extra")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--layers", type=int, default=48, help="(debug) model depth; 48 is the benchmark")
     ap.add_argument("--prompt", type=int, default=164, help="prompt length (164 = config[1])")
@@ -535,9 +539,44 @@ def run_b200(a) -> None:
             "step_hbm_gbs": round(vb / (vms / a.steps / 1e3) / 1e9, 1),
             "kernels_per_step": model_launches(m),
         }
-        m._graphs.clear()
-        del m
-        torch.cuda.empty_cache()
+        # ---- config[4]: speculative decoding, this 2.6B-class draft + the 12.7B-class target ----
+        if not a.no_spec:
+            from mlx_motif.speculative import SpeculativeDecoder
+
+            m._graphs.clear()
+            del m
+            torch.cuda.empty_cache()
+            n_prompt, n_gen, K, T = 800, 256, 4, 0.7
+            cap = n_prompt + n_gen + 2 * K + 16
+            draft = MotifDecoder.random(van, seed=0, cache="fp16", max_seq=cap, device=dev)
+            target = MotifDecoder.random(args, seed=0, cache="fp16", max_seq=cap, device=dev)
+            sprompt = np.random.default_rng(4).integers(0, args.vocab_size, n_prompt).tolist()
+            spec = SpeculativeDecoder(target, draft, k=K, temperature=T, seed=0)
+            spec.generate(sprompt, 16)  # warm-up: graphs, buffers
+            spec.stats = {k2: 0 for k2 in spec.stats}
+            torch.cuda.synchronize()
+            t0 = time.perf_counter()
+            toks = spec.generate(sprompt, n_gen)
+            torch.cuda.synchronize()
+            wall = time.perf_counter() - t0
+            st_ = spec.stats
+            extra["speculative"] = {
+                "workload": "config[4]: draft 2.6B-class vanilla q4, target 12.7B-class GDA q4 (1 GPU), K=4, "
+                            "temperature 0.7, top-p 1.0, 800 random prompt ids, 256 generated tokens; wall time "
+                            "includes both prompts' ingestion",
+                "tok_s": round(len(toks) / wall, 2), "seconds": round(wall, 3),
+                "acceptance": round(st_["accepted"] / max(1, st_["drafted"]), 4),
+                "target_forwards": st_["target_forwards"], "cycles": st_["cycles"],
+                "note": "draft and target are independent random-init models, so few draft tokens match "
+                        "the target's distribution; the verify forward streams the target's weights once per "
+                        "row (K+1 GEMV passes)",
+            }
+            del spec, draft, target
+            torch.cuda.empty_cache()
+        else:
+            m._graphs.clear()
+            del m
+            torch.cuda.empty_cache()
 
     cpu = None
     if rank == 0 and world == 1 and not a.no_cpu_baseline:
