@@ -72,6 +72,10 @@ def parse_args():
     ap.add_argument("--layers", type=int, default=48, help="(debug) model depth; 48 is the benchmark")
     ap.add_argument("--prompt", type=int, default=164, help="prompt length (164 = config[1])")
     ap.add_argument("--vocab", type=int, default=219520, help="(profiling) vocabulary size; 219520 is the benchmark")
+    ap.add_argument("--kernel-case", choices=["gemm", "prefill_attn", "long_q4", "long_fp16"], default=None,
+                    help="(profiling) run one small single-kernel case --steps times and exit: the prompt GEMM "
+                         "(3204 x 16384 x 2048), a 2048-row vanilla prompt-attention block, or the long-cache "
+                         "decode step at 16000 rows (q4 / fp16 cache)")
     ap.add_argument("--profile", action="store_true",
                     help="profiler window only: cudaProfilerStart/Stop around the timed steps, then exit "
                          "(for `ncu --profile-from-start off`)")
@@ -647,6 +651,67 @@ def model_launches(model) -> int:
 # --------------------------------------------------------------------------- #
 # reference arm: the CPU oracle port
 # --------------------------------------------------------------------------- #
+def run_kernel_case(a) -> None:
+    """Small single-kernel workloads for ncu captures (one GPU; nothing is timed here)."""
+    import os
+
+    import torch
+
+    from mlx_motif import _native as N
+    from mlx_motif.cache import MotifGroupedKVCache, MotifGroupedQuantizedKVCache
+    from mlx_motif.model import rope_inv_freq
+    from mlx_motif.quantization import quantize
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    g = torch.Generator(device=dev).manual_seed(0)
+    reps = a.steps
+    if a.kernel_case == "gemm":
+        M, n, k = 3204, 16384, 2048
+        d, s, b = quantize((torch.randn((n, k), generator=g, device=dev) * 0.02).half(), 64, 4)
+        x = torch.randn((M, k), generator=g, device=dev).half()
+        y = torch.empty((M, n), dtype=torch.float16, device=dev)
+        for _ in range(reps):
+            N.check(N.lib.motif_q4_gemm(x.data_ptr(), M, k, d.data_ptr(), s.data_ptr(), b.data_ptr(), n, y.data_ptr(),
+                                        None, None, N.stream()), "q4_gemm")
+    elif a.kernel_case == "prefill_attn":
+        S, Hk, n_rep = 2048, 2, 4
+        qh = 2 * Hk * n_rep
+        c = MotifGroupedKVCache(max_size=4096)
+        c.update_and_fetch_4(*(torch.randn((1, Hk, S, 128), generator=g, device=dev).half() * 0.5 for _ in range(4)))
+        q = torch.randn((qh, S, 128), generator=g, device=dev).half()
+        o = torch.empty((S, qh, 256), dtype=torch.float16, device=dev)
+        for _ in range(reps):
+            N.check(N.lib.motif_prefill_attention(q.data_ptr(), S, qh, c.slots_struct(), 0, 1, n_rep, 128 ** -0.5,
+                                                  o.data_ptr(), None, N.stream()), "prefill_attention")
+    else:
+        os.environ["MOTIF_LONG_ATTN_MIN_CAP"] = "0"
+        G, gr, d_, L = 8, 3, 128, 16000
+        qh = G * (gr + 1)
+        if a.kernel_case == "long_q4":
+            c = MotifGroupedQuantizedKVCache(64, 4, max_size=L + 64)
+            c.update_and_fetch_4_quantized(*(torch.randn((1, G, L - 1, d_), generator=g, device=dev).half() * 0.5
+                                             for _ in range(4)))
+        else:
+            c = MotifGroupedKVCache(max_size=L + 64)
+            c.update_and_fetch_4(*(torch.randn((1, G, L - 1, d_), generator=g, device=dev).half() * 0.5
+                                   for _ in range(4)))
+        inv = rope_inv_freq(d_, 10000.0, dev)
+        pos = torch.tensor([L - 1, L], dtype=torch.int32, device=dev)
+        tq = torch.randn(qh * d_ + 4 * G * d_, generator=g, device=dev).half()
+        sub = torch.ones(2 * d_, device=dev).half()
+        lam = torch.tensor([0.3], device=dev)
+        out = torch.empty(G * gr * 2 * d_, device=dev).half()
+        wb = N.lib.motif_gda_decode_step_workspace_bytes(qh, d_, 64)
+        ws = torch.zeros(wb, dtype=torch.uint8, device=dev)
+        for _ in range(reps):
+            N.check(N.lib.motif_gda_decode_step(tq.data_ptr(), inv.data_ptr(), c.slots_struct(), pos.data_ptr(),
+                                                d_ ** -0.5, G, gr, sub.data_ptr(), lam.data_ptr(), 1, 0.8, 1e-5,
+                                                out.data_ptr(), ws.data_ptr(), wb, N.stream()), "decode step")
+    torch.cuda.synchronize()
+    print(json.dumps({"kernel_case": a.kernel_case, "launches": reps}))
+
+
 def run_reference(a) -> None:
     """Reference arm: the oracle port on all host cores; each step is one full-size layer
     sample scaled to a token. Stops early (reporting the steps done) after ~150 s."""
@@ -685,6 +750,8 @@ def main():
     a = parse_args()
     if a.impl == "reference":
         run_reference(a)
+    elif a.kernel_case:
+        run_kernel_case(a)
     else:
         run_b200(a)
 
