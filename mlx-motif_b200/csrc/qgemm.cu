@@ -6,7 +6,8 @@
 // multiplies them on the matrix units with fp32 accumulation; this kernel does the same on
 // tcgen05.
 //
-// One CTA computes a 128 × BN tile of Y (BN 256 or 128) over K in 64-wide stages:
+// One CTA computes a 128 × BN (or 256 × BN: two row tiles sharing each dequantized B tile) tile
+// of Y (BN 256 or 128) over K in 64-wide stages:
 //   warp 0      one lane issues the TMA loads of a stage: the X tile (128 rows × 128 bytes in
 //               the 128-byte swizzle, the tcgen05 K-major layout), the BN rows × 32 bytes of
 //               packed codes and the BN × 16-byte boxes of scales and biases that hold the
@@ -47,9 +48,9 @@ struct GemmArgs {
   int* err;  // optional error word (1 = a wait timed out)
 };
 
-template <int BN, int ST>
+template <int BN, int ST, int MT>
 struct GemmLayout {
-  static constexpr int kA = kGemmBM * 128;  // X tile
+  static constexpr int kA = MT * kGemmBM * 128;  // X tiles (MT stacked 128-row tiles)
   static constexpr int kB = BN * 128;       // dequantized W tile
   static constexpr int kW = BN * 32;        // packed codes
   static constexpr int kS = BN * 16;        // scales (and biases) box
@@ -80,9 +81,11 @@ __device__ __forceinline__ uint4 dequant_word(uint32_t w, __half2 s2, __half2 b2
   return o;
 }
 
-template <int BN, int ST>
+// MT = 1 or 2 row tiles of 128 per CTA: with two, both MMAs of a K step read the same
+// dequantized B tile, halving the dequant work per FLOP (accumulators: MT × BN TMEM columns).
+template <int BN, int ST, int MT>
 __global__ void __launch_bounds__(kGemmThreads, 1) q4_gemm_tc_kernel(const __grid_constant__ GemmArgs a) {
-  using L = GemmLayout<BN, ST>;
+  using L = GemmLayout<BN, ST, MT>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + ST * L::kStage);
@@ -99,7 +102,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) q4_gemm_tc_kernel(const __gri
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nk = (int)(a.K / 64);
-  const int n0 = blockIdx.x * BN, m0 = blockIdx.y * kGemmBM;
+  const int n0 = blockIdx.x * BN, m0 = blockIdx.y * kGemmBM * MT;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < ST; ++s) {
@@ -112,7 +115,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) q4_gemm_tc_kernel(const __gri
     tc::mbar_fence_init();
   }
   if (warp == 1) {
-    tc::tmem_alloc(tc::smem_addr(tmem_slot), BN);
+    tc::tmem_alloc(tc::smem_addr(tmem_slot), BN * MT);
     tc::tmem_relinquish();
   }
   tc::tc_fence_before();
@@ -133,7 +136,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1) q4_gemm_tc_kernel(const __gri
         if (*abort_flag) break;
         const uint32_t base = st_a(s);
         tc::mbar_expect_tx(full(s), L::kA + L::kW + 2 * L::kS);
-        tc::tma_load_2d(base, &a.tm_x, it * 128, m0, full(s));
+#pragma unroll
+        for (int t = 0; t < MT; ++t) tc::tma_load_2d(base + t * 16384, &a.tm_x, it * 128, m0 + t * kGemmBM, full(s));
         tc::tma_load_2d(base + L::kA + L::kB, &a.tm_w, it * 32, n0, full(s));
         tc::tma_load_2d(base + L::kA + L::kB + L::kW, &a.tm_s, (it >> 3) * 16, n0, full(s));
         tc::tma_load_2d(base + L::kA + L::kB + L::kW + L::kS, &a.tm_b, (it >> 3) * 16, n0, full(s));
@@ -156,9 +160,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1) q4_gemm_tc_kernel(const __gri
         if (*abort_flag) break;
         tc::tc_fence_after();
 #pragma unroll
-        for (int kk = 0; kk < 4; ++kk)
-          tc::mma_f16(tmem, tc::desc_kmajor_sw128(st_a(s) + kk * 32), tc::desc_kmajor_sw128(st_b(s) + kk * 32), idesc,
-                      (it | kk) != 0);
+        for (int kk = 0; kk < 4; ++kk) {
+          const uint64_t bdesc = tc::desc_kmajor_sw128(st_b(s) + kk * 32);
+#pragma unroll
+          for (int t = 0; t < MT; ++t)
+            tc::mma_f16(tmem + t * BN, tc::desc_kmajor_sw128(st_a(s) + t * 16384 + kk * 32), bdesc, idesc,
+                        (it | kk) != 0);
+        }
         tc::mma_commit(empty(s));
       }
       tc::mma_commit(acc);  // also on abort: the accumulator barrier tracks the MMAs in flight
@@ -205,13 +213,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1) q4_gemm_tc_kernel(const __gri
     if (!ok) *abort_flag = 1;
     tc::tc_fence_after();
     const int q = warp & 3, half = (warp - 2) >> 2;
-    const int64_t grow = m0 + q * 32 + lane;
+#pragma unroll 1
+    for (int t = 0; t < MT; ++t) {
+    const int64_t grow = m0 + t * kGemmBM + q * 32 + lane;
     const bool live = ok && !*abort_flag && grow < a.M;
 #pragma unroll 1
     for (int cb = 0; cb < BN / 64; ++cb) {
       const int col = half * (BN / 2) + cb * 32;
       uint32_t r[32];
-      tc::tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + col, r);
+      tc::tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + t * BN + col, r);
       tc::tmem_ld_wait();
       if (live) {
         __half* dst = a.y + grow * a.N + n0 + col;
@@ -231,28 +241,29 @@ __global__ void __launch_bounds__(kGemmThreads, 1) q4_gemm_tc_kernel(const __gri
         }
       }
     }
+    }
   }
 
   tc::tc_fence_before();
   __syncthreads();
   if (warp == 1) {
     tc::tc_fence_after();
-    tc::tmem_dealloc(tmem, BN);
+    tc::tmem_dealloc(tmem, BN * MT);
   }
   if (threadIdx.x == 0 && *abort_flag && a.err) atomicExch(a.err, 1);
 }
 
-template <int BN, int ST>
+template <int BN, int ST, int MT>
 int launch_gemm(GemmArgs& a, cudaStream_t st) {
-  using L = GemmLayout<BN, ST>;
-  auto kern = q4_gemm_tc_kernel<BN, ST>;
+  using L = GemmLayout<BN, ST, MT>;
+  auto kern = q4_gemm_tc_kernel<BN, ST, MT>;
   static bool configured = false;
   if (!configured) {
     const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kBytes);
     if (e != cudaSuccess) return fail(MOTIF_ERR_CUDA, "q4_gemm: smem attribute: %s", cudaGetErrorString(e));
     configured = true;
   }
-  const dim3 grid((unsigned)(a.N / BN), (unsigned)ceil_div(a.M, kGemmBM));
+  const dim3 grid((unsigned)(a.N / BN), (unsigned)ceil_div(a.M, kGemmBM * MT));
   kern<<<grid, kGemmThreads, L::kBytes, st>>>(a);
   return check_launch("q4_gemm");
 }
@@ -281,7 +292,20 @@ int q4_gemm(const void* x, int64_t m, int64_t k, const uint32_t* w, const void* 
   a.N = n;
   a.K = k;
   a.err = err;
-  return bn == 256 ? launch_gemm<256, 3>(a, st) : launch_gemm<128, 4>(a, st);
+  // Two row tiles per CTA when the estimated time is lower: waves × per-CTA time, a two-tile CTA
+  // taking about 1.6× a one-tile CTA (measured at 3204 × 28672 × 4096: 82 vs 51 µs per wave).
+  static int sms = 0;
+  if (!sms) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+      sms = 148;
+  }
+  if (bn == 256) {
+    const int64_t w1 = ceil_div((n / 256) * ceil_div(m, kGemmBM), sms);
+    const int64_t w2 = ceil_div((n / 256) * ceil_div(m, 2 * kGemmBM), sms);
+    if (16 * w2 < 10 * w1) return launch_gemm<256, 2, 2>(a, st);
+  }
+  return bn == 256 ? launch_gemm<256, 3, 1>(a, st) : launch_gemm<128, 4, 1>(a, st);
 }
 
 }  // namespace motif

@@ -27,10 +27,11 @@ def _dev_triple(tr, dev):
 
 
 @pytest.mark.parametrize("M,N,K", [(128, 256, 512), (300, 384, 1024), (129, 128, 2048), (1000, 3072, 2048),
-                                   (517, 2048, 8192)])
+                                   (517, 2048, 8192), (1000, 16384, 512), (1100, 38400, 512)])
 def test_q4_gemm_matches_oracle(cuda, M, N, K):
     """motif_q4_gemm (tcgen05) == oracle quantized_matmul (fp64 of the dequantized weights),
-    fp16 tolerance; rows past M are never written; the error word stays 0."""
+    fp16 tolerance; rows past M are never written; the error word stays 0. The last two shapes
+    fill a whole wave with 256-row CTAs (two row tiles per B tile, ragged last pair)."""
     from mlx_motif import _native as N_
 
     rng = np.random.default_rng(M + N + K)
