@@ -714,7 +714,7 @@ struct LongCfg<16> {
   static constexpr int kOffRed = kOffP + 8192;    // softmax scratch (768 B)
   static constexpr int kOffRow = kOffRed + 1024;  // append scratch (unused for fp16)
   static constexpr int kOffBar = kOffRow;
-  static constexpr int kBars = 2 * kRing + 6;     // full[3], free[3], s_full[2], p_full[2], o_bar, drain
+  static constexpr int kBars = 2 * kRing + 7;     // full[3], free[3], s_full[2], p_full[2], o_bar[2], drain
 };
 template <>
 struct LongCfg<4> {
@@ -726,7 +726,7 @@ struct LongCfg<4> {
   static constexpr int kOffRed = kOffP + 8192;
   static constexpr int kOffRow = kOffPk + kPacked;  // append scratch aliases packed entry 1 (free then)
   static constexpr int kOffBar = kOffRed + 1024;
-  static constexpr int kBars = 14;  // ofull[2], ofree[2], pfull[2], pfree[2], s_full[2], p_full[2], o_bar, drain
+  static constexpr int kBars = 15;  // ofull[2], ofree[2], pfull[2], pfree[2], s_full[2], p_full[2], o_bar[2], drain
 };
 template <int BITS>
 constexpr int long_smem() {
@@ -793,8 +793,10 @@ __global__ void __launch_bounds__(LongCfg<BITS>::kThreads, 1)
   constexpr int kS = Q4 ? 8 : 6;
   auto s_full = [&](int b) { return bar + 8u * (kS + b); };
   auto p_full = [&](int b) { return bar + 8u * (kS + 2 + b); };
-  const uint32_t o_bar = bar + 8u * (kS + 4);
-  const uint32_t drain = bar + 8u * (kS + 5);
+  // PV(j) completes phase j / 2 of o_bar(j mod 2): a wait for PV(k) can only have PV(k+2) (same
+  // barrier, next phase) behind it, which needs P(k+2) from the waiting thread itself.
+  auto o_bar = [&](int b) { return bar + 8u * (kS + 4 + b); };
+  const uint32_t drain = bar + 8u * (kS + 6);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::kOffBar + C::kBars * 8);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   float* red = reinterpret_cast<float*>(smem + C::kOffRed);
@@ -972,7 +974,7 @@ __global__ void __launch_bounds__(LongCfg<BITS>::kThreads, 1)
           tc::mma_f16(tmem + 80, tc::desc_mnmajor_sw128(vb + 32768 + kk * 2048, 16384, 1024), bdesc, idesc_pv,
                       (jj | kk) != 0);
         }
-        tc::mma_commit(o_bar);
+        tc::mma_commit(o_bar(jj & 1));
         tc::mma_commit(freebar(e));
         return true;
       };
@@ -1003,9 +1005,9 @@ __global__ void __launch_bounds__(LongCfg<BITS>::kThreads, 1)
     }
     int o_seen = 0;
     bool alive = true;
-    auto observe = [&](int upto) -> bool {  // PV(0 .. upto-1) complete, phases in order
+    auto observe = [&](int upto) -> bool {  // PV(0 .. upto-1) complete, in order
       while (o_seen < upto) {
-        if (!tc::mbar_wait(o_bar, o_seen & 1)) return false;
+        if (!tc::mbar_wait(o_bar(o_seen & 1), (o_seen >> 1) & 1)) return false;
         ++o_seen;
       }
       return true;
@@ -1053,11 +1055,11 @@ __global__ void __launch_bounds__(LongCfg<BITS>::kThreads, 1)
         pv[h] = __float2half_rn(x[h] == -INFINITY ? 0.f : exp2f(x[h] - m_ref[h]));
         L[h] += __half2float(pv[h]);
       }
-      // PV(0 .. j-1) observed in order before P(j) is written: PV(j) cannot complete before that,
-      // so no o_bar wait ever has two completed phases behind it (its parity stays unambiguous);
-      // O is then also stable for the rescale.
-      const bool okw = observe(j);
+      // Pᵀ buffer (j mod 2) was last read by PV(j-2); a rescale of O also needs PV(j-1) finished.
+      // PV(j-1) otherwise keeps running while this tile's softmax proceeds.
+      bool okw = observe(j - 1);
       if (okw && any_need && j > 0) {
+        okw = observe(j);
         if (__all_sync(0xffffffffu, okw)) {
           tc::tc_fence_after();
 #pragma unroll
