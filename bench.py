@@ -564,6 +564,31 @@ def run_b200(a) -> None:
             torch.cuda.synchronize()
             wall = time.perf_counter() - t0
             st_ = spec.stats
+            # one [1, K+1] verify forward (multi-row GEMVs, logits for every row) against one decode
+            # step of the target; both rewound so the cache stays at the same length
+            vids = torch.as_tensor(sprompt[: K + 1], dtype=torch.int32, device=dev)
+            plog = torch.empty((K + 1, target.V_local), dtype=torch.float16, device=dev)
+            base = target.offset
+
+            def verify_once():
+                target.forward_rows(vids, plog)
+                target.rewind(base)
+
+            def step_once():
+                target.step_device(with_head=True)
+                target.rewind(base)
+
+            rows_ms = {}
+            for name, fn in (("verify_forward_ms", verify_once), ("decode_step_ms", step_once)):
+                for _ in range(3):
+                    fn()
+                torch.cuda.synchronize()
+                e0.record(st)
+                for _ in range(10):
+                    fn()
+                e1.record(st)
+                torch.cuda.synchronize()
+                rows_ms[name] = round(e0.elapsed_time(e1) / 10, 3)
             extra["speculative"] = {
                 "workload": "config[4]: draft 2.6B-class vanilla q4, target 12.7B-class GDA q4 (1 GPU), K=4, "
                             "temperature 0.7, top-p 1.0, 800 random prompt ids, 256 generated tokens; wall time "
@@ -571,9 +596,11 @@ def run_b200(a) -> None:
                 "tok_s": round(len(toks) / wall, 2), "seconds": round(wall, 3),
                 "acceptance": round(st_["accepted"] / max(1, st_["drafted"]), 4),
                 "target_forwards": st_["target_forwards"], "cycles": st_["cycles"],
+                **rows_ms,
                 "note": "draft and target are independent random-init models, so few draft tokens match "
-                        "the target's distribution; the verify forward streams the target's weights once per "
-                        "row (K+1 GEMV passes)",
+                        "the target's distribution; the verify forward streams the target's weights once for "
+                        "its K+1 rows (multi-row GEMV); verify_forward_ms includes the host's launch gaps "
+                        "(the row block is not graph-captured) and its error-word read",
             }
             del spec, draft, target
             torch.cuda.empty_cache()

@@ -898,6 +898,208 @@ __global__ void __launch_bounds__(kTmaThreads, kTmaMinBlocks) q4_gemv_tma_kernel
   if (!ok && lane == 0 && a.err) atomicExch(a.err, 1);
 }
 
+// ---- several x rows at once: the [1, K+1] speculative verify, short prompt blocks ------------
+//
+// The weight stream of q4_gemv_tma_kernel (units of 16 rows × 512 k, a per-warp TMA ring,
+// stream-K over the grid), but the MMA's eight B columns are up to eight x rows instead of the
+// eight groups of a unit. Lane (r, c) feeds rows r and r+8 with words 2c and 2c+1 of ONE group
+// per quad of MMAs, so each MMA's 16 k values all belong to that group and C[row][x row] is
+// the group's exact dot; the MLX affine epilogue s·(C − corr) + b·Σx then runs per group and
+// per x row. Every weight byte is streamed once for all the rows. x rows are staged like the
+// one-row kernel's x (dequant order 0,4,1,5,.., odd k pre-scaled by 1/16, per-group Σx and
+// corr = 1024·Σ stored), one row every 2K + 16 bytes so the eight rows spread over the banks.
+constexpr int kRowsMax = 8;
+constexpr int kRowsSmemCap = 225 * 1024;  // one CTA per SM
+
+// Ring slots, then their barriers rounded up to 128 B, then the staged rows.
+__host__ __device__ inline size_t rows_xs_offset(int warps) {
+  return (size_t)warps * kStages * kSlotBytes + (((size_t)warps * kStages * 8 + 127) & ~(size_t)127);
+}
+
+size_t rows_xbytes(int64_t K, int R) { return (size_t)R * ((size_t)K * 2 + 16) + 2 * (size_t)R * (K / 64) * 4; }
+
+size_t rows_smem_bytes(int64_t K, int R, int warps) { return rows_xs_offset(warps) + rows_xbytes(K, R); }
+
+// Warps per CTA (up to 16) that fit beside the staged rows (each takes kStages ring slots).
+int rows_warps(int64_t K, int R) {
+  int w = 16;
+  while (w > 0 && rows_smem_bytes(K, R, w) > (size_t)kRowsSmemCap) --w;
+  return w;
+}
+
+template <int R>
+__global__ void __launch_bounds__(512, 1) q4_gemv_rows_kernel(const __grid_constant__ LinArgs a) {
+  extern __shared__ __align__(1024) unsigned char smem_rows[];
+  const int nw = blockDim.x >> 5;
+  unsigned char* ring = smem_rows;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(ring + (size_t)nw * kStages * kSlotBytes);
+  unsigned char* xs = smem_rows + rows_xs_offset(nw);
+  const int64_t K = a.K;
+  const int G = (int)(K / 64);
+  const int64_t xstride = K * 2 + 16;
+  float* corr_s = reinterpret_cast<float*>(xs + R * xstride);
+  float* xsum_s = corr_s + R * G;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int r = lane >> 2, c = lane & 3;
+  const int gw = blockIdx.x * nw + warp;
+  const uint32_t units = (uint32_t)a.units, tw = (uint32_t)a.total_warps;
+  const int u0 = gw < a.total_warps ? (int)((uint32_t)gw * units / tw) : (int)units;
+  const int u1 = gw < a.total_warps ? (int)((uint32_t)(gw + 1) * units / tw) : (int)units;
+  const int nblk = a.nblk;
+  unsigned char* my_ring = ring + (size_t)warp * kStages * kSlotBytes;
+  uint64_t* my_bars = bars + warp * kStages;
+
+  if (threadIdx.x == 0) {
+    asm volatile("prefetch.tensormap [%0];\n" ::"l"(reinterpret_cast<uint64_t>(&a.tm_w)) : "memory");
+    asm volatile("prefetch.tensormap [%0];\n" ::"l"(reinterpret_cast<uint64_t>(&a.tm_s)) : "memory");
+    asm volatile("prefetch.tensormap [%0];\n" ::"l"(reinterpret_cast<uint64_t>(&a.tm_b)) : "memory");
+  }
+  if (lane == 0) {
+    for (int i = 0; i < kStages; ++i) mbar_init(smem_u32(&my_bars[i]), 1);
+    asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+  }
+  __syncwarp();
+  // weights do not depend on the previous kernel: fill the ring before waiting for it
+  int it = u0 / nblk, ib = u0 - (u0 / nblk) * nblk;
+  if (lane == 0) {
+    for (int i = 0; i < kStages && u0 + i < u1; ++i) {
+      issue_unit(a, it, ib, smem_u32(my_ring + i * kSlotBytes), smem_u32(&my_bars[i]));
+      if (++ib == nblk) { ib = 0; ++it; }
+    }
+  }
+  grid_dep_wait();
+  grid_dep_launch();
+  // ---- stage the x rows, one (row, group) per thread step ----
+  const __half sixteenth = __float2half_rn(0.0625f);
+  for (int i = threadIdx.x; i < R * G; i += blockDim.x) {
+    const int row = i / G, g = i - row * G;
+    const __half* src = a.x + (int64_t)row * K + (int64_t)g * 64;
+    unsigned char* dst = xs + row * xstride + (int64_t)g * 128;
+    float lo = 0.f, hi = 0.f;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) {
+      const uint4 v = *reinterpret_cast<const uint4*>(src + w * 8);
+      const __half* e = reinterpret_cast<const __half*>(&v);
+      __half h[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) h[j] = (j & 1) ? __hmul(e[j], sixteenth) : e[j];
+#pragma unroll
+      for (int j = 0; j < 8; j += 2) {
+        lo += __half2float(h[j]);
+        hi += __half2float(h[j + 1]);
+      }
+      uint4 o;
+      __half* oe = reinterpret_cast<__half*>(&o);
+      oe[0] = h[0]; oe[1] = h[4]; oe[2] = h[1]; oe[3] = h[5];
+      oe[4] = h[2]; oe[5] = h[6]; oe[6] = h[3]; oe[7] = h[7];
+      *reinterpret_cast<uint4*>(dst + w * 16) = o;
+    }
+    xsum_s[row * G + g] = lo + 16.f * hi;
+    corr_s[row * G + g] = 1024.f * (lo + hi);
+  }
+  __syncthreads();
+
+  const int n0 = 2 * c, n1 = 2 * c + 1;  // this lane's x rows in C
+  float acc[4] = {0.f, 0.f, 0.f, 0.f};  // (row r, n0) (row r, n1) (row r+8, n0) (row r+8, n1)
+  bool ok = true;
+  int tile = u0 / nblk, blk = u0 - (u0 / nblk) * nblk;
+  for (int u = u0; u < u1; ++u) {
+    const int j = u - u0;
+    const int slot_i = j % kStages;
+    if (!mbar_wait(smem_u32(&my_bars[slot_i]), (uint32_t)((j / kStages) & 1))) {
+      ok = false;
+      for (int v = u + 1; v < u1 && v < u + kStages; ++v) {
+        const int jv = v - u0;
+        mbar_wait(smem_u32(&my_bars[jv % kStages]), (uint32_t)((jv / kStages) & 1));
+      }
+      break;
+    }
+    const unsigned char* slot = my_ring + slot_i * kSlotBytes;
+#pragma unroll
+    for (int gi = 0; gi < 8; ++gi) {
+      const int chunk = 2 * (gi & 3) + (c >> 1);
+      const uint32_t off = (gi >> 2) * 2048 + r * 128 + ((chunk ^ r) << 4) + (c & 1) * 8;
+      const uint2 wr = lds64(slot + off), wr8 = lds64(slot + off + 1024);
+      uint32_t P0[4], P1[4], Q0[4], Q1[4];
+      dequant_word_offset(wr.x, P0);
+      dequant_word_offset(wr.y, P1);
+      dequant_word_offset(wr8.x, Q0);
+      dequant_word_offset(wr8.y, Q1);
+      const int gg = blk * 8 + gi;
+      uint4 b0 = make_uint4(0, 0, 0, 0), b1 = make_uint4(0, 0, 0, 0);
+      if (r < R) {
+        const unsigned char* xp = xs + r * xstride + (int64_t)gg * 128 + c * 32;
+        b0 = lds128(xp);
+        b1 = lds128(xp + 16);
+      }
+      float C[4] = {0.f, 0.f, 0.f, 0.f};
+      mma16816(C, P0[0], Q0[0], P0[1], Q0[1], b0.x, b0.y);
+      mma16816(C, P0[2], Q0[2], P0[3], Q0[3], b0.z, b0.w);
+      mma16816(C, P1[0], Q1[0], P1[1], Q1[1], b1.x, b1.y);
+      mma16816(C, P1[2], Q1[2], P1[3], Q1[3], b1.z, b1.w);
+      const unsigned char* sp = slot + 4096 + r * 16 + gi * 2;
+      const float s_r = __half2float(*reinterpret_cast<const __half*>(sp));
+      const float s_r8 = __half2float(*reinterpret_cast<const __half*>(sp + 128));
+      const float b_r = __half2float(*reinterpret_cast<const __half*>(sp + 256));
+      const float b_r8 = __half2float(*reinterpret_cast<const __half*>(sp + 384));
+      const float cr0 = n0 < R ? corr_s[n0 * G + gg] : 0.f, xs0 = n0 < R ? xsum_s[n0 * G + gg] : 0.f;
+      const float cr1 = n1 < R ? corr_s[n1 * G + gg] : 0.f, xs1 = n1 < R ? xsum_s[n1 * G + gg] : 0.f;
+      acc[0] += s_r * (C[0] - cr0) + b_r * xs0;
+      acc[1] += s_r * (C[1] - cr1) + b_r * xs1;
+      acc[2] += s_r8 * (C[2] - cr0) + b_r8 * xs0;
+      acc[3] += s_r8 * (C[3] - cr1) + b_r8 * xs1;
+    }
+    __syncwarp();
+    if (lane == 0 && u + kStages < u1) {
+      issue_unit(a, it, ib, smem_u32(my_ring + slot_i * kSlotBytes), smem_u32(&my_bars[slot_i]));
+      if (++ib == nblk) { ib = 0; ++it; }
+    }
+    if (u + 1 >= u1 || blk + 1 == nblk) {
+      // ---- finish this warp's share of the tile (16 rows × up to 8 x rows) ----
+      const uint32_t u_first = (uint32_t)tile * (uint32_t)nblk;
+      const int w_first = warp_of_unit(u_first, units, tw);
+      const int w_last = warp_of_unit(u_first + nblk - 1, units, tw);
+      const int nc = w_last - w_first + 1;
+      const int64_t row0 = (int64_t)tile * kTileRows;
+      if (nc == 1) {
+        const int rr[4] = {r, r, r + 8, r + 8}, nn[4] = {n0, n1, n0, n1};
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+          if (nn[q] < R && row0 + rr[q] < a.N) a.y[(int64_t)nn[q] * a.N + row0 + rr[q]] = __float2half_rn(acc[q]);
+      } else {
+        float* p = a.partial + ((int64_t)tile * a.maxc + (gw - w_first)) * (kTileRows * kRowsMax);
+        p[r * kRowsMax + n0] = acc[0];
+        p[r * kRowsMax + n1] = acc[1];
+        p[(r + 8) * kRowsMax + n0] = acc[2];
+        p[(r + 8) * kRowsMax + n1] = acc[3];
+        __syncwarp();
+        int old = 0;
+        if (lane == 0) {
+          __threadfence();
+          old = atomicAdd(a.counters + tile, 1);
+        }
+        old = __shfl_sync(0xffffffffu, old, 0);
+        if (old == nc - 1) {
+          __threadfence();
+          const float* base = a.partial + (int64_t)tile * a.maxc * (kTileRows * kRowsMax);
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const int idx = lane * 4 + q, row = idx / kRowsMax, n = idx % kRowsMax;
+            float sum = 0.f;
+            for (int i = 0; i < nc; ++i) sum += __ldcg(base + i * (kTileRows * kRowsMax) + idx);
+            if (n < R && row0 + row < a.N) a.y[(int64_t)n * a.N + row0 + row] = __float2half_rn(sum);
+          }
+          if (lane == 0) a.counters[tile] = 0;
+        }
+      }
+      acc[0] = acc[1] = acc[2] = acc[3] = 0.f;
+    }
+    if (++blk == nblk) { blk = 0; ++tile; }
+  }
+  if (!ok && lane == 0 && a.err) atomicExch(a.err, 1);
+}
+
 // ---- general CUDA-core path: one warp per (row, m) --------------------------
 template <typename T>
 __global__ void qlinear_general_kernel(const T* __restrict__ x, int64_t M, int64_t K,
@@ -1082,7 +1284,7 @@ int launch_q4(LinArgs& a, void* workspace, size_t ws_bytes, cudaStream_t st) {
     for (auto k : {q4_gemv_kernel<0>, q4_gemv_kernel<1>, q4_gemv_kernel<2>})
       if (e == cudaSuccess) e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024);
     for (auto k : {q4_gemv_tma_kernel<0>, q4_gemv_tma_kernel<1>, q4_gemv_tma_kernel<2>})
-      if (e == cudaSuccess) e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, kTmaSmemCap);
+      if (e == cudaSuccess) e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, kRowsSmemCap);
     if (e != cudaSuccess) return fail(MOTIF_ERR_CUDA, "quantized_linear: smem attribute: %s", cudaGetErrorString(e));
     configured = true;
   }
@@ -1118,6 +1320,74 @@ int launch_q4(LinArgs& a, void* workspace, size_t ws_bytes, cudaStream_t st) {
   return check_launch("quantized_linear");
 }
 
+// Workspace of the multi-row GEMV for (n, k, rows), 0 when its shape does not fit it.
+size_t rows_ws_bytes(int64_t n, int64_t k, int rows) {
+  if (rows < 2 || rows > kRowsMax || k % 512 != 0) return 0;
+  const int warps = rows_warps(k, rows);
+  if (warps < 4) return 0;
+  const Plan p = make_plan(n, k, num_sms(), warps);
+  return kCounterBytes + sizeof(float) * (size_t)p.ntiles * p.maxc * kTileRows * kRowsMax;
+}
+
+// Workspace for m rows taken in balanced chunks of up to kRowsMax (sizes q and q + 1), 0 if a
+// chunk size does not fit the kernel.
+size_t rows_ws_need(int64_t n, int64_t k, int64_t m) {
+  const int64_t chunks = ceil_div(m, kRowsMax);
+  const int q = (int)(m / chunks);
+  const size_t a = rows_ws_bytes(n, k, q);
+  const size_t b = m % chunks ? rows_ws_bytes(n, k, q + 1) : a;
+  return a && b ? (a > b ? a : b) : 0;
+}
+
+// y (rows, n) = x (rows, k) · dequant(W)ᵀ with the weights streamed once; returns -1 (nothing
+// launched) when the shape or the workspace does not fit the kernel.
+int launch_q4_rows(LinArgs& a, int rows, void* workspace, size_t ws_bytes, cudaStream_t st) {
+  const size_t need = rows_ws_bytes(a.N, a.K, rows);
+  if (!need || !workspace || ws_bytes < need || !try_tma(a)) return -1;
+  const int warps = rows_warps(a.K, rows);
+  const Plan p = make_plan(a.N, a.K, num_sms(), warps);
+  if ((uint64_t)p.units * (uint64_t)p.total_warps >= (1ull << 32) || p.ntiles > kTileCounterCap) return -1;
+  a.nblk = p.nblk;
+  a.ntiles = p.ntiles;
+  a.units = p.units;
+  a.total_warps = p.total_warps;
+  a.maxc = p.maxc;
+  a.counters = static_cast<int*>(workspace);
+  a.partial = reinterpret_cast<float*>(static_cast<char*>(workspace) + kCounterBytes);
+  a.err = a.counters + kErrSlot;
+  static bool configured = false;
+  if (!configured) {
+    cudaError_t e = cudaSuccess;
+    for (auto k : {q4_gemv_rows_kernel<2>, q4_gemv_rows_kernel<3>, q4_gemv_rows_kernel<4>, q4_gemv_rows_kernel<5>,
+                   q4_gemv_rows_kernel<6>, q4_gemv_rows_kernel<7>, q4_gemv_rows_kernel<8>})
+      if (e == cudaSuccess) e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, kRowsSmemCap);
+    if (e != cudaSuccess) return fail(MOTIF_ERR_CUDA, "quantized_linear rows: smem attribute: %s", cudaGetErrorString(e));
+    configured = true;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(p.ctas);
+  cfg.blockDim = dim3(warps * 32);
+  cfg.dynamicSmemBytes = rows_smem_bytes(a.K, rows, warps);
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e;
+  switch (rows) {
+    case 2: e = cudaLaunchKernelEx(&cfg, q4_gemv_rows_kernel<2>, a); break;
+    case 3: e = cudaLaunchKernelEx(&cfg, q4_gemv_rows_kernel<3>, a); break;
+    case 4: e = cudaLaunchKernelEx(&cfg, q4_gemv_rows_kernel<4>, a); break;
+    case 5: e = cudaLaunchKernelEx(&cfg, q4_gemv_rows_kernel<5>, a); break;
+    case 6: e = cudaLaunchKernelEx(&cfg, q4_gemv_rows_kernel<6>, a); break;
+    case 7: e = cudaLaunchKernelEx(&cfg, q4_gemv_rows_kernel<7>, a); break;
+    default: e = cudaLaunchKernelEx(&cfg, q4_gemv_rows_kernel<8>, a); break;
+  }
+  if (e != cudaSuccess) return fail(MOTIF_ERR_CUDA, "quantized_linear rows launch: %s", cudaGetErrorString(e));
+  return check_launch("quantized_linear rows");
+}
+
 bool al16(const void* p) { return p == nullptr || (reinterpret_cast<uintptr_t>(p) % 16) == 0; }
 
 }  // namespace
@@ -1141,9 +1411,10 @@ extern "C" {
 
 size_t motif_quantized_linear_workspace_bytes(int64_t m, int64_t n, int64_t k, int bits,
                                               int group_size) {
-  (void)m;
   if (bits != 4 || group_size != 64 || k % 128 != 0 || n <= 0) return 0;
-  return ws_bytes_for(n, k);
+  const size_t one = ws_bytes_for(n, k);
+  const size_t rows = m >= 2 ? rows_ws_need(n, k, m) : 0;
+  return rows > one ? rows : one;
 }
 
 int motif_quantized_linear(int dtype, int bits, int group_size, const void* x, int64_t m,
@@ -1162,6 +1433,30 @@ int motif_quantized_linear(int dtype, int bits, int group_size, const void* x, i
   if (q4_gemm_supported(dtype, bits, group_size, m, n, k, x, w, scales, biases, y))
     return q4_gemm(x, m, k, w, scales, biases, n, y, nullptr, nullptr, st);
   if (fast_path_ok(dtype, bits, group_size, k, x, w, scales, biases)) {
+    // several rows: balanced chunks of up to kRowsMax rows, each streaming the weights once
+    const size_t rows_need = m >= 2 ? rows_ws_need(n, k, m) : 0;
+    if (rows_need && workspace && workspace_bytes >= rows_need) {
+      const int64_t chunks = ceil_div(m, kRowsMax);
+      int64_t row = 0;
+      for (int64_t i = 0; i < chunks; ++i) {
+        const int rows = (int)(m / chunks + (i < m % chunks ? 1 : 0));
+        LinArgs a{};
+        a.w = w;
+        a.sc = static_cast<const __half*>(scales);
+        a.bi = static_cast<const __half*>(biases);
+        a.N = n;
+        a.K = k;
+        a.y = static_cast<__half*>(y) + row * n;
+        a.mode = kModeX;
+        a.x = static_cast<const __half*>(x) + row * k;
+        const int rc = launch_q4_rows(a, rows, workspace, workspace_bytes, st);
+        if (rc < 0 && row == 0) break;  // the weights' tensor maps could not be encoded: one row at a time
+        if (rc < 0) return fail(MOTIF_ERR_CUDA, "quantized_linear rows: chunk %lld not launched", (long long)i);
+        if (rc) return rc;
+        row += rows;
+      }
+      if (row == m) return MOTIF_OK;
+    }
     for (int64_t i = 0; i < m; ++i) {
       LinArgs a{};
       a.w = w;

@@ -397,6 +397,11 @@ class MotifDecoder:
         lin_ws = max(lib.motif_linear_fused_workspace_bytes(ql.out_dim, ql.in_dim)
                      for L in self.layers for ql in (L["qkv"], L["o"], L["gate_up"], L["down"]))
         lin_ws = max(lin_ws, lib.motif_linear_fused_workspace_bytes(self.V_local, H))
+        # short row blocks (speculative verify, prompt tails): chunks of 2..8 rows share one weight pass
+        lin_ws = max([lin_ws] + [lib.motif_quantized_linear_workspace_bytes(m, ql.out_dim, ql.in_dim, 4, 64)
+                                 for m in range(2, 9)
+                                 for ql in [self.lm_head] + [L[n] for L in self.layers
+                                                             for n in ("qkv", "o", "gate_up", "down")]])
         if self.inter % 16:
             raise ValueError("intermediate size per rank must be a multiple of 16")
         self.lin_ws = torch.zeros(max(lin_ws, 16), dtype=torch.uint8, device=dev)
@@ -739,14 +744,18 @@ class MotifDecoder:
         self._launch_step(with_head)
         self._bump_host()
 
-    # Row blocks of at least this many prompt rows go through the tensor-core prefill.
+    # Row blocks of at least this many prompt rows run the tensor-core GEMMs; shorter blocks of at
+    # least min_rows_block rows run the multi-row GEMV (one weight pass per 8 rows). A prompt tail
+    # shorter than that takes the decode step, one graph launch per token.
     min_block_rows = 128
+    min_rows_block = 4
 
     def prefill(self, ids, chunk: int | None = None, batched: bool | None = None) -> None:
         """Ingest a prompt. All rows but the last run as blocks of up to ``chunk`` rows
-        (default 2048, mlx-lm's prefill step) through the tensor-core prompt path (q4 GEMMs,
-        causal prompt attention); the last token, and a remainder shorter than
-        ``min_block_rows``, take the decode step, which also yields the first greedy token.
+        (default 2048, mlx-lm's prefill step) through the prompt path (q4 GEMMs on the tensor
+        cores, or the multi-row GEMV below ``min_block_rows`` rows, and causal prompt attention);
+        the last token, and a remainder shorter than ``min_rows_block``, take the decode step,
+        which also yields the first greedy token.
         ``batched=False`` (or MOTIF_BATCHED_PREFILL=0, or tensor parallelism) runs every row
         through the decode step."""
         ids_d = torch.as_tensor(ids, dtype=torch.int32).reshape(-1).to(self.device)
@@ -757,7 +766,7 @@ class MotifDecoder:
         chunk = chunk or 2048
         i = 0
         if batched:
-            while n - 1 - i >= self.min_block_rows:
+            while n - 1 - i >= self.min_rows_block:
                 S = min(chunk, n - 1 - i)
                 self._prefill_block(ids_d[i : i + S])
                 i += S
@@ -825,8 +834,8 @@ class MotifDecoder:
         RoPE + cache append, causal attention over the cache + combine, o_proj (+ residual), post
         norm, gate|up, PolyNorm·up, down (+ residual) — ``MotifDecoderLayer`` (model.py:845-855)
         over the block. Blocks of at least 128 rows run the tcgen05 GEMMs with the residual
-        fused; shorter blocks (the speculative verify) run the q4 GEMV per row and fold the
-        residual into the next norm. With ``logits_out`` (S, V) the final norm and lm_head run
+        fused; shorter blocks (the speculative verify, prompt tails) run the multi-row q4 GEMV,
+        which streams the weights once per 8 rows, and fold the residual into the next norm. With ``logits_out`` (S, V) the final norm and lm_head run
         for every row (model.py:858-905); otherwise only the K/V rows stay (in the cache)."""
         S = ids_d.numel()
         off = self.offset
@@ -907,12 +916,12 @@ class MotifDecoder:
         return logits_out
 
     def ingest(self, ids) -> None:
-        """Append tokens to the cache without producing a next token (blocks of ``min_block_rows``
-        or more on the tensor cores, the rest through the decode step without its head)."""
+        """Append tokens to the cache without producing a next token (blocks of ``min_rows_block``
+        or more through the prompt path, the rest through the decode step without its head)."""
         ids_d = torch.as_tensor(ids, dtype=torch.int32).reshape(-1).to(self.device)
         n, i = ids_d.numel(), 0
         if self.tp_group is None and self._block_ok():
-            while n - i >= self.min_block_rows:
+            while n - i >= self.min_rows_block:
                 S = min(2048, n - i)
                 self._prefill_block(ids_d[i : i + S])
                 i += S

@@ -58,6 +58,28 @@ def test_quantized_linear_multi_row_uses_fast_path(cuda):
     assert_close(down(got), ref, "float16", what="5-row linear")
 
 
+@pytest.mark.parametrize("M", [2, 3, 5, 8, 9, 17])
+@pytest.mark.parametrize("N,K", [(2048, 2048), (16384, 2048), (2048, 8192), (1000, 4096), (100, 512)])
+def test_quantized_linear_row_chunks_match_oracle(cuda, M, N, K):
+    """2..127 rows run the multi-row GEMV (chunks of up to 8 rows, one weight pass per chunk);
+    the same workspace serves two calls in a row (split-tile counters return to zero)."""
+    from mlx_motif.linear import quantized_matmul
+    from mlx_motif.quantization import quantize
+
+    rng = np.random.default_rng(M * 131 + N + K)
+    w = rounded(rng.standard_normal((N, K)) * 0.02, "float16")
+    x = rounded(rng.standard_normal((M, K)), "float16")
+    d, s, b = quantize(up(w), 64, 4)
+    ref = O.quantized_matmul(x, d.cpu().numpy().view(np.uint32), down(s), down(b), 64, 4)
+    from mlx_motif._native import lib
+
+    ws = torch.zeros(max(lib.motif_quantized_linear_workspace_bytes(M, N, K, 4, 64), 16), dtype=torch.uint8,
+                     device="cuda")
+    for call in range(2):
+        got = quantized_matmul(up(x), d, s, b, workspace=ws)
+        assert_close(down(got), ref, "float16", what=f"{M}-row linear {N}x{K} call {call}")
+
+
 # ---------------------------------------------------------------- rope / norms / argmax
 @pytest.mark.parametrize("offset", [0, 5, 16000])
 def test_rope_matches_oracle(cuda, offset):

@@ -225,18 +225,29 @@ def _vanilla_model(n_rep, seed=0):
 @pytest.mark.parametrize("kind", ["grouped-fp16", "grouped-q4", "grouped-q8", "vanilla-4", "vanilla-1"])
 def test_batched_prefill_matches_stepwise(cuda, kind):
     """A prompt ingested in tensor-core row blocks (chunks of 128, so several blocks with a
-    nonzero cache offset, the chunked-prefill case) leaves the same cache and greedy
-    continuation as feeding it through the decode step one token at a time: K/V rows within
-    fp16 tolerance, identical greedy tokens, close final logits."""
+    nonzero cache offset, the chunked-prefill case; the 43-row tail runs the multi-row GEMV)
+    leaves the same cache and greedy continuation as feeding it through the decode step one
+    token at a time: K/V rows within fp16 tolerance, identical greedy tokens, close final logits."""
+    _compare_prefill(kind, 300, 128)
+
+
+@pytest.mark.parametrize("kind", ["grouped-fp16", "grouped-q4", "vanilla-4"])
+def test_short_prompt_row_block_matches_stepwise(cuda, kind):
+    """A 37-token prompt: one 36-row block on the multi-row GEMV (chunks of 7 and 8 rows), then
+    the decode step for the last token, against the all-decode-step ingestion."""
+    _compare_prefill(kind, 37, None)
+
+
+def _compare_prefill(kind, n, chunk):
     def make():
         if kind.startswith("grouped"):
             return _grouped_model(kind.split("-")[1], seed=3)
         return _vanilla_model(int(kind.split("-")[1]), seed=3)
 
-    prompt = np.random.default_rng(1).integers(0, 1024, 300).tolist()
+    prompt = np.random.default_rng(1).integers(0, 1024, n).tolist()
     a, b = make(), make()
     assert a._block_ok()
-    a.prefill(prompt, chunk=128, batched=True)
+    a.prefill(prompt, chunk=chunk, batched=True)
     b.prefill(prompt, batched=False)
     assert a.offset == b.offset == len(prompt)
     assert int(a.token.item()) == int(b.token.item())
@@ -245,18 +256,18 @@ def test_batched_prefill_matches_stepwise(cuda, kind):
     lt = {"q4": 0.15, "q8": 0.05}.get(kind.split("-")[1], 2e-2)
     assert_close(down(a.logits), down(b.logits), "float16", atol=lt, rtol=2e-2, what="first-token logits")
     ca, cb = a.caches[-1], b.caches[-1]
-    for n in ("k1", "k2", "v1", "v2"):
-        x, y = getattr(ca, n), getattr(cb, n)
+    for slot in ("k1", "k2", "v1", "v2"):
+        x, y = getattr(ca, slot), getattr(cb, slot)
         if isinstance(x, tuple):  # quantized: the rows agree but for boundary flips of single codes
             from mlx_motif.quantization import dequantize
 
-            dx = dequantize(*(t[..., :300, :].contiguous() for t in x), group_size=64, bits=ca.bits).float()
-            dy = dequantize(*(t[..., :300, :].contiguous() for t in y), group_size=64, bits=cb.bits).float()
+            dx = dequantize(*(t[..., :n, :].contiguous() for t in x), group_size=64, bits=ca.bits).float()
+            dy = dequantize(*(t[..., :n, :].contiguous() for t in y), group_size=64, bits=cb.bits).float()
             rel = ((dx - dy).abs().mean() / dy.abs().mean()).item()
-            assert rel <= 0.05, f"last-layer {n}: mean |difference| is {rel:.3f} of mean |value|"
+            assert rel <= 0.05, f"last-layer {slot}: mean |difference| is {rel:.3f} of mean |value|"
         else:
-            assert_close(down(x[..., :300, :]), down(y[..., :300, :]), "float16", atol=2e-2, rtol=2e-2,
-                         what=f"last-layer {n} rows")
+            assert_close(down(x[..., :n, :]), down(y[..., :n, :]), "float16", atol=2e-2, rtol=2e-2,
+                         what=f"last-layer {slot} rows")
     ta = [int(a.token.item())]
     tb = [int(b.token.item())]
     for _ in range(6):
