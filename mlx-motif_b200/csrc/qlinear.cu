@@ -906,8 +906,10 @@ __global__ void __launch_bounds__(kTmaThreads, kTmaMinBlocks) q4_gemv_tma_kernel
 // per quad of MMAs, so each MMA's 16 k values all belong to that group and C[row][x row] is
 // the group's exact dot; the MLX affine epilogue s·(C − corr) + b·Σx then runs per group and
 // per x row. Every weight byte is streamed once for all the rows. x rows are staged like the
-// one-row kernel's x (dequant order 0,4,1,5,.., odd k pre-scaled by 1/16, per-group Σx and
-// corr = 1024·Σ stored), one row every 2K + 16 bytes so the eight rows spread over the banks.
+// one-row kernel's x (dequant order 0,4,1,5,.., odd k pre-scaled by 1/16), one row every 2K + 16
+// bytes so the eight rows spread over the banks; per group, the float4 {corr, Σx} of x rows 2c
+// and 2c+1 (corr = 1024·Σ of the staged values, the dequant offset) sits where lane c reads it
+// with one load, and the MMA accumulator starts at −corr so only s·C + b·Σx remains per group.
 constexpr int kRowsMax = 8;
 constexpr int kRowsSmemCap = 225 * 1024;  // one CTA per SM
 
@@ -916,7 +918,7 @@ __host__ __device__ inline size_t rows_xs_offset(int warps) {
   return (size_t)warps * kStages * kSlotBytes + (((size_t)warps * kStages * 8 + 127) & ~(size_t)127);
 }
 
-size_t rows_xbytes(int64_t K, int R) { return (size_t)R * ((size_t)K * 2 + 16) + 2 * (size_t)R * (K / 64) * 4; }
+size_t rows_xbytes(int64_t K, int R) { return (size_t)R * ((size_t)K * 2 + 16) + (size_t)(K / 64) * 64; }
 
 size_t rows_smem_bytes(int64_t K, int R, int warps) { return rows_xs_offset(warps) + rows_xbytes(K, R); }
 
@@ -925,6 +927,11 @@ int rows_warps(int64_t K, int R) {
   int w = 16;
   while (w > 0 && rows_smem_bytes(K, R, w) > (size_t)kRowsSmemCap) --w;
   return w;
+}
+
+// fp16 half `hi` (0 = low 16 bits) of a packed pair, as float.
+__device__ __forceinline__ float half_of(uint32_t w, int hi) {
+  return __half2float(__ushort_as_half((unsigned short)(hi ? w >> 16 : w & 0xFFFFu)));
 }
 
 template <int R>
@@ -937,8 +944,7 @@ __global__ void __launch_bounds__(512, 1) q4_gemv_rows_kernel(const __grid_const
   const int64_t K = a.K;
   const int G = (int)(K / 64);
   const int64_t xstride = K * 2 + 16;
-  float* corr_s = reinterpret_cast<float*>(xs + R * xstride);
-  float* xsum_s = corr_s + R * G;
+  float4* cx_s = reinterpret_cast<float4*>(xs + R * xstride);  // [G][4]: {corr, Σx} of x rows 2c, 2c+1
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int r = lane >> 2, c = lane & 3;
@@ -970,33 +976,40 @@ __global__ void __launch_bounds__(512, 1) q4_gemv_rows_kernel(const __grid_const
   }
   grid_dep_wait();
   grid_dep_launch();
-  // ---- stage the x rows, one (row, group) per thread step ----
+  // ---- stage the x rows: one (group, row pair) per thread step ----
   const __half sixteenth = __float2half_rn(0.0625f);
-  for (int i = threadIdx.x; i < R * G; i += blockDim.x) {
-    const int row = i / G, g = i - row * G;
-    const __half* src = a.x + (int64_t)row * K + (int64_t)g * 64;
-    unsigned char* dst = xs + row * xstride + (int64_t)g * 128;
-    float lo = 0.f, hi = 0.f;
+  for (int i = threadIdx.x; i < 4 * G; i += blockDim.x) {
+    const int g = i >> 2, pair = i & 3;
+    float cx[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-    for (int w = 0; w < 8; ++w) {
-      const uint4 v = *reinterpret_cast<const uint4*>(src + w * 8);
-      const __half* e = reinterpret_cast<const __half*>(&v);
-      __half h[8];
+    for (int h2 = 0; h2 < 2; ++h2) {
+      const int row = 2 * pair + h2;
+      if (row >= R) break;
+      const __half* src = a.x + (int64_t)row * K + (int64_t)g * 64;
+      unsigned char* dst = xs + row * xstride + (int64_t)g * 128;
+      float lo = 0.f, hi = 0.f;
 #pragma unroll
-      for (int j = 0; j < 8; ++j) h[j] = (j & 1) ? __hmul(e[j], sixteenth) : e[j];
+      for (int w = 0; w < 8; ++w) {
+        const uint4 v = *reinterpret_cast<const uint4*>(src + w * 8);
+        const __half* e = reinterpret_cast<const __half*>(&v);
+        __half h[8];
 #pragma unroll
-      for (int j = 0; j < 8; j += 2) {
-        lo += __half2float(h[j]);
-        hi += __half2float(h[j + 1]);
+        for (int j = 0; j < 8; ++j) h[j] = (j & 1) ? __hmul(e[j], sixteenth) : e[j];
+#pragma unroll
+        for (int j = 0; j < 8; j += 2) {
+          lo += __half2float(h[j]);
+          hi += __half2float(h[j + 1]);
+        }
+        uint4 o;
+        __half* oe = reinterpret_cast<__half*>(&o);
+        oe[0] = h[0]; oe[1] = h[4]; oe[2] = h[1]; oe[3] = h[5];
+        oe[4] = h[2]; oe[5] = h[6]; oe[6] = h[3]; oe[7] = h[7];
+        *reinterpret_cast<uint4*>(dst + w * 16) = o;
       }
-      uint4 o;
-      __half* oe = reinterpret_cast<__half*>(&o);
-      oe[0] = h[0]; oe[1] = h[4]; oe[2] = h[1]; oe[3] = h[5];
-      oe[4] = h[2]; oe[5] = h[6]; oe[6] = h[3]; oe[7] = h[7];
-      *reinterpret_cast<uint4*>(dst + w * 16) = o;
+      cx[2 * h2] = 1024.f * (lo + hi);
+      cx[2 * h2 + 1] = lo + 16.f * hi;
     }
-    xsum_s[row * G + g] = lo + 16.f * hi;
-    corr_s[row * G + g] = 1024.f * (lo + hi);
+    cx_s[i] = make_float4(cx[0], cx[1], cx[2], cx[3]);
   }
   __syncthreads();
 
@@ -1016,39 +1029,44 @@ __global__ void __launch_bounds__(512, 1) q4_gemv_rows_kernel(const __grid_const
       break;
     }
     const unsigned char* slot = my_ring + slot_i * kSlotBytes;
+#pragma unroll 1
+    for (int half = 0; half < 2; ++half) {  // groups 4·half .. 4·half+3 (one 128B-swizzled box)
+      // fp16 scales / biases of rows r and r+8 for these four groups
+      const unsigned char* sp = slot + 4096 + r * 16 + half * 8;
+      const uint2 sr = lds64(sp), sr8 = lds64(sp + 128), br = lds64(sp + 256), br8 = lds64(sp + 384);
 #pragma unroll
-    for (int gi = 0; gi < 8; ++gi) {
-      const int chunk = 2 * (gi & 3) + (c >> 1);
-      const uint32_t off = (gi >> 2) * 2048 + r * 128 + ((chunk ^ r) << 4) + (c & 1) * 8;
-      const uint2 wr = lds64(slot + off), wr8 = lds64(slot + off + 1024);
-      uint32_t P0[4], P1[4], Q0[4], Q1[4];
-      dequant_word_offset(wr.x, P0);
-      dequant_word_offset(wr.y, P1);
-      dequant_word_offset(wr8.x, Q0);
-      dequant_word_offset(wr8.y, Q1);
-      const int gg = blk * 8 + gi;
-      uint4 b0 = make_uint4(0, 0, 0, 0), b1 = make_uint4(0, 0, 0, 0);
-      if (r < R) {
-        const unsigned char* xp = xs + r * xstride + (int64_t)gg * 128 + c * 32;
-        b0 = lds128(xp);
-        b1 = lds128(xp + 16);
+      for (int q = 0; q < 4; ++q) {
+        const int gi = 4 * half + q;
+        const int chunk = 2 * q + (c >> 1);
+        const uint32_t off = (gi >> 2) * 2048 + r * 128 + ((chunk ^ r) << 4) + (c & 1) * 8;
+        const uint2 wr = lds64(slot + off), wr8 = lds64(slot + off + 1024);
+        uint32_t P0[4], P1[4], Q0[4], Q1[4];
+        dequant_word_offset(wr.x, P0);
+        dequant_word_offset(wr.y, P1);
+        dequant_word_offset(wr8.x, Q0);
+        dequant_word_offset(wr8.y, Q1);
+        const int gg = blk * 8 + gi;
+        uint4 b0 = make_uint4(0, 0, 0, 0), b1 = make_uint4(0, 0, 0, 0);
+        if (r < R) {
+          const unsigned char* xp = xs + r * xstride + (int64_t)gg * 128 + c * 32;
+          b0 = lds128(xp);
+          b1 = lds128(xp + 16);
+        }
+        const float4 cx = cx_s[gg * 4 + c];  // {corr, Σx} of x rows n0, n1 (zeros past R)
+        float C[4] = {-cx.x, -cx.z, -cx.x, -cx.z};
+        mma16816(C, P0[0], Q0[0], P0[1], Q0[1], b0.x, b0.y);
+        mma16816(C, P0[2], Q0[2], P0[3], Q0[3], b0.z, b0.w);
+        mma16816(C, P1[0], Q1[0], P1[1], Q1[1], b1.x, b1.y);
+        mma16816(C, P1[2], Q1[2], P1[3], Q1[3], b1.z, b1.w);
+        const uint32_t ws = (q & 2) ? sr.y : sr.x, ws8 = (q & 2) ? sr8.y : sr8.x;
+        const uint32_t wb = (q & 2) ? br.y : br.x, wb8 = (q & 2) ? br8.y : br8.x;
+        const float s_r = half_of(ws, q & 1), s_r8 = half_of(ws8, q & 1);
+        const float b_r = half_of(wb, q & 1), b_r8 = half_of(wb8, q & 1);
+        acc[0] = fmaf(s_r, C[0], fmaf(b_r, cx.y, acc[0]));
+        acc[1] = fmaf(s_r, C[1], fmaf(b_r, cx.w, acc[1]));
+        acc[2] = fmaf(s_r8, C[2], fmaf(b_r8, cx.y, acc[2]));
+        acc[3] = fmaf(s_r8, C[3], fmaf(b_r8, cx.w, acc[3]));
       }
-      float C[4] = {0.f, 0.f, 0.f, 0.f};
-      mma16816(C, P0[0], Q0[0], P0[1], Q0[1], b0.x, b0.y);
-      mma16816(C, P0[2], Q0[2], P0[3], Q0[3], b0.z, b0.w);
-      mma16816(C, P1[0], Q1[0], P1[1], Q1[1], b1.x, b1.y);
-      mma16816(C, P1[2], Q1[2], P1[3], Q1[3], b1.z, b1.w);
-      const unsigned char* sp = slot + 4096 + r * 16 + gi * 2;
-      const float s_r = __half2float(*reinterpret_cast<const __half*>(sp));
-      const float s_r8 = __half2float(*reinterpret_cast<const __half*>(sp + 128));
-      const float b_r = __half2float(*reinterpret_cast<const __half*>(sp + 256));
-      const float b_r8 = __half2float(*reinterpret_cast<const __half*>(sp + 384));
-      const float cr0 = n0 < R ? corr_s[n0 * G + gg] : 0.f, xs0 = n0 < R ? xsum_s[n0 * G + gg] : 0.f;
-      const float cr1 = n1 < R ? corr_s[n1 * G + gg] : 0.f, xs1 = n1 < R ? xsum_s[n1 * G + gg] : 0.f;
-      acc[0] += s_r * (C[0] - cr0) + b_r * xs0;
-      acc[1] += s_r * (C[1] - cr1) + b_r * xs1;
-      acc[2] += s_r8 * (C[2] - cr0) + b_r8 * xs0;
-      acc[3] += s_r8 * (C[3] - cr1) + b_r8 * xs1;
     }
     __syncwarp();
     if (lane == 0 && u + kStages < u1) {
@@ -1329,14 +1347,26 @@ size_t rows_ws_bytes(int64_t n, int64_t k, int rows) {
   return kCounterBytes + sizeof(float) * (size_t)p.ntiles * p.maxc * kTileRows * kRowsMax;
 }
 
-// Workspace for m rows taken in balanced chunks of up to kRowsMax (sizes q and q + 1), 0 if a
-// chunk size does not fit the kernel.
+// Most x rows one launch stages for in-dimension k (at least 4 warps of ring beside them), 0 if
+// not even two fit.
+int rows_cap(int64_t k) {
+  if (k % 512) return 0;
+  for (int r = kRowsMax; r >= 2; --r)
+    if (rows_warps(k, r) >= 4) return r;
+  return 0;
+}
+
+// Workspace for m rows taken in balanced chunks of up to rows_cap(k) rows (sizes q and q + 1; a
+// one-row chunk runs the one-row kernel), 0 if the multi-row kernel does not fit.
 size_t rows_ws_need(int64_t n, int64_t k, int64_t m) {
-  const int64_t chunks = ceil_div(m, kRowsMax);
+  const int cap = rows_cap(k);
+  if (!cap || m < 2) return 0;
+  const int64_t chunks = ceil_div(m, cap);
   const int q = (int)(m / chunks);
-  const size_t a = rows_ws_bytes(n, k, q);
-  const size_t b = m % chunks ? rows_ws_bytes(n, k, q + 1) : a;
-  return a && b ? (a > b ? a : b) : 0;
+  auto need = [&](int rows) { return rows == 1 ? ws_bytes_for(n, k) : rows_ws_bytes(n, k, rows); };
+  const size_t a = need(q);
+  const size_t b = m % chunks ? need(q + 1) : a;
+  return a > b ? a : b;
 }
 
 // y (rows, n) = x (rows, k) · dequant(W)ᵀ with the weights streamed once; returns -1 (nothing
@@ -1413,7 +1443,7 @@ size_t motif_quantized_linear_workspace_bytes(int64_t m, int64_t n, int64_t k, i
                                               int group_size) {
   if (bits != 4 || group_size != 64 || k % 128 != 0 || n <= 0) return 0;
   const size_t one = ws_bytes_for(n, k);
-  const size_t rows = m >= 2 ? rows_ws_need(n, k, m) : 0;
+  const size_t rows = rows_ws_need(n, k, m);
   return rows > one ? rows : one;
 }
 
@@ -1434,9 +1464,9 @@ int motif_quantized_linear(int dtype, int bits, int group_size, const void* x, i
     return q4_gemm(x, m, k, w, scales, biases, n, y, nullptr, nullptr, st);
   if (fast_path_ok(dtype, bits, group_size, k, x, w, scales, biases)) {
     // several rows: balanced chunks of up to kRowsMax rows, each streaming the weights once
-    const size_t rows_need = m >= 2 ? rows_ws_need(n, k, m) : 0;
+    const size_t rows_need = rows_ws_need(n, k, m);
     if (rows_need && workspace && workspace_bytes >= rows_need) {
-      const int64_t chunks = ceil_div(m, kRowsMax);
+      const int64_t chunks = ceil_div(m, rows_cap(k));
       int64_t row = 0;
       for (int64_t i = 0; i < chunks; ++i) {
         const int rows = (int)(m / chunks + (i < m % chunks ? 1 : 0));
@@ -1449,7 +1479,8 @@ int motif_quantized_linear(int dtype, int bits, int group_size, const void* x, i
         a.y = static_cast<__half*>(y) + row * n;
         a.mode = kModeX;
         a.x = static_cast<const __half*>(x) + row * k;
-        const int rc = launch_q4_rows(a, rows, workspace, workspace_bytes, st);
+        const int rc = rows == 1 ? launch_q4(a, workspace, workspace_bytes, st)
+                                 : launch_q4_rows(a, rows, workspace, workspace_bytes, st);
         if (rc < 0 && row == 0) break;  // the weights' tensor maps could not be encoded: one row at a time
         if (rc < 0) return fail(MOTIF_ERR_CUDA, "quantized_linear rows: chunk %lld not launched", (long long)i);
         if (rc) return rc;
