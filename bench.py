@@ -72,10 +72,13 @@ def parse_args():
     ap.add_argument("--layers", type=int, default=48, help="(debug) model depth; 48 is the benchmark")
     ap.add_argument("--prompt", type=int, default=164, help="prompt length (164 = config[1])")
     ap.add_argument("--vocab", type=int, default=219520, help="(profiling) vocabulary size; 219520 is the benchmark")
-    ap.add_argument("--kernel-case", choices=["gemm", "prefill_attn", "long_q4", "long_fp16"], default=None,
-                    help="(profiling) run one small single-kernel case --steps times and exit: the prompt GEMM "
-                         "(3204 x 16384 x 2048), a 2048-row vanilla prompt-attention block, or the long-cache "
-                         "decode step at 16000 rows (q4 / fp16 cache)")
+    ap.add_argument("--kernel-case", choices=["gemm", "prefill_attn", "long_q4", "long_fp16", "rows_gemv", "verify"],
+                    default=None,
+                    help="(profiling) run one small case --steps times and exit: the prompt GEMM "
+                         "(3204 x 16384 x 2048), a 2048-row vanilla prompt-attention block, the long-cache "
+                         "decode step at 16000 rows (q4 / fp16 cache), the 5-row GEMV on the 12.7B-class "
+                         "gate|up shape, or the speculative verify (a 5-row forward of the 12.7B-class model "
+                         "at an 800-row cache; the last one inside cudaProfilerStart/Stop)")
     ap.add_argument("--profile", action="store_true",
                     help="profiler window only: cudaProfilerStart/Stop around the timed steps, then exit "
                          "(for `ncu --profile-from-start off`)")
@@ -682,6 +685,7 @@ def run_kernel_case(a) -> None:
     """Small single-kernel workloads for ncu captures (one GPU; nothing is timed here)."""
     import os
 
+    import numpy as np
     import torch
 
     from mlx_motif import _native as N
@@ -701,6 +705,37 @@ def run_kernel_case(a) -> None:
         for _ in range(reps):
             N.check(N.lib.motif_q4_gemm(x.data_ptr(), M, k, d.data_ptr(), s.data_ptr(), b.data_ptr(), n, y.data_ptr(),
                                         None, None, N.stream()), "q4_gemm")
+    elif a.kernel_case == "rows_gemv":
+        M, n, k = 5, 28672, 4096
+        d, s, b = quantize((torch.randn((n, k), generator=g, device=dev) * 0.02).half(), 64, 4)
+        x = torch.randn((M, k), generator=g, device=dev).half()
+        y = torch.empty((M, n), dtype=torch.float16, device=dev)
+        wb = N.lib.motif_quantized_linear_workspace_bytes(M, n, k, 4, 64)
+        ws = torch.zeros(max(wb, 16), dtype=torch.uint8, device=dev)
+        for _ in range(reps):
+            N.check(N.lib.motif_quantized_linear(0, 4, 64, x.data_ptr(), M, k, d.data_ptr(), s.data_ptr(),
+                                                 b.data_ptr(), n, y.data_ptr(), ws.data_ptr(), wb, N.stream()),
+                    "quantized_linear")
+    elif a.kernel_case == "verify":
+        from mlx_motif.model import ModelArgs, MotifDecoder
+
+        m = MotifDecoder.random(ModelArgs(num_hidden_layers=a.layers, vocab_size=a.vocab), seed=0, cache="fp16",
+                                max_seq=1024, device=dev)
+        ids = np.random.default_rng(4).integers(0, a.vocab, 800).tolist()
+        m.ingest(ids)
+        rows = torch.as_tensor(ids[:5], dtype=torch.int32, device=dev)
+        logits = torch.empty((5, m.V_local), dtype=torch.float16, device=dev)
+        base = m.offset
+        for i in range(reps):
+            last = i == reps - 1
+            if last:
+                torch.cuda.synchronize()
+                torch.cuda.profiler.start()
+            m.forward_rows(rows, logits)
+            if last:
+                torch.cuda.synchronize()
+                torch.cuda.profiler.stop()
+            m.rewind(base)
     elif a.kernel_case == "prefill_attn":
         S, Hk, n_rep = 2048, 2, 4
         qh = 2 * Hk * n_rep

@@ -305,6 +305,21 @@ MOTIF_API int motif_prefill_attention(const void* q, int64_t seq, int64_t q_head
                                       int64_t offset, int mode, int64_t gr, float scale, void* out, int* err,
                                       void* stream);
 
+/* motif_prefill_attention for a short block over a long cache (the [1, K+1]
+ * speculative verify, prompt tails): with seq <= 128 and a workspace of at least
+ * motif_prefill_attention_split_workspace_bytes(seq, q_heads) bytes, the cache
+ * rows are divided among up to 16 CTAs per query head (at least two 64-row
+ * tiles each, at most one CTA per SM in total) whose fp32 softmax states a
+ * second kernel merges; otherwise it is motif_prefill_attention. Results agree
+ * with it within fp32 rounding before the fp16 output. No reference
+ * counterpart beyond motif_prefill_attention's (the same SDPAs, model.py:486-559,
+ * 769-807). */
+MOTIF_API size_t motif_prefill_attention_split_workspace_bytes(int64_t seq, int64_t q_heads);
+MOTIF_API int motif_prefill_attention_split(const void* q, int64_t seq, int64_t q_heads,
+                                            const motif_kv4_slots* cache, int64_t offset, int mode, int64_t gr,
+                                            float scale, void* out, void* workspace, size_t workspace_bytes,
+                                            int* err, void* stream);
+
 /* The differential combine over prompt rows: o (seq, q_heads, 256) from
  * motif_prefill_attention -> y (seq, out_heads, 256), the o_proj input.
  * mode 0: gda_post_split (kernels/gda.py:223-282) of each group's gr origin

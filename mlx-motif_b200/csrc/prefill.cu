@@ -51,7 +51,13 @@ struct PrefillArgs {
   int mode, gr, q_origin;
   float scale_log2;
   int* err;
+  float* part;  // split-KV partials (gridDim.z > 1): [QH][splits][S][kPartStride] fp32
 };
+
+// A split's partial state of one (head, row): unnormalised O (256), its reference maximum
+// (log2 domain) and Σp, padded to a 16-byte multiple.
+constexpr int kPartStride = 260;
+constexpr int kMaxSplits = 16;
 
 // shared-memory map (bytes from a 1024-byte aligned base)
 constexpr int kOffQ = 0;            // 2 × 16 KB
@@ -103,7 +109,12 @@ __global__ void __launch_bounds__(kPAThreads, 1) prefill_attn_kernel(const __gri
     g = (h >> 1) / a.gr;
   }
   const int kv_end = a.off + q0 + rows;  // keys [0, kv_end) are visible to some row of the tile
-  const int nt = (kv_end + kKT - 1) / kKT;
+  const int nt_all = (kv_end + kKT - 1) / kKT;
+  // Split-KV (short blocks): this CTA takes key tiles [j0, j0 + nt); the host keeps every
+  // split non-empty. Below, j counts this CTA's tiles (ring stages, barrier parities).
+  const int nsplit = gridDim.z, split = blockIdx.z;
+  const int j0 = (int)((int64_t)split * nt_all / nsplit);
+  const int nt = (int)((int64_t)(split + 1) * nt_all / nsplit) - j0;
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < kNumBars; ++i) tc::mbar_init(bar + 8u * i, (i == 11 || i == 12) ? 4 : 1);
@@ -133,16 +144,17 @@ __global__ void __launch_bounds__(kPAThreads, 1) prefill_attn_kernel(const __gri
         if (*abort_flag) break;
         const uint32_t kb = sb + kOffK + s * 16384;
         tc::mbar_expect_tx(k_full(s), 16384);
-        tc::tma_load_2d(kb, &a.tm_k[kslot], 0, krow + j * kKT, k_full(s));
-        tc::tma_load_2d(kb + 8192, &a.tm_k[kslot], 128, krow + j * kKT, k_full(s));
+        const int kpos = krow + (j0 + j) * kKT;
+        tc::tma_load_2d(kb, &a.tm_k[kslot], 0, kpos, k_full(s));
+        tc::tma_load_2d(kb + 8192, &a.tm_k[kslot], 128, kpos, k_full(s));
         k_iss = j + 1;
         if (j >= 2 && !tc::mbar_wait(v_empty(s), (r - 1) & 1)) { *abort_flag = 1; break; }
         const uint32_t vb = sb + kOffV + s * 32768;
         tc::mbar_expect_tx(v_full(s), 32768);
-        tc::tma_load_2d(vb, &a.tm_v[0], 0, krow + j * kKT, v_full(s));
-        tc::tma_load_2d(vb + 8192, &a.tm_v[0], 128, krow + j * kKT, v_full(s));
-        tc::tma_load_2d(vb + 16384, &a.tm_v[1], 0, krow + j * kKT, v_full(s));
-        tc::tma_load_2d(vb + 24576, &a.tm_v[1], 128, krow + j * kKT, v_full(s));
+        tc::tma_load_2d(vb, &a.tm_v[0], 0, kpos, v_full(s));
+        tc::tma_load_2d(vb + 8192, &a.tm_v[0], 128, kpos, v_full(s));
+        tc::tma_load_2d(vb + 16384, &a.tm_v[1], 0, kpos, v_full(s));
+        tc::tma_load_2d(vb + 24576, &a.tm_v[1], 128, kpos, v_full(s));
         v_iss = j + 1;
       }
       // drain: the loads issued last on each stage have landed before the CTA may exit
@@ -216,7 +228,7 @@ __global__ void __launch_bounds__(kPAThreads, 1) prefill_attn_kernel(const __gri
       tc::tmem_ld32(trow + kColS + 64 * s, sv[0]);
       tc::tmem_ld32(trow + kColS + 64 * s + 32, sv[1]);
       tc::tmem_ld_wait();
-      const int p0 = j * kKT;
+      const int p0 = (j0 + j) * kKT;
       float x[64];
       float m_tile = -INFINITY;
 #pragma unroll
@@ -231,11 +243,13 @@ __global__ void __launch_bounds__(kPAThreads, 1) prefill_attn_kernel(const __gri
         m_ref = m_tile;
       }
       l *= factor;
+      // a row with no visible key yet (a later split's first tiles) keeps m_ref = -inf and p = 0
+      const float mb = m_ref == -INFINITY ? 0.f : m_ref;
       uint32_t pk[32];
       float psum = 0.f;
 #pragma unroll
       for (int c = 0; c < 64; c += 2) {
-        const __half2 hp = __floats2half2_rn(exp2f(x[c] - m_ref), exp2f(x[c + 1] - m_ref));
+        const __half2 hp = __floats2half2_rn(exp2f(x[c] - mb), exp2f(x[c + 1] - mb));
         const float2 fp = __half22float2(hp);
         psum += fp.x + fp.y;
         pk[c >> 1] = *reinterpret_cast<const uint32_t*>(&hp);
@@ -280,12 +294,24 @@ __global__ void __launch_bounds__(kPAThreads, 1) prefill_attn_kernel(const __gri
     const bool live = fin && r < rows;
     const float inv_l = l > 0.f ? 1.f / l : 0.f;
     __half* dst = a.out + ((int64_t)(q0 + r) * a.QH + h) * 256;
+    float* pdst = a.part + (((int64_t)h * nsplit + split) * a.S + q0 + r) * kPartStride;
+    if (nsplit > 1 && live) {
+      pdst[256] = m_ref;
+      pdst[257] = l;
+    }
 #pragma unroll 1
     for (int cb = 0; cb < 8; ++cb) {
       uint32_t ov[32];
       tc::tmem_ld32(trow + kColO + cb * 32, ov);
       tc::tmem_ld_wait();
-      if (live) {
+      if (nsplit > 1) {  // unnormalised O of this split, merged by prefill_merge_kernel
+        if (live)
+#pragma unroll
+          for (int v = 0; v < 8; ++v)
+            *reinterpret_cast<float4*>(pdst + cb * 32 + v * 4) =
+                make_float4(__uint_as_float(ov[4 * v]), __uint_as_float(ov[4 * v + 1]),
+                            __uint_as_float(ov[4 * v + 2]), __uint_as_float(ov[4 * v + 3]));
+      } else if (live) {
 #pragma unroll
         for (int v = 0; v < 4; ++v) {
           uint4 o;
@@ -306,6 +332,26 @@ __global__ void __launch_bounds__(kPAThreads, 1) prefill_attn_kernel(const __gri
     tc::tmem_dealloc(tmem, 512);
   }
   if (threadIdx.x == 0 && *abort_flag && a.err) atomicExch(a.err, 1);
+}
+
+// Merge of the split-KV partials: per (row, head) the splits' states are rescaled to their
+// common maximum, O = Σ w·O_s / Σ w·l_s, rounded to fp16 like the one-CTA path's output.
+__global__ void __launch_bounds__(256) prefill_merge_kernel(const float* __restrict__ part, int nsplit, int S, int QH,
+                                                            __half* __restrict__ out) {
+  const int row = blockIdx.x, h = blockIdx.y, c = threadIdx.x;
+  const int64_t sstride = (int64_t)S * kPartStride;
+  const float* base = part + ((int64_t)h * nsplit * S + row) * kPartStride;
+  float M = -INFINITY;
+  for (int i = 0; i < nsplit; ++i) M = fmaxf(M, base[i * sstride + 256]);
+  float L = 0.f, o = 0.f;
+  for (int i = 0; i < nsplit; ++i) {
+    const float* p = base + i * sstride;
+    const float m = p[256];
+    const float w = m == -INFINITY ? 0.f : exp2f(m - M);
+    L += w * p[257];
+    o += w * p[c];
+  }
+  out[((int64_t)row * QH + h) * 256 + c] = __float2half_rn(L > 0.f ? o * (1.f / L) : 0.f);
 }
 
 // ---- the differential combine over rows -----------------------------------------------------
@@ -396,10 +442,21 @@ int launch_post(int gr, dim3 grid, cudaStream_t st, const __half* o, int QH, int
 
 using namespace motif;
 
-extern "C" {
+namespace {
+int device_sms() {
+  static int n = 0;
+  if (!n) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
+        n <= 0)
+      n = 148;
+  }
+  return n;
+}
 
-int motif_prefill_attention(const void* q, int64_t seq, int64_t q_heads, const motif_kv4_slots* cache,
-                            int64_t offset, int mode, int64_t gr, float scale, void* out, int* err, void* stream) {
+int prefill_attention(const void* q, int64_t seq, int64_t q_heads, const motif_kv4_slots* cache, int64_t offset,
+                      int mode, int64_t gr, float scale, void* out, void* workspace, size_t workspace_bytes, int* err,
+                      void* stream) {
   MOTIF_REQUIRE(q && cache && out, MOTIF_ERR_NULL, "prefill_attention: null pointer");
   const motif_kv4_slots& c = *cache;
   for (int i = 0; i < 4; ++i) MOTIF_REQUIRE(c.data[i], MOTIF_ERR_NULL, "prefill_attention: slot %d null", i);
@@ -444,9 +501,49 @@ int motif_prefill_attention(const void* q, int64_t seq, int64_t q_heads, const m
     if (e != cudaSuccess) return fail(MOTIF_ERR_CUDA, "prefill_attention: smem attribute: %s", cudaGetErrorString(e));
     configured = true;
   }
-  const dim3 grid((unsigned)ceil_div(seq, kQT), (unsigned)q_heads);
-  prefill_attn_kernel<<<grid, kPAThreads, kPASmem, as_stream(stream)>>>(a);
+  // Split-KV for a single query tile over a long cache: up to one CTA per SM in total, at
+  // least two key tiles per split.
+  int nsplit = 1;
+  const size_t ws_need = motif_prefill_attention_split_workspace_bytes(seq, q_heads);
+  if (ws_need && workspace && workspace_bytes >= ws_need) {
+    const int64_t nt_all = ceil_div(offset + seq, kKT);
+    int64_t n = device_sms() / q_heads;
+    if (n > nt_all / 2) n = nt_all / 2;
+    if (n > kMaxSplits) n = kMaxSplits;
+    if (n >= 2) nsplit = (int)n;
+  }
+  a.part = nsplit > 1 ? static_cast<float*>(workspace) : nullptr;
+  cudaStream_t st = as_stream(stream);
+  const dim3 grid((unsigned)ceil_div(seq, kQT), (unsigned)q_heads, (unsigned)nsplit);
+  prefill_attn_kernel<<<grid, kPAThreads, kPASmem, st>>>(a);
+  if (nsplit > 1) {
+    const int rc = check_launch("prefill_attention");
+    if (rc) return rc;
+    prefill_merge_kernel<<<dim3((unsigned)seq, (unsigned)q_heads), 256, 0, st>>>(a.part, nsplit, (int)seq, (int)q_heads,
+                                                                                 a.out);
+    return check_launch("prefill_attention merge");
+  }
   return check_launch("prefill_attention");
+}
+}  // namespace
+
+extern "C" {
+
+size_t motif_prefill_attention_split_workspace_bytes(int64_t seq, int64_t q_heads) {
+  if (seq < 1 || seq > kQT || q_heads < 1 || q_heads > 65535) return 0;
+  return sizeof(float) * kPartStride * (size_t)kMaxSplits * (size_t)q_heads * (size_t)seq;
+}
+
+int motif_prefill_attention(const void* q, int64_t seq, int64_t q_heads, const motif_kv4_slots* cache,
+                            int64_t offset, int mode, int64_t gr, float scale, void* out, int* err, void* stream) {
+  return prefill_attention(q, seq, q_heads, cache, offset, mode, gr, scale, out, nullptr, 0, err, stream);
+}
+
+int motif_prefill_attention_split(const void* q, int64_t seq, int64_t q_heads, const motif_kv4_slots* cache,
+                                  int64_t offset, int mode, int64_t gr, float scale, void* out, void* workspace,
+                                  size_t workspace_bytes, int* err, void* stream) {
+  return prefill_attention(q, seq, q_heads, cache, offset, mode, gr, scale, out, workspace, workspace_bytes, err,
+                           stream);
 }
 
 int motif_prefill_post(const void* o, int64_t seq, int64_t q_heads, int mode, int64_t groups, int64_t gr,

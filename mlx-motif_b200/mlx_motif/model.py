@@ -852,6 +852,12 @@ class MotifDecoder:
         gu, act, err = b["gu"][:S], b["act"][:S], b["err"]
         mode = 1 if self.vanilla else 0
         big = S >= self.min_block_rows and self._block_ok()
+        split_ws = None
+        wsb = lib.motif_prefill_attention_split_workspace_bytes(S, self.q_heads)
+        if wsb:
+            split_ws = getattr(self, "_split_ws", None)
+            if split_ws is None or split_ws.numel() < wsb:
+                split_ws = self._split_ws = torch.empty(wsb, dtype=torch.uint8, device=self.device)
 
         def lin(xin, ql, out, residual=None):
             if big:
@@ -881,8 +887,13 @@ class MotifDecoder:
             check(lib.motif_rope_qkv_append_rows(ptr(qkv), S, ptr(self.inv_freq), self.q_heads, self._slots[li],
                                                  off, None, ptr(q), st), "rope rows")
             slots = self._attn_slots(li, off + S)
-            check(lib.motif_prefill_attention(ptr(q), S, self.q_heads, slots, off, mode, self.gr, self.scale,
-                                              ptr(o), ptr(err), st), "prefill_attention")
+            if split_ws is not None:  # a short block over a longer cache: split-KV
+                check(lib.motif_prefill_attention_split(ptr(q), S, self.q_heads, slots, off, mode, self.gr,
+                                                        self.scale, ptr(o), ptr(split_ws), split_ws.numel(),
+                                                        ptr(err), st), "prefill_attention")
+            else:
+                check(lib.motif_prefill_attention(ptr(q), S, self.q_heads, slots, off, mode, self.gr, self.scale,
+                                                  ptr(o), ptr(err), st), "prefill_attention")
             check(lib.motif_prefill_post(ptr(o), S, self.q_heads, mode, self.q_groups, self.gr, ptr(L["subln"]),
                                          ptr(L["lambda_full"]), L["lambda_full"].numel(), L["lambda_init"],
                                          a.attn_rms_norm_eps, ptr(attn), st), "prefill_post")

@@ -170,6 +170,46 @@ def test_prefill_attention_grouped_matches_oracle(cuda, S, off):
                  what="gda post rows")
 
 
+@pytest.mark.parametrize("G,S,off", [(8, 5, 800), (8, 1, 300), (8, 17, 2000), (8, 128, 1000), (8, 3, 190),
+                                     (2, 5, 830), (8, 64, 255)])
+def test_prefill_attention_split_matches_oracle(cuda, G, S, off):
+    """motif_prefill_attention_split (key tiles divided among CTAs per head, fp32 partial
+    states merged by a second kernel) == the oracle's per-slab causal SDPAs, and == the
+    one-CTA-per-head launch within fp16 rounding; rows whose first visible key lies in a
+    later split (the block's own causal tail) included."""
+    from mlx_motif import _native as N_
+
+    gr, d = 3, 128
+    qh = G * (gr + 1)
+    rng = np.random.default_rng(7 * S + off + G)
+    cache, (k1, k2, v1, v2) = _filled_cache(rng, G, off + S, 4096, cuda)
+    tq = up(rounded(rng.standard_normal((qh, S, d)), "float16"))
+    q = down(tq)
+    ws_bytes = N_.lib.motif_prefill_attention_split_workspace_bytes(S, qh)
+    assert ws_bytes > 0
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=cuda)
+    err = torch.zeros(1, dtype=torch.int32, device=cuda)
+    outs = []
+    for split in (True, False):
+        o = torch.full((S, qh, 2 * d), float("nan"), dtype=torch.float16, device=cuda)
+        if split:
+            N_.check(N_.lib.motif_prefill_attention_split(tq.data_ptr(), S, qh, cache.slots_struct(), off, 0, gr,
+                                                          d ** -0.5, o.data_ptr(), ws.data_ptr(), ws_bytes,
+                                                          err.data_ptr(), N_.stream()), "prefill_attention_split")
+        else:
+            N_.check(N_.lib.motif_prefill_attention(tq.data_ptr(), S, qh, cache.slots_struct(), off, 0, gr,
+                                                    d ** -0.5, o.data_ptr(), err.data_ptr(), N_.stream()),
+                     "prefill_attention")
+        outs.append(o)
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    ao, an = O.grouped_prompt_attention_reference(q[None, : G * gr], q[None, G * gr:], k1, k2, v1, v2, d ** -0.5, off)
+    got = down(outs[0]).transpose(1, 0, 2)[None]
+    assert_close(got[:, : G * gr], ao.astype(np.float64), "float16", what="split: origin heads")
+    assert_close(got[:, G * gr:], an.astype(np.float64), "float16", what="split: noise heads")
+    assert_close(down(outs[0]), down(outs[1]).astype(np.float64), "float16", what="split vs one CTA per head")
+
+
 @pytest.mark.parametrize("n_rep,S,off", [(4, 200, 0), (4, 129, 300), (2, 64, 0), (1, 257, 5)])
 def test_prefill_attention_vanilla_matches_oracle(cuda, n_rep, S, off):
     """mode 1 + the vanilla combine == _forward_vanilla's prompt attention (model.py:486-559):
