@@ -602,8 +602,8 @@ def run_b200(a) -> None:
                 **rows_ms,
                 "note": "draft and target are independent random-init models, so few draft tokens match "
                         "the target's distribution; the verify forward streams the target's weights once for "
-                        "its K+1 rows (multi-row GEMV); verify_forward_ms includes the host's launch gaps "
-                        "(the row block is not graph-captured) and its error-word read",
+                        "its K+1 rows (multi-row GEMV); the verify replays a CUDA graph (positions read from "
+                        "the device offset), verify_forward_ms also covers the host's rewind between calls",
             }
             del spec, draft, target
             torch.cuda.empty_cache()

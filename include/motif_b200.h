@@ -309,16 +309,21 @@ MOTIF_API int motif_prefill_attention(const void* q, int64_t seq, int64_t q_head
  * speculative verify, prompt tails): with seq <= 128 and a workspace of at least
  * motif_prefill_attention_split_workspace_bytes(seq, q_heads) bytes, the cache
  * rows are divided among up to 16 CTAs per query head (at least two 64-row
- * tiles each, at most one CTA per SM in total) whose fp32 softmax states a
- * second kernel merges; otherwise it is motif_prefill_attention. Results agree
- * with it within fp32 rounding before the fp16 output. No reference
+ * tiles each at `offset`, at most one CTA per SM in total) whose fp32 softmax
+ * states a second kernel merges; otherwise it is motif_prefill_attention.
+ * Results agree with it within fp32 rounding before the fp16 output.
+ * offset_dev (optional device int32): the position of query 0 is read there at
+ * run time (a CUDA graph replayed at every offset); `offset` is then the
+ * largest value it may hold, used for the launch shape, and splits left
+ * without key tiles at a smaller offset contribute nothing. A device offset
+ * outside [0, capacity - seq] sets *err and reads nothing. No reference
  * counterpart beyond motif_prefill_attention's (the same SDPAs, model.py:486-559,
  * 769-807). */
 MOTIF_API size_t motif_prefill_attention_split_workspace_bytes(int64_t seq, int64_t q_heads);
 MOTIF_API int motif_prefill_attention_split(const void* q, int64_t seq, int64_t q_heads,
-                                            const motif_kv4_slots* cache, int64_t offset, int mode, int64_t gr,
-                                            float scale, void* out, void* workspace, size_t workspace_bytes,
-                                            int* err, void* stream);
+                                            const motif_kv4_slots* cache, int64_t offset, const int32_t* offset_dev,
+                                            int mode, int64_t gr, float scale, void* out, void* workspace,
+                                            size_t workspace_bytes, int* err, void* stream);
 
 /* The differential combine over prompt rows: o (seq, q_heads, 256) from
  * motif_prefill_attention -> y (seq, out_heads, 256), the o_proj input.

@@ -52,6 +52,7 @@ struct PrefillArgs {
   float scale_log2;
   int* err;
   float* part;  // split-KV partials (gridDim.z > 1): [QH][splits][S][kPartStride] fp32
+  const int32_t* off_dev;  // when set, the position of query 0 is read here (graph replays)
 };
 
 // A split's partial state of one (head, row): unnormalised O (256), its reference maximum
@@ -108,13 +109,26 @@ __global__ void __launch_bounds__(kPAThreads, 1) prefill_attn_kernel(const __gri
     kslot = h & 1;
     g = (h >> 1) / a.gr;
   }
-  const int kv_end = a.off + q0 + rows;  // keys [0, kv_end) are visible to some row of the tile
+  const int off = a.off_dev ? *a.off_dev : a.off;
+  if (off < 0 || off + a.S > a.cap) {  // a device offset outside the cache: nothing is read
+    if (threadIdx.x == 0 && a.err) atomicExch(a.err, 1);
+    return;
+  }
+  const int kv_end = off + q0 + rows;  // keys [0, kv_end) are visible to some row of the tile
   const int nt_all = (kv_end + kKT - 1) / kKT;
-  // Split-KV (short blocks): this CTA takes key tiles [j0, j0 + nt); the host keeps every
-  // split non-empty. Below, j counts this CTA's tiles (ring stages, barrier parities).
+  // Split-KV (short blocks): this CTA takes key tiles [j0, j0 + nt). Below, j counts this
+  // CTA's tiles (ring stages, barrier parities).
   const int nsplit = gridDim.z, split = blockIdx.z;
   const int j0 = (int)((int64_t)split * nt_all / nsplit);
   const int nt = (int)((int64_t)(split + 1) * nt_all / nsplit) - j0;
+  if (nt <= 0) {  // more splits than key tiles (a device offset below the launch's bound): empty state
+    for (int r = threadIdx.x; r < rows; r += blockDim.x) {
+      float* pdst = a.part + (((int64_t)h * nsplit + split) * a.S + q0 + r) * kPartStride;
+      pdst[256] = -INFINITY;
+      pdst[257] = 0.f;
+    }
+    return;
+  }
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < kNumBars; ++i) tc::mbar_init(bar + 8u * i, (i == 11 || i == 12) ? 4 : 1);
@@ -211,7 +225,7 @@ __global__ void __launch_bounds__(kPAThreads, 1) prefill_attn_kernel(const __gri
   } else {  // ---- softmax + epilogue: one thread per query row ----
     const int q = warp & 3;
     const int r = q * 32 + lane;
-    const int qa = a.off + q0 + r;  // absolute position of this row's query
+    const int qa = off + q0 + r;  // absolute position of this row's query
     const uint32_t trow = tmem + ((uint32_t)(q * 32) << 16);
     float m_ref = -INFINITY, l = 0.f;
     bool alive = true;
@@ -347,7 +361,8 @@ __global__ void __launch_bounds__(256) prefill_merge_kernel(const float* __restr
   for (int i = 0; i < nsplit; ++i) {
     const float* p = base + i * sstride;
     const float m = p[256];
-    const float w = m == -INFINITY ? 0.f : exp2f(m - M);
+    if (m == -INFINITY) continue;  // a split that saw no key of this row (its O is not written)
+    const float w = exp2f(m - M);
     L += w * p[257];
     o += w * p[c];
   }
@@ -455,8 +470,8 @@ int device_sms() {
 }
 
 int prefill_attention(const void* q, int64_t seq, int64_t q_heads, const motif_kv4_slots* cache, int64_t offset,
-                      int mode, int64_t gr, float scale, void* out, void* workspace, size_t workspace_bytes, int* err,
-                      void* stream) {
+                      const int32_t* offset_dev, int mode, int64_t gr, float scale, void* out, void* workspace,
+                      size_t workspace_bytes, int* err, void* stream) {
   MOTIF_REQUIRE(q && cache && out, MOTIF_ERR_NULL, "prefill_attention: null pointer");
   const motif_kv4_slots& c = *cache;
   for (int i = 0; i < 4; ++i) MOTIF_REQUIRE(c.data[i], MOTIF_ERR_NULL, "prefill_attention: slot %d null", i);
@@ -489,6 +504,7 @@ int prefill_attention(const void* q, int64_t seq, int64_t q_heads, const motif_k
   a.QH = (int)q_heads;
   a.cap = (int)c.capacity;
   a.off = (int)offset;
+  a.off_dev = offset_dev;
   a.mode = mode;
   a.gr = (int)gr;
   a.q_origin = mode == 0 ? (int)(G * gr) : 0;
@@ -536,14 +552,14 @@ size_t motif_prefill_attention_split_workspace_bytes(int64_t seq, int64_t q_head
 
 int motif_prefill_attention(const void* q, int64_t seq, int64_t q_heads, const motif_kv4_slots* cache,
                             int64_t offset, int mode, int64_t gr, float scale, void* out, int* err, void* stream) {
-  return prefill_attention(q, seq, q_heads, cache, offset, mode, gr, scale, out, nullptr, 0, err, stream);
+  return prefill_attention(q, seq, q_heads, cache, offset, nullptr, mode, gr, scale, out, nullptr, 0, err, stream);
 }
 
 int motif_prefill_attention_split(const void* q, int64_t seq, int64_t q_heads, const motif_kv4_slots* cache,
-                                  int64_t offset, int mode, int64_t gr, float scale, void* out, void* workspace,
-                                  size_t workspace_bytes, int* err, void* stream) {
-  return prefill_attention(q, seq, q_heads, cache, offset, mode, gr, scale, out, workspace, workspace_bytes, err,
-                           stream);
+                                  int64_t offset, const int32_t* offset_dev, int mode, int64_t gr, float scale,
+                                  void* out, void* workspace, size_t workspace_bytes, int* err, void* stream) {
+  return prefill_attention(q, seq, q_heads, cache, offset, offset_dev, mode, gr, scale, out, workspace,
+                           workspace_bytes, err, stream);
 }
 
 int motif_prefill_post(const void* o, int64_t seq, int64_t q_heads, int mode, int64_t groups, int64_t gr,

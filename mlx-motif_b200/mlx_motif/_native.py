@@ -110,7 +110,7 @@ SIGNATURES = {
     "motif_rope_qkv_append_rows": (_I, [_P, _L, _P, _L, _KV, _L, _P, _P, _P]),
     "motif_prefill_attention": (_I, [_P, _L, _L, _KV, _L, _I, _L, _F, _P, _P, _P]),
     "motif_prefill_attention_split_workspace_bytes": (_S, [_L, _L]),
-    "motif_prefill_attention_split": (_I, [_P, _L, _L, _KV, _L, _I, _L, _F, _P, _P, _S, _P, _P]),
+    "motif_prefill_attention_split": (_I, [_P, _L, _L, _KV, _L, _P, _I, _L, _F, _P, _P, _S, _P, _P]),
     "motif_prefill_post": (_I, [_P, _L, _L, _I, _L, _L, _P, _P, _L, _F, _F, _P, _P]),
     "motif_vanilla_decode_step": (
         _I,

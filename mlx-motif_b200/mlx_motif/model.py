@@ -420,6 +420,10 @@ class MotifDecoder:
         self.seed = 0
         self.stream_id = 0
         self._graphs: dict[bool, torch.cuda.CUDAGraph] = {}
+        # row-block forwards (the speculative verify) captured per (rows, logits buffer)
+        self._row_graphs: dict[tuple, torch.cuda.CUDAGraph] = {}
+        self._rows_seen: set = set()
+        self._rows_ids = torch.zeros(128, dtype=torch.int32, device=dev)
         self.pinned_in = torch.zeros(1, dtype=torch.int32).pin_memory()
         self.pinned_out = torch.zeros(1, dtype=torch.int32).pin_memory()
         # Tensor parallelism exchanges the row-parallel outputs and the PolyNorm statistics through
@@ -799,6 +803,7 @@ class MotifDecoder:
             err=torch.zeros(1, dtype=torch.int32, device=dev),
         )
         self._blk = b
+        self._row_graphs.clear()  # captured row blocks point at the old buffers
         return b
 
     def _attn_slots(self, li: int, rows: int):
@@ -838,9 +843,20 @@ class MotifDecoder:
         which streams the weights once per 8 rows, and fold the residual into the next norm. With ``logits_out`` (S, V) the final norm and lm_head run
         for every row (model.py:858-905); otherwise only the K/V rows stay (in the cache)."""
         S = ids_d.numel()
+        if self.offset + S + 1 > self.max_seq:
+            raise ValueError(f"KV capacity {self.max_seq} exhausted by a {S}-row block at {self.offset}")
+        b = self._launch_block(ids_d, logits_out, device_offset=False)
+        self._bump_host(S)
+        self.pos_len.copy_(torch.tensor([self.offset, self.offset + 1], dtype=torch.int32))
+        if int(b["err"].item()) != 0:
+            raise RuntimeError("prompt block: a tensor-core pipeline wait timed out")
+
+    def _launch_block(self, ids_d: torch.Tensor, logits_out: torch.Tensor | None, device_offset: bool) -> dict:
+        """The launches of ``_prefill_block``. With ``device_offset`` the rows' positions are read
+        from ``pos_len[0]`` at run time (a CUDA graph replayed at every offset; the split attention
+        is shaped for the largest offset the capacity allows) and ``pos_len`` advances on the device."""
+        S = ids_d.numel()
         off = self.offset
-        if off + S + 1 > self.max_seq:
-            raise ValueError(f"KV capacity {self.max_seq} exhausted by a {S}-row block at {off}")
         b = self._block_buffers(S)
         a = self.args
         st = stream(self.device)
@@ -858,6 +874,9 @@ class MotifDecoder:
             split_ws = getattr(self, "_split_ws", None)
             if split_ws is None or split_ws.numel() < wsb:
                 split_ws = self._split_ws = torch.empty(wsb, dtype=torch.uint8, device=self.device)
+                self._row_graphs.clear()
+        off_dev = ptr(self.pos_len) if device_offset else None
+        attn_off = self.max_seq - S - 1 if device_offset else off  # device offset: the launch's bound
 
         def lin(xin, ql, out, residual=None):
             if big:
@@ -885,11 +904,11 @@ class MotifDecoder:
                 norm_after(tmp, L["input_norm"])
             lin(x, L["qkv"], qkv)
             check(lib.motif_rope_qkv_append_rows(ptr(qkv), S, ptr(self.inv_freq), self.q_heads, self._slots[li],
-                                                 off, None, ptr(q), st), "rope rows")
+                                                 off, off_dev, ptr(q), st), "rope rows")
             slots = self._attn_slots(li, off + S)
             if split_ws is not None:  # a short block over a longer cache: split-KV
-                check(lib.motif_prefill_attention_split(ptr(q), S, self.q_heads, slots, off, mode, self.gr,
-                                                        self.scale, ptr(o), ptr(split_ws), split_ws.numel(),
+                check(lib.motif_prefill_attention_split(ptr(q), S, self.q_heads, slots, attn_off, off_dev, mode,
+                                                        self.gr, self.scale, ptr(o), ptr(split_ws), split_ws.numel(),
                                                         ptr(err), st), "prefill_attention")
             else:
                 check(lib.motif_prefill_attention(ptr(q), S, self.q_heads, slots, off, mode, self.gr, self.scale,
@@ -909,10 +928,9 @@ class MotifDecoder:
             check(lib.motif_quantized_linear(0, 4, 64, ptr(x), S, ql.in_dim, ptr(ql.weight), ptr(ql.scales),
                                              ptr(ql.biases), ql.out_dim, ptr(logits_out), ptr(self.lin_ws),
                                              self.lin_ws.numel(), st), "lm_head rows")
-        self._bump_host(S)
-        self.pos_len.copy_(torch.tensor([self.offset, self.offset + 1], dtype=torch.int32))
-        if int(err.item()) != 0:
-            raise RuntimeError("prompt block: a tensor-core pipeline wait timed out")
+        if device_offset:
+            self.pos_len.add_(S)
+        return b
 
     def forward_rows(self, ids, logits_out: torch.Tensor | None = None) -> torch.Tensor:
         """Feed a block of tokens at the current position and return their logits (S, V) fp16: the
@@ -923,8 +941,38 @@ class MotifDecoder:
         S = ids_d.numel()
         if logits_out is None:
             logits_out = torch.empty((S, self.V_local), dtype=torch.float16, device=self.device)
-        self._prefill_block(ids_d, logits_out)
+        key = (S, logits_out.data_ptr())
+        if not self._rows_graph_ok(S) or key not in self._rows_seen:
+            self._rows_seen.add(key)  # the first call runs eagerly (attributes, buffers), the next captures
+            self._prefill_block(ids_d, logits_out)
+            return logits_out
+        if self.offset + S + 1 > self.max_seq:
+            raise ValueError(f"KV capacity {self.max_seq} exhausted by a {S}-row block at {self.offset}")
+        g = self._row_graphs.get(key)
+        if g is None:
+            torch.cuda.synchronize(self.device)
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                self._launch_block(self._rows_ids[:S], logits_out, device_offset=True)
+            self._row_graphs[key] = g
+        self._rows_ids[:S].copy_(ids_d)
+        g.replay()
+        self._bump_host(S)
         return logits_out
+
+    def _rows_graph_ok(self, S: int) -> bool:
+        """A row block replays as a CUDA graph when its launches take no host-side offset: an fp16
+        cache (a quantized cache is dequantized up to the block's rows) and a short block (the
+        multi-row GEMV and split attention path). MOTIF_ROWS_GRAPH=0 keeps every call eager."""
+        return (self.cache_kind == "fp16" and 1 <= S < min(self.min_block_rows, 129)
+                and os.environ.get("MOTIF_ROWS_GRAPH", "1") != "0")
+
+    def check_rows_error(self) -> None:
+        """Raise if a graph-replayed row block's pipeline wait timed out (its error word is read
+        here, not after every replay)."""
+        b = getattr(self, "_blk", None)
+        if b is not None and int(b["err"].item()) != 0:
+            raise RuntimeError("row block: a tensor-core pipeline wait timed out")
 
     def ingest(self, ids) -> None:
         """Append tokens to the cache without producing a next token (blocks of ``min_rows_block``

@@ -10,7 +10,8 @@ rule accepts while the draft equals the target's argmax, so the output equals th
 greedy decode.
 
 Device work per cycle: K draft decode steps (CUDA graphs, sampling in the head), one target
-row-block forward with logits, one acceptance kernel; the host reads back two int32 per cycle.
+row-block forward with logits (a CUDA graph after its first call), one acceptance kernel; the host
+reads back two int32 and the row block's error word per cycle.
 """
 
 from __future__ import annotations
@@ -70,6 +71,7 @@ class SpeculativeDecoder:
                                                ptr(self.draft_tokens), k, t.V_local, self.temperature, self.seed,
                                                None, base, ptr(self.result), st), "speculative_accept")
             self.result_host.copy_(self.result)
+            t.check_rows_error()
             n_acc, nxt = int(self.result_host[0]), int(self.result_host[1])
             accepted = self.draft_tokens[:n_acc].tolist()
             # target: rows of last and x_1 .. x_n are valid

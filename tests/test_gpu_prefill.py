@@ -193,7 +193,7 @@ def test_prefill_attention_split_matches_oracle(cuda, G, S, off):
     for split in (True, False):
         o = torch.full((S, qh, 2 * d), float("nan"), dtype=torch.float16, device=cuda)
         if split:
-            N_.check(N_.lib.motif_prefill_attention_split(tq.data_ptr(), S, qh, cache.slots_struct(), off, 0, gr,
+            N_.check(N_.lib.motif_prefill_attention_split(tq.data_ptr(), S, qh, cache.slots_struct(), off, None, 0, gr,
                                                           d ** -0.5, o.data_ptr(), ws.data_ptr(), ws_bytes,
                                                           err.data_ptr(), N_.stream()), "prefill_attention_split")
         else:

@@ -113,6 +113,39 @@ def test_row_block_forward_matches_decode_steps(cuda):
     assert_close(down(rows), np.stack(ref), "float16", atol=1e-2, rtol=2e-2, what="verify rows vs decode steps")
 
 
+def test_row_block_graph_replays_match_eager(cuda):
+    """forward_rows replays a captured CUDA graph after its first (eager) call: the rows'
+    positions come from the device offset, so one graph serves every offset; logits match the
+    eager launches within tolerance (the split attention may be cut differently, so later layers
+    differ by rounding), the first layer's K/V rows are written identically at the device offset,
+    and the host and device offsets advance by the block."""
+    tgt, _ = _models(cuda)
+    rng = np.random.default_rng(8)
+    tgt.ingest(rng.integers(0, 1024, 300).tolist())
+    ids = [5, 900, 17, 3, 44]
+    ids_d = torch.tensor(ids, dtype=torch.int32, device=cuda)
+    out_g = torch.empty((5, tgt.V_local), dtype=torch.float16, device=cuda)
+    out_e = torch.empty_like(out_g)
+    tgt.forward_rows(ids, out_g)  # first call (at 300): eager
+    for base in (290, 250, 100, 37):  # rewind only moves back
+        tgt.rewind(base)
+        tgt.forward_rows(ids, out_g)  # graph
+        assert tgt.offset == base + 5 and tgt.pos_len.tolist() == [base + 5, base + 6]
+        slots = ("k1", "k2", "v1", "v2")
+        kv_g = [[getattr(c, n)[..., base:base + 5, :].clone() for n in slots] for c in (tgt.caches[0], tgt.caches[-1])]
+        tgt.rewind(base)
+        tgt._prefill_block(ids_d, out_e)
+        kv_e = [[getattr(c, n)[..., base:base + 5, :] for n in slots] for c in (tgt.caches[0], tgt.caches[-1])]
+        assert all(torch.equal(x, y) for x, y in zip(kv_g[0], kv_e[0])), f"first-layer rows differ at {base}"
+        for x, y in zip(kv_g[1], kv_e[1]):
+            assert_close(down(x), down(y).astype(np.float64), "float16", atol=2e-2, rtol=2e-2,
+                         what=f"last-layer rows at {base}")
+        assert_close(down(out_g), down(out_e).astype(np.float64), "float16", atol=1e-2, rtol=2e-2,
+                     what=f"graph vs eager at {base}")
+    tgt.check_rows_error()
+    assert len(tgt._row_graphs) == 1
+
+
 def test_speculative_greedy_equals_target_greedy(cuda):
     from mlx_motif.speculative import SpeculativeDecoder
 
