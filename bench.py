@@ -482,7 +482,7 @@ def run_b200(a) -> None:
                 pms = timed_prefill(m, long_prompt)
                 pre = {"ms": round(pms, 2), "tok_s": round(16000 / (pms / 1e3), 1),
                        "tflops": round(prefill_flops(m, 16000) / (pms / 1e3) / 1e12, 1)}
-            else:  # the prompt path is single-GPU: synthetic rows stand in for the prompt's KV
+            else:  # synthetic rows stand in for the prompt's KV (keeps the multi-GPU run short)
                 m.fill_cache_synthetic(16000, seed=1)
                 m.token.fill_(1)
             for _ in range(a.warmup):

@@ -88,6 +88,19 @@ MOTIF_API int motif_polynorm_mul(int dtype, const void* gate, const void* up, in
                        const void* weight, const void* bias, float eps, int64_t rows, int64_t dim,
                        void* y, void* stream);
 
+/* motif_polynorm_mul with the intermediate axis sharded over tensor-parallel
+ * ranks: motif_polynorm_row_stats writes this rank's (Σx², Σx⁴, Σx⁶) of each
+ * row's `dim` gate values to stats (rows × 3 fp32); once the caller has summed
+ * them over the ranks, motif_polynorm_mul_stats applies PolyNorm·up to this
+ * rank's slice with the means taken over full_dim values. No reference
+ * counterpart (the reference is single-device); the arithmetic is
+ * motif_polynorm_mul's (mlp.py:119-157, model.py:267-268). */
+MOTIF_API int motif_polynorm_row_stats(int dtype, const void* x, int64_t in_stride, int64_t rows, int64_t dim,
+                                       float* stats, void* stream);
+MOTIF_API int motif_polynorm_mul_stats(int dtype, const void* gate, const void* up, int64_t in_stride,
+                                       const void* weight, const void* bias, float eps, int64_t rows,
+                                       int64_t dim, const float* stats, int64_t full_dim, void* y, void* stream);
+
 /* ---- GDA post reduction -----------------------------------------------------
  * y = (o − λ·n[h/gr]) · rsqrt(mean(d²) + eps) · subln_w · (1 − λ_init).
  * Replaces gda_post_split (src/mlx_motif/kernels/gda.py:223-282).

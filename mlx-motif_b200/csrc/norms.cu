@@ -36,29 +36,48 @@ int vec_width(int64_t dim, std::initializer_list<const void*> ptrs, std::initial
 //             + w2·x·rsqrt(mean x²+eps) + b                (mlp.py:13-16)
 // With `up`, y = T(polynorm(x)) · up (MotifMLP, model.py:267-268).
 // ---------------------------------------------------------------------------
+//
+// Tensor-parallel split (the intermediate axis sharded over ranks): stats_out receives this
+// slice's (Σx², Σx⁴, Σx⁶) per row and nothing else is written; stats_in supplies the sums over
+// the whole row (full_dim values, summed across ranks) instead of this slice's.
 template <typename T, int V>
 __global__ void polynorm_kernel(const T* __restrict__ x, const T* __restrict__ up,
                                 int64_t in_stride, const T* __restrict__ w,
                                 const T* __restrict__ b, float eps, int dim,
-                                T* __restrict__ y) {
+                                T* __restrict__ y, float* __restrict__ stats_out = nullptr,
+                                const float* __restrict__ stats_in = nullptr, int full_dim = 0) {
   __shared__ float scratch[32 * 3];
   const int64_t row = blockIdx.x;
   const T* xr = x + row * in_stride;
   float acc[3] = {0.f, 0.f, 0.f};
-  for (int i = threadIdx.x * V; i < dim; i += blockDim.x * V) {
-    float v[V];
-    load_vec<T, V>(xr + i, v);
+  if (stats_in) {
+    acc[0] = stats_in[row * 3];
+    acc[1] = stats_in[row * 3 + 1];
+    acc[2] = stats_in[row * 3 + 2];
+  } else {
+    for (int i = threadIdx.x * V; i < dim; i += blockDim.x * V) {
+      float v[V];
+      load_vec<T, V>(xr + i, v);
 #pragma unroll
-    for (int j = 0; j < V; ++j) {
-      float v2 = v[j] * v[j];
-      float v4 = v2 * v2;
-      acc[0] += v2;
-      acc[1] += v4;
-      acc[2] += v4 * v2;
+      for (int j = 0; j < V; ++j) {
+        float v2 = v[j] * v[j];
+        float v4 = v2 * v2;
+        acc[0] += v2;
+        acc[1] += v4;
+        acc[2] += v4 * v2;
+      }
+    }
+    block_sum<3>(acc, scratch);
+    if (stats_out) {
+      if (threadIdx.x == 0) {
+        stats_out[row * 3] = acc[0];
+        stats_out[row * 3 + 1] = acc[1];
+        stats_out[row * 3 + 2] = acc[2];
+      }
+      return;
     }
   }
-  block_sum<3>(acc, scratch);
-  const float inv_d = 1.0f / (float)dim;
+  const float inv_d = 1.0f / (float)(stats_in ? full_dim : dim);
   const float rs2 = rsqrtf(acc[0] * inv_d + eps);
   const float rs4 = rsqrtf(acc[1] * inv_d + eps);
   const float rs6 = rsqrtf(acc[2] * inv_d + eps);
@@ -84,7 +103,8 @@ __global__ void polynorm_kernel(const T* __restrict__ x, const T* __restrict__ u
 template <typename T>
 int launch_polynorm(const void* x, const void* up, int64_t in_stride, const void* w,
                     const void* b, float eps, int64_t rows, int64_t dim, void* y,
-                    cudaStream_t st) {
+                    cudaStream_t st, float* stats_out = nullptr, const float* stats_in = nullptr,
+                    int64_t full_dim = 0) {
   const int V = vec_width<T>(dim, {x, up, y}, {in_stride});
   const int threads = pick_threads(ceil_div(dim, V));
   auto xp = static_cast<const T*>(x);
@@ -92,11 +112,11 @@ int launch_polynorm(const void* x, const void* up, int64_t in_stride, const void
   if (V == 1)
     polynorm_kernel<T, 1><<<rows, threads, 0, st>>>(xp, up_p, in_stride, static_cast<const T*>(w),
                                                     static_cast<const T*>(b), eps, (int)dim,
-                                                    static_cast<T*>(y));
+                                                    static_cast<T*>(y), stats_out, stats_in, (int)full_dim);
   else
     polynorm_kernel<T, 16 / sizeof(T)><<<rows, threads, 0, st>>>(
         xp, up_p, in_stride, static_cast<const T*>(w), static_cast<const T*>(b), eps, (int)dim,
-        static_cast<T*>(y));
+        static_cast<T*>(y), stats_out, stats_in, (int)full_dim);
   return check_launch("polynorm");
 }
 
@@ -304,6 +324,32 @@ int motif_polynorm_mul(int dtype, const void* gate, const void* up, int64_t in_s
                 (long long)in_stride);
   if (rows == 0) return MOTIF_OK;
   MOTIF_DISPATCH_FLOAT(dtype, T, return launch_polynorm<T>(gate, up, in_stride, weight, bias, eps, rows, dim, y, as_stream(stream)));
+  return MOTIF_OK;
+}
+
+int motif_polynorm_row_stats(int dtype, const void* x, int64_t in_stride, int64_t rows, int64_t dim, float* stats,
+                             void* stream) {
+  MOTIF_REQUIRE(x && stats, MOTIF_ERR_NULL, "polynorm_row_stats: null pointer");
+  MOTIF_REQUIRE(rows >= 0 && dim > 0 && dim < (1ll << 31) && in_stride >= dim, MOTIF_ERR_BAD_SHAPE,
+                "polynorm_row_stats: rows=%lld dim=%lld stride=%lld", (long long)rows, (long long)dim,
+                (long long)in_stride);
+  if (rows == 0) return MOTIF_OK;
+  MOTIF_DISPATCH_FLOAT(dtype, T, return launch_polynorm<T>(x, nullptr, in_stride, nullptr, nullptr, 0.f, rows, dim,
+                                                           nullptr, as_stream(stream), stats));
+  return MOTIF_OK;
+}
+
+int motif_polynorm_mul_stats(int dtype, const void* gate, const void* up, int64_t in_stride, const void* weight,
+                             const void* bias, float eps, int64_t rows, int64_t dim, const float* stats,
+                             int64_t full_dim, void* y, void* stream) {
+  MOTIF_REQUIRE(gate && up && weight && bias && stats && y, MOTIF_ERR_NULL, "polynorm_mul_stats: null pointer");
+  MOTIF_REQUIRE(rows >= 0 && dim > 0 && dim < (1ll << 31) && in_stride >= dim && full_dim >= dim &&
+                    full_dim < (1ll << 31),
+                MOTIF_ERR_BAD_SHAPE, "polynorm_mul_stats: rows=%lld dim=%lld stride=%lld full_dim=%lld",
+                (long long)rows, (long long)dim, (long long)in_stride, (long long)full_dim);
+  if (rows == 0) return MOTIF_OK;
+  MOTIF_DISPATCH_FLOAT(dtype, T, return launch_polynorm<T>(gate, up, in_stride, weight, bias, eps, rows, dim, y,
+                                                           as_stream(stream), nullptr, stats, full_dim));
   return MOTIF_OK;
 }
 

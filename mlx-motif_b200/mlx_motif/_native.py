@@ -109,6 +109,8 @@ SIGNATURES = {
     "motif_embed_rms_norm_rows": (_I, [_I, _P, _L, _P, _L, _L, _P, _F, _P, _P, _P]),
     "motif_rope_qkv_append_rows": (_I, [_P, _L, _P, _L, _KV, _L, _P, _P, _P]),
     "motif_prefill_attention": (_I, [_P, _L, _L, _KV, _L, _I, _L, _F, _P, _P, _P]),
+    "motif_polynorm_row_stats": (_I, [_I, _P, _L, _L, _L, _P, _P]),
+    "motif_polynorm_mul_stats": (_I, [_I, _P, _P, _L, _P, _P, _F, _L, _L, _P, _L, _P, _P]),
     "motif_prefill_attention_split_workspace_bytes": (_S, [_L, _L]),
     "motif_prefill_attention_split": (_I, [_P, _L, _L, _KV, _L, _P, _I, _L, _F, _P, _P, _S, _P, _P]),
     "motif_prefill_post": (_I, [_P, _L, _L, _I, _L, _L, _P, _P, _L, _F, _F, _P, _P]),

@@ -766,7 +766,7 @@ class MotifDecoder:
         n = ids_d.numel()
         if batched is None:
             batched = os.environ.get("MOTIF_BATCHED_PREFILL", "1") != "0"
-        batched = batched and self.tp_group is None and self._block_ok()
+        batched = batched and self._block_ok()
         chunk = chunk or 2048
         i = 0
         if batched:
@@ -779,7 +779,12 @@ class MotifDecoder:
             self.step_device(with_head=(j == n - 1))
 
     def _block_ok(self) -> bool:
-        """The prompt path's contracts: q4 GEMM shapes (k % 512, n % 128) and head_dim 128."""
+        """The prompt path's contract: head_dim 128 (the prompt attention and its combine)."""
+        return self.d == 128
+
+    def _gemm_ok(self) -> bool:
+        """The tensor-core GEMM's shapes (k % 512, n % 128) for every linear of a layer; blocks
+        of other shapes run the multi-row GEMV."""
         lins = [L[k] for L in self.layers for k in ("qkv", "o", "gate_up", "down")]
         return self.d == 128 and all(ql.in_dim % 512 == 0 and ql.out_dim % 128 == 0 for ql in lins)
 
@@ -802,6 +807,10 @@ class MotifDecoder:
             act=torch.empty((S, self.inter), dtype=f16, device=dev),
             err=torch.zeros(1, dtype=torch.int32, device=dev),
         )
+        if self.tp_group is not None:  # PolyNorm statistics and the lm_head shard's rows
+            b["stats"] = torch.empty((S, 3), dtype=torch.float32, device=dev)
+            b["logits"] = torch.empty((S, self.V_local), dtype=f16, device=dev)
+            b["gathered"] = torch.empty(self.tp * S * self.V_local, dtype=f16, device=dev)
         self._blk = b
         self._row_graphs.clear()  # captured row blocks point at the old buffers
         return b
@@ -867,7 +876,11 @@ class MotifDecoder:
         q = b["q"].view(-1)[: self.q_heads * S * d].view(self.q_heads, S, d)  # head-major, contiguous
         gu, act, err = b["gu"][:S], b["act"][:S], b["err"]
         mode = 1 if self.vanilla else 0
-        big = S >= self.min_block_rows and self._block_ok()
+        tp = self.tp_group is not None
+        big = S >= self.min_block_rows and self._gemm_ok()
+        # one GPU: the GEMM epilogue adds the residual; otherwise the row-parallel partials are
+        # all-reduced (tensor parallelism) and the residual is folded into the next norm
+        fuse = big and not tp
         split_ws = None
         wsb = lib.motif_prefill_attention_split_workspace_bytes(S, self.q_heads)
         if wsb:
@@ -889,8 +902,8 @@ class MotifDecoder:
                                                  self.lin_ws.numel(), st), "quantized_linear")
 
         def norm_after(residual_out, w):
-            # big: the residual was added in the GEMM epilogue; small: h += residual_out, then the norm
-            if big:
+            # fused: the residual was added in the GEMM epilogue; else h += residual_out, then the norm
+            if fuse:
                 check(lib.motif_rms_norm(0, ptr(h), ptr(w), eps, S, H, ptr(x), st), "rms_norm")
             else:
                 check(lib.motif_add_rms_norm(0, ptr(h), ptr(residual_out), ptr(w), eps, S, H, ptr(x), st),
@@ -916,31 +929,47 @@ class MotifDecoder:
             check(lib.motif_prefill_post(ptr(o), S, self.q_heads, mode, self.q_groups, self.gr, ptr(L["subln"]),
                                          ptr(L["lambda_full"]), L["lambda_full"].numel(), L["lambda_init"],
                                          a.attn_rms_norm_eps, ptr(attn), st), "prefill_post")
-            lin(attn, L["o"], h if big else tmp, residual=h if big else None)
+            lin(attn, L["o"], h if fuse else tmp, residual=h if fuse else None)
+            if tp:
+                self._allreduce(tmp)
             norm_after(tmp, L["post_norm"])
             lin(x, L["gate_up"], gu)
-            check(lib.motif_polynorm_mul(0, ptr(gu), ptr(gu) + 2 * I, 2 * I, ptr(L["polynorm_w"]),
-                                         ptr(L["polynorm_b"]), 1e-6, S, I, ptr(act), st), "polynorm_mul")
-            lin(act, L["down"], h if big else tmp, residual=h if big else None)
+            if tp:  # PolyNorm's means run over the whole intermediate row: sum the ranks' statistics
+                stats = b["stats"][:S]
+                check(lib.motif_polynorm_row_stats(0, ptr(gu), 2 * I, S, I, ptr(stats), st), "polynorm stats")
+                self._allreduce(stats)
+                check(lib.motif_polynorm_mul_stats(0, ptr(gu), ptr(gu) + 2 * I, 2 * I, ptr(L["polynorm_w"]),
+                                                   ptr(L["polynorm_b"]), 1e-6, S, I, ptr(stats),
+                                                   a.intermediate_size, ptr(act), st), "polynorm_mul_stats")
+            else:
+                check(lib.motif_polynorm_mul(0, ptr(gu), ptr(gu) + 2 * I, 2 * I, ptr(L["polynorm_w"]),
+                                             ptr(L["polynorm_b"]), 1e-6, S, I, ptr(act), st), "polynorm_mul")
+            lin(act, L["down"], h if fuse else tmp, residual=h if fuse else None)
+            if tp:
+                self._allreduce(tmp)
         if logits_out is not None:
             norm_after(tmp, self.final_norm)
             ql = self.lm_head
+            local = b["logits"][:S] if tp else logits_out  # this rank's vocabulary shard
             check(lib.motif_quantized_linear(0, 4, 64, ptr(x), S, ql.in_dim, ptr(ql.weight), ptr(ql.scales),
-                                             ptr(ql.biases), ql.out_dim, ptr(logits_out), ptr(self.lin_ws),
+                                             ptr(ql.biases), ql.out_dim, ptr(local), ptr(self.lin_ws),
                                              self.lin_ws.numel(), st), "lm_head rows")
+            if tp:  # rank r holds vocabulary rows [r·V/tp, (r+1)·V/tp): gather them into (S, V)
+                gathered = b["gathered"][: self.tp * S * self.V_local]
+                torch.distributed.all_gather_into_tensor(gathered, local.reshape(-1), group=self.tp_group)
+                logits_out.view(S, self.tp, self.V_local).copy_(gathered.view(self.tp, S, self.V_local).transpose(0, 1))
         if device_offset:
             self.pos_len.add_(S)
         return b
 
     def forward_rows(self, ids, logits_out: torch.Tensor | None = None) -> torch.Tensor:
-        """Feed a block of tokens at the current position and return their logits (S, V) fp16: the
-        batched ``[1, S]`` forward of a speculative verify (one GPU). The cache advances by S."""
-        if self.tp_group is not None:
-            raise ValueError("the row-block forward runs on one GPU")
+        """Feed a block of tokens at the current position and return their logits (S, V) fp16 (the
+        whole vocabulary, gathered from the ranks under tensor parallelism): the batched
+        ``[1, S]`` forward of a speculative verify. The cache advances by S."""
         ids_d = torch.as_tensor(ids, dtype=torch.int32).reshape(-1).to(self.device)
         S = ids_d.numel()
         if logits_out is None:
-            logits_out = torch.empty((S, self.V_local), dtype=torch.float16, device=self.device)
+            logits_out = torch.empty((S, self.V_local * self.tp), dtype=torch.float16, device=self.device)
         key = (S, logits_out.data_ptr())
         if not self._rows_graph_ok(S) or key not in self._rows_seen:
             self._rows_seen.add(key)  # the first call runs eagerly (attributes, buffers), the next captures
@@ -964,7 +993,7 @@ class MotifDecoder:
         """A row block replays as a CUDA graph when its launches take no host-side offset: an fp16
         cache (a quantized cache is dequantized up to the block's rows) and a short block (the
         multi-row GEMV and split attention path). MOTIF_ROWS_GRAPH=0 keeps every call eager."""
-        return (self.cache_kind == "fp16" and 1 <= S < min(self.min_block_rows, 129)
+        return (self.cache_kind == "fp16" and self.tp_group is None and 1 <= S < min(self.min_block_rows, 129)
                 and os.environ.get("MOTIF_ROWS_GRAPH", "1") != "0")
 
     def check_rows_error(self) -> None:
@@ -979,7 +1008,7 @@ class MotifDecoder:
         or more through the prompt path, the rest through the decode step without its head)."""
         ids_d = torch.as_tensor(ids, dtype=torch.int32).reshape(-1).to(self.device)
         n, i = ids_d.numel(), 0
-        if self.tp_group is None and self._block_ok():
+        if self._block_ok():
             while n - i >= self.min_rows_block:
                 S = min(2048, n - i)
                 self._prefill_block(ids_d[i : i + S])

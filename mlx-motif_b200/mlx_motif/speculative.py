@@ -9,6 +9,11 @@ the first rejection, and a bonus token from p_K when all K are accepted. At temp
 rule accepts while the draft equals the target's argmax, so the output equals the target's
 greedy decode.
 
+Under tensor parallelism the target is sharded and the draft is replicated on every rank: each
+rank runs the same draft steps (same seed, same kernels), the verify gathers the full vocabulary
+rows, and the acceptance kernel draws the same tokens everywhere, so the ranks stay in step with
+no extra exchange.
+
 Device work per cycle: K draft decode steps (CUDA graphs, sampling in the head), one target
 row-block forward with logits (a CUDA graph after its first call), one acceptance kernel; the host
 reads back two int32 and the row block's error word per cycle.
@@ -25,8 +30,11 @@ from .model import MotifDecoder
 class SpeculativeDecoder:
     def __init__(self, target: MotifDecoder, draft: MotifDecoder, k: int = 4, temperature: float = 0.7,
                  seed: int = 0):
-        if target.V_local != draft.V_local:
-            raise ValueError(f"target vocabulary {target.V_local} != draft vocabulary {draft.V_local}")
+        if draft.tp_group is not None:
+            raise ValueError("the draft runs on one GPU (under tensor parallelism every rank holds a replica)")
+        V = target.V_local * target.tp  # the verify gathers the target's vocabulary shards
+        if V != draft.V_local:
+            raise ValueError(f"target vocabulary {V} != draft vocabulary {draft.V_local}")
         if not 1 <= k <= 16:
             raise ValueError("k must be in 1..16")
         self.target, self.draft, self.k = target, draft, k
@@ -34,7 +42,7 @@ class SpeculativeDecoder:
         self.seed = int(seed)
         dev = target.device
         self.q_logits = torch.empty((k, draft.V_local), dtype=torch.float16, device=dev)
-        self.p_logits = torch.empty((k + 1, target.V_local), dtype=torch.float16, device=dev)
+        self.p_logits = torch.empty((k + 1, V), dtype=torch.float16, device=dev)
         self.draft_tokens = torch.zeros(k, dtype=torch.int32, device=dev)
         self.verify_ids = torch.zeros(k + 1, dtype=torch.int32, device=dev)
         self.result = torch.zeros(2, dtype=torch.int32, device=dev)
@@ -68,7 +76,8 @@ class SpeculativeDecoder:
             self.verify_ids[1:].copy_(self.draft_tokens)
             t.forward_rows(self.verify_ids, self.p_logits)
             check(lib.motif_speculative_accept(ptr(self.p_logits), ptr(self.q_logits), self.p_logits.shape[1],
-                                               ptr(self.draft_tokens), k, t.V_local, self.temperature, self.seed,
+                                               ptr(self.draft_tokens), k, self.p_logits.shape[1], self.temperature,
+                                               self.seed,
                                                None, base, ptr(self.result), st), "speculative_accept")
             self.result_host.copy_(self.result)
             t.check_rows_error()

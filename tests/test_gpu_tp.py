@@ -72,3 +72,74 @@ def test_tp_decode_equals_single_gpu(world, exchange):
         assert got[r] == got[0], f"rank {r} disagrees on the greedy tokens"
     assert got[0][0] == ref, f"TP{world} tokens {got[0][0]} != single-GPU tokens {ref}"
     assert got[0][1] == ref, f"TP{world} tokens after reset() differ"
+
+
+ROW_PROMPT = [(7 + 13 * i) % 2048 for i in range(170)]  # 170 ids inside the vocabulary
+VERIFY_IDS = [5, 900, 17, 3, 44]
+
+
+def _draft_args():
+    from mlx_motif.model import ModelArgs
+
+    return ModelArgs(hidden_size=512, num_hidden_layers=2, intermediate_size=1024, num_attention_heads=4,
+                     num_key_value_heads=2, num_noise_heads=None, vocab_size=2048)
+
+
+def _rows_worker(rank, world, port, q):
+    import torch.distributed as dist
+    from mlx_motif.model import MotifDecoder
+    from mlx_motif.speculative import SpeculativeDecoder
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60))
+    try:
+        dev = f"cuda:{rank}"
+        m = MotifDecoder.random(_args(), seed=5, std=0.05, max_seq=256, device=dev, tp_group=dist.group.WORLD,
+                                rank=rank, world=world)
+        m.prefill(ROW_PROMPT)  # a 169-row block: GEMMs (TP2) or the multi-row GEMV (TP4), all-reduced
+        first = int(m.token.item())
+        rows = m.forward_rows(VERIFY_IDS).float().cpu().numpy()
+        draft = MotifDecoder.random(_draft_args(), seed=12, std=0.05, max_seq=256, device=dev)
+        spec = SpeculativeDecoder(m, draft, k=4, temperature=0.0)
+        toks = spec.generate(ROW_PROMPT[:40], 12)
+        m._graphs.clear()
+        torch.cuda.synchronize()
+        dist.barrier()
+        m.release_exchange()
+        q.put((rank, (first, rows, toks)))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_tp_row_blocks_and_speculative_verify(world):
+    """Prompt ingestion in row blocks and the [1, K+1] verify under tensor parallelism (NCCL
+    all-reduce of the row-parallel outputs and of the PolyNorm statistics, the lm_head shards
+    gathered) agree with one GPU; speculative greedy decoding with a replicated draft
+    reproduces the single-GPU greedy tokens on every rank."""
+    from mlx_motif.model import MotifDecoder
+
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = 29950 + (os.getpid() % 40) + 3 * world
+    procs = [ctx.Process(target=_rows_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    got = dict(q.get(timeout=300) for _ in procs)
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    ref = MotifDecoder.random(_args(), seed=5, std=0.05, max_seq=256, device="cuda:0")
+    ref.prefill(ROW_PROMPT)
+    first = int(ref.token.item())
+    rows = ref.forward_rows(VERIFY_IDS).float().cpu().numpy()
+    ref.reset()  # generate() prefills at the current position
+    greedy = ref.generate(ROW_PROMPT[:40], 12)
+    for r in range(world):
+        assert got[r][0] == first, f"rank {r}: first token {got[r][0]} != {first}"
+        err = float(abs(got[r][1] - rows).max())
+        assert err < 5e-2, f"rank {r}: verify logits differ by {err}"
+        assert got[r][2] == greedy, f"rank {r}: speculative tokens {got[r][2]} != greedy {greedy}"
