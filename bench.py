@@ -547,70 +547,22 @@ def run_b200(a) -> None:
             "kernels_per_step": model_launches(m),
         }
         # ---- config[4]: speculative decoding, this 2.6B-class draft + the 12.7B-class target ----
+        m._graphs.clear()
+        del m
+        torch.cuda.empty_cache()
         if not a.no_spec:
-            from mlx_motif.speculative import SpeculativeDecoder
+            extra["speculative"] = speculative_extra(a, args, van, dev, st, e0, e1, group, rank, world)
 
-            m._graphs.clear()
-            del m
+    # config[4] under tensor parallelism, at the rank counts its tests cover
+    if world in (2, 4) and not a.no_spec:
+        if model is not None:
+            model._graphs.clear()
+            del model
+            model = None
             torch.cuda.empty_cache()
-            n_prompt, n_gen, K, T = 800, 256, 4, 0.7
-            cap = n_prompt + n_gen + 2 * K + 16
-            draft = MotifDecoder.random(van, seed=0, cache="fp16", max_seq=cap, device=dev)
-            target = MotifDecoder.random(args, seed=0, cache="fp16", max_seq=cap, device=dev)
-            sprompt = np.random.default_rng(4).integers(0, args.vocab_size, n_prompt).tolist()
-            spec = SpeculativeDecoder(target, draft, k=K, temperature=T, seed=0)
-            spec.generate(sprompt, 16)  # warm-up: graphs, buffers
-            spec.stats = {k2: 0 for k2 in spec.stats}
-            torch.cuda.synchronize()
-            t0 = time.perf_counter()
-            toks = spec.generate(sprompt, n_gen)
-            torch.cuda.synchronize()
-            wall = time.perf_counter() - t0
-            st_ = spec.stats
-            # one [1, K+1] verify forward (multi-row GEMVs, logits for every row) against one decode
-            # step of the target; both rewound so the cache stays at the same length
-            vids = torch.as_tensor(sprompt[: K + 1], dtype=torch.int32, device=dev)
-            plog = torch.empty((K + 1, target.V_local), dtype=torch.float16, device=dev)
-            base = target.offset
-
-            def verify_once():
-                target.forward_rows(vids, plog)
-                target.rewind(base)
-
-            def step_once():
-                target.step_device(with_head=True)
-                target.rewind(base)
-
-            rows_ms = {}
-            for name, fn in (("verify_forward_ms", verify_once), ("decode_step_ms", step_once)):
-                for _ in range(3):
-                    fn()
-                torch.cuda.synchronize()
-                e0.record(st)
-                for _ in range(10):
-                    fn()
-                e1.record(st)
-                torch.cuda.synchronize()
-                rows_ms[name] = round(e0.elapsed_time(e1) / 10, 3)
-            extra["speculative"] = {
-                "workload": "config[4]: draft 2.6B-class vanilla q4, target 12.7B-class GDA q4 (1 GPU), K=4, "
-                            "temperature 0.7, top-p 1.0, 800 random prompt ids, 256 generated tokens; wall time "
-                            "includes both prompts' ingestion",
-                "tok_s": round(len(toks) / wall, 2), "seconds": round(wall, 3),
-                "acceptance": round(st_["accepted"] / max(1, st_["drafted"]), 4),
-                "target_forwards": st_["target_forwards"], "cycles": st_["cycles"],
-                **rows_ms,
-                "note": "draft and target are independent random-init models, so few draft tokens match "
-                        "the target's distribution; the verify forward streams the target's weights once for "
-                        "its K+1 rows (multi-row GEMV); the verify replays a CUDA graph (positions read from "
-                        "the device offset), verify_forward_ms also covers the host's rewind between calls",
-            }
-            del spec, draft, target
-            torch.cuda.empty_cache()
-        else:
-            m._graphs.clear()
-            del m
-            torch.cuda.empty_cache()
+        van = ModelArgs(hidden_size=2048, num_hidden_layers=32, intermediate_size=8192, num_attention_heads=16,
+                        num_key_value_heads=4, num_noise_heads=None, vocab_size=a.vocab)
+        extra["speculative"] = speculative_extra(a, args, van, dev, st, e0, e1, group, rank, world)
 
     cpu = None
     if rank == 0 and world == 1 and not a.no_cpu_baseline:
@@ -648,6 +600,80 @@ def prefill_flops(model, n: int) -> float:
     pairs = n * (n + 1) / 2
     attn = len(model.layers) * model.q_heads * pairs * 2 * (model.d + 2 * model.d)
     return 2.0 * lin * n + attn + 2.0 * model.lm_head.out_dim * model.lm_head.in_dim
+
+
+def speculative_extra(a, args, van, dev, st, e0, e1, group, rank, world) -> dict:
+    """config[4]: the 2.6B-class draft (a replica on every rank) and the 12.7B-class target (sharded
+    under tensor parallelism); tok/s over the generated tokens, max over ranks."""
+    import numpy as np
+    import torch
+
+    from mlx_motif.model import MotifDecoder
+    from mlx_motif.speculative import SpeculativeDecoder
+
+    par = "1 GPU" if world == 1 else f"TP{world}, draft replicated"
+    n_prompt, n_gen, K, T = 800, 256, 4, 0.7
+    cap = n_prompt + n_gen + 2 * K + 16
+    draft = MotifDecoder.random(van, seed=0, cache="fp16", max_seq=cap, device=dev)
+    target = MotifDecoder.random(args, seed=0, cache="fp16", max_seq=cap, device=dev, tp_group=group, rank=rank,
+                                 world=world)
+    sprompt = np.random.default_rng(4).integers(0, args.vocab_size, n_prompt).tolist()
+    spec = SpeculativeDecoder(target, draft, k=K, temperature=T, seed=0)
+    spec.generate(sprompt, 16)  # warm-up: graphs, buffers
+    spec.stats = {k2: 0 for k2 in spec.stats}
+    torch.cuda.synchronize()
+    barrier(world)
+    t0 = time.perf_counter()
+    toks = spec.generate(sprompt, n_gen)
+    torch.cuda.synchronize()
+    wall = max_over_ranks(time.perf_counter() - t0, world)
+    st_ = spec.stats
+    # one [1, K+1] verify forward (multi-row GEMVs, logits for every row) against one decode
+    # step of the target; both rewound so the cache stays at the same length
+    vids = torch.as_tensor(sprompt[: K + 1], dtype=torch.int32, device=dev)
+    plog = torch.empty((K + 1, target.V_local * target.tp), dtype=torch.float16, device=dev)
+    base = target.offset
+
+    def verify_once():
+        target.forward_rows(vids, plog)
+        target.rewind(base)
+
+    def step_once():
+        target.step_device(with_head=True)
+        target.rewind(base)
+
+    rows_ms = {}
+    for name, fn in (("verify_forward_ms", verify_once), ("decode_step_ms", step_once)):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        barrier(world)
+        e0.record(st)
+        for _ in range(10):
+            fn()
+        e1.record(st)
+        torch.cuda.synchronize()
+        rows_ms[name] = round(max_over_ranks(e0.elapsed_time(e1), world) / 10, 3)
+    out = {
+        "workload": f"config[4]: draft 2.6B-class vanilla q4, target 12.7B-class GDA q4 ({par}), K=4, "
+                    "temperature 0.7, top-p 1.0, 800 random prompt ids, 256 generated tokens; wall time "
+                    "includes both prompts' ingestion",
+        "tok_s": round(len(toks) / wall, 2), "seconds": round(wall, 3),
+        "acceptance": round(st_["accepted"] / max(1, st_["drafted"]), 4),
+        "target_forwards": st_["target_forwards"], "cycles": st_["cycles"],
+        **rows_ms,
+        "note": "draft and target are independent random-init models, so few draft tokens match "
+                "the target's distribution; the verify forward streams the target's weights once for "
+                "its K+1 rows (multi-row GEMV); on one GPU the verify replays a CUDA graph (positions "
+                "read from the device offset), under TP it runs eagerly with NCCL all-reduces; "
+                "verify_forward_ms and decode_step_ms also cover the host's rewind between calls",
+    }
+    target._graphs.clear()  # graphs may hold NCCL calls: released before the communicator
+    torch.cuda.synchronize()
+    barrier(world)
+    del spec, draft, target
+    torch.cuda.empty_cache()
+    return out
 
 
 def timed_prefill(model, prompt) -> float:
