@@ -308,7 +308,7 @@ __global__ void __launch_bounds__(kPAThreads, 1) prefill_attn_kernel(const __gri
     const bool live = fin && r < rows;
     const float inv_l = l > 0.f ? 1.f / l : 0.f;
     __half* dst = a.out + ((int64_t)(q0 + r) * a.QH + h) * 256;
-    float* pdst = a.part + (((int64_t)h * nsplit + split) * a.S + q0 + r) * kPartStride;
+    float* pdst = nsplit > 1 ? a.part + (((int64_t)h * nsplit + split) * a.S + q0 + r) * kPartStride : nullptr;
     if (nsplit > 1 && live) {
       pdst[256] = m_ref;
       pdst[257] = l;
