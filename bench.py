@@ -456,6 +456,7 @@ def run_b200(a) -> None:
                 "frac": round(gem["gbs"] / peak, 4), "traffic": traffic,
                 "bytes_per_launch": round(gem["bytes_per_launch"]), "ms_per_launch": round(gem["ms_per_launch"], 5)}
     attn_p164 = time_attention(model)
+    attn_p164["attention_kernel"] = model.attention_kernel()
     step_frac = bytes_per_step / world / (ms / a.steps / 1e3) / 1e9 / peak
 
     extra = {"weights_gb": round(model.weight_bytes * world / 1e9, 3), "init_s": round(t_init, 1),
@@ -499,6 +500,7 @@ def run_b200(a) -> None:
             att = time_attention(m)
             extra[f"p16k_{kind}"] = {
                 "tok_s": round(a.steps / (lms / 1e3), 2), "ms_per_step": round(lms / a.steps, 4),
+                "attention_kernel": m.attention_kernel(), "cache_capacity": int(m._slots[0].capacity),
                 "attention_gbs": round(att["gbs"], 1), "attention_frac": round(att["gbs"] / peak, 4),
                 "attention_ms_per_step": round(att["ms_48_layers"], 4),
                 "peak_hbm_bytes": int(torch.cuda.max_memory_allocated(dev)),

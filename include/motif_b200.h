@@ -140,13 +140,18 @@ MOTIF_API int motif_sdpa_dual_v(int dtype, const void* q, const void* k, const v
  * file-scope __device__ array of motif_sdpa_dual_v_static_scratch_bytes()
  * (4 MiB) that each GPU loading the library keeps until exit. The first
  * call on a device resolves the array's device address (call it once
- * before any stream capture). Shapes whose two-split partials
+ * before any stream capture; concurrent first calls from several host
+ * threads are safe). Shapes whose two-split partials
  * (batch*h_q*(2*head_dim+2)*4*2 bytes) exceed the array are rejected with
- * MOTIF_ERR_WORKSPACE. Nothing in the array needs to start at zero (every
- * split writes its partial before the merge reads it), but all calls share
- * it: calls that overlap on the GPU (different streams, or devices sharing
- * nothing else) race and must be serialised by the caller. Otherwise the
- * same arguments and results as motif_sdpa_dual_v. */
+ * MOTIF_ERR_WORKSPACE. The rejection is deliberate: this entry is the
+ * split-KV kernel with its partials in the array, and a shape too large for
+ * it is refused with a clear error rather than silently run as one long
+ * split (motif_sdpa_dual_v with workspace_bytes 0 is that one-split form,
+ * for a caller that wants it). Nothing in the array needs to start at zero
+ * (every split writes its partial before the merge reads it), but all calls
+ * on one device share that device's copy: calls that overlap on the GPU
+ * (on different streams) race and must be serialised by the caller. Otherwise
+ * the same arguments and results as motif_sdpa_dual_v. */
 MOTIF_API size_t motif_sdpa_dual_v_static_scratch_bytes(void);
 MOTIF_API int motif_sdpa_dual_v_static(int dtype, const void* q, const void* k, const void* v1,
                                        const void* v2, float scale, int64_t batch, int64_t h_q,
@@ -219,6 +224,19 @@ MOTIF_API int motif_vanilla_decode_step(const void* qkv, const float* inv_freq, 
                                         const void* subln_w, const float* lambda_full, float lambda_init,
                                         float eps, void* out, void* workspace, size_t workspace_bytes,
                                         void* stream);
+
+/* Which kernel motif_gda_decode_step / motif_vanilla_decode_step launch for
+ * this cache (no reference counterpart: the reference has one Metal kernel
+ * per dtype, kernels/attention.py:190-260 and 510-645). Returns
+ * MOTIF_ATTN_KERNEL_TCGEN05 for the tensor-core long-cache step (fp16 rows,
+ * or q4 group 64 with a capacity that is a multiple of 4, capacity at least
+ * MOTIF_LONG_ATTN_MIN_CAP rows, default 2048, 16-byte aligned slots),
+ * MOTIF_ATTN_KERNEL_SPLIT for the CUDA-core split-KV step, or a negative
+ * status for a cache neither accepts. Pure host arithmetic on the view: no
+ * CUDA call, so it answers on a machine without a GPU. */
+#define MOTIF_ATTN_KERNEL_SPLIT 1
+#define MOTIF_ATTN_KERNEL_TCGEN05 2
+MOTIF_API int motif_decode_step_kernel(const motif_kv4_slots* cache);
 
 /* ---- affine quantization ---------------------------------------------------
  * MLX-layout affine group quantization along the last axis (bits 4 or 8):

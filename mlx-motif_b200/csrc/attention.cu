@@ -16,6 +16,7 @@
 // Packed caches (bits 4/8, MLX affine triples) are dequantized in registers:
 // a lane's D/32 channels sit in one uint32 and one scale/bias group, the same
 // lane→word contract the reference enforces (attention.py:565-608).
+#include <atomic>
 #include <cmath>
 
 #include "common.cuh"
@@ -1521,21 +1522,31 @@ int64_t long_min_cap() {
   return v ? atoll(v) : 2048;
 }
 
-// The tensor-core step's maps over the four slots (fp16, or q4 group 64 with the capacity a
-// multiple of 4), or false when the cache does not fit it.
-bool long_maps(const motif_kv4_slots& c, LongMaps& m) {
+// Whether the tensor-core step takes this cache: fp16 rows, or q4 group 64 with the capacity a
+// multiple of 4 (scales and biases travel as 16-byte lines of four rows, so a head's rows must
+// start on a line), a capacity of at least long_min_cap() rows and 16-byte aligned slots. Host
+// arithmetic only; the caches of mlx_motif allocate whole 256-row steps, so the capacity rule
+// always holds for them.
+bool long_eligible(const motif_kv4_slots& c) {
   if (c.capacity < long_min_cap() || c.heads >= kLErrSlot || c.heads * c.capacity >= (1ll << 31)) return false;
   const bool q4 = c.bits == 4 && c.group_size == 64 && c.capacity % 4 == 0;
   if (c.bits != 16 && !q4) return false;
+  for (int i = 0; i < 4; ++i) {
+    uintptr_t addr = reinterpret_cast<uintptr_t>(c.data[i]);
+    if (c.bits != 16) addr |= reinterpret_cast<uintptr_t>(c.scales[i]) | reinterpret_cast<uintptr_t>(c.biases[i]);
+    if (!c.data[i] || addr % 16) return false;
+  }
+  return true;
+}
+
+// The tensor-core step's maps over the four slots, or false when the cache does not fit it.
+bool long_maps(const motif_kv4_slots& c, LongMaps& m) {
+  if (!long_eligible(c)) return false;
   const uint64_t rows = (uint64_t)(c.heads * c.capacity);
   for (int i = 0; i < 4; ++i) {
     if (c.bits == 16) {
-      if (reinterpret_cast<uintptr_t>(c.data[i]) % 16) return false;
       if (!encode_tma_rows(&m.slot[i], c.data[i], 256, rows, 128, kLT, true)) return false;
     } else {
-      if ((reinterpret_cast<uintptr_t>(c.data[i]) | reinterpret_cast<uintptr_t>(c.scales[i]) |
-           reinterpret_cast<uintptr_t>(c.biases[i])) % 16)
-        return false;
       if (!encode_tma_rows(&m.slot[i], c.data[i], 64, rows, 64, kLT, false) ||
           !encode_tma_rows(&m.sc[i], c.scales[i], 16, rows / 4, 16, kLT / 4, false) ||
           !encode_tma_rows(&m.bi[i], c.biases[i], 16, rows / 4, 16, kLT / 4, false))
@@ -1584,6 +1595,13 @@ int check_fused_cache(const motif_kv4_slots& c, int64_t groups, const char* who)
 }  // namespace motif
 
 extern "C" {
+
+int motif_decode_step_kernel(const motif_kv4_slots* cache) {
+  if (!cache) return -fail(MOTIF_ERR_NULL, "decode_step_kernel: null cache");
+  const motif_kv4_slots& c = *cache;
+  if (int rc = check_fused_cache(c, c.heads, "decode_step_kernel")) return -rc;
+  return long_eligible(c) ? MOTIF_ATTN_KERNEL_TCGEN05 : MOTIF_ATTN_KERNEL_SPLIT;
+}
 
 size_t motif_gda_decode_step_workspace_bytes(int64_t q_heads, int64_t head_dim, int64_t max_splits) {
   if (q_heads <= 0 || head_dim <= 0 || max_splits <= 0) return 0;
@@ -1726,7 +1744,9 @@ constexpr size_t kStaticScratchBytes = 4u << 20;  // 4 MiB of split partials
 static __device__ __align__(256) float g_attn_scratch[kStaticScratchBytes / sizeof(float)];
 
 constexpr int kMaxDevices = 64;
-static void* g_scratch_ptr[kMaxDevices] = {};
+// One resolved address per device. Atomic, so host threads making their first call on the
+// same device at the same time do not race: each may resolve it, all store the same value.
+static std::atomic<void*> g_scratch_ptr[kMaxDevices];
 
 // Host code may not use g_attn_scratch as a device address: it names the
 // host-side stand-in. Resolve the device address once per device, with that
@@ -1736,14 +1756,14 @@ int static_scratch(void** out) {
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return fail(MOTIF_ERR_CUDA, "sdpa_dual_v_static: cudaGetDevice: %s", cudaGetErrorString(e));
   if (dev < 0 || dev >= kMaxDevices) return fail(MOTIF_ERR_CUDA, "sdpa_dual_v_static: device %d out of range", dev);
-  if (!g_scratch_ptr[dev]) {
-    void* p = nullptr;
+  void* p = g_scratch_ptr[dev].load(std::memory_order_acquire);
+  if (!p) {
     e = cudaGetSymbolAddress(&p, g_attn_scratch);
     if (e != cudaSuccess || !p)
       return fail(MOTIF_ERR_CUDA, "sdpa_dual_v_static: cudaGetSymbolAddress: %s", cudaGetErrorString(e));
-    g_scratch_ptr[dev] = p;
+    g_scratch_ptr[dev].store(p, std::memory_order_release);
   }
-  *out = g_scratch_ptr[dev];
+  *out = p;
   return MOTIF_OK;
 }
 

@@ -172,15 +172,35 @@ __device__ __forceinline__ long long tp_pair(float v, int number) {
   return (long long)(((unsigned long long)(uint32_t)number << 32) | __float_as_uint(v));
 }
 
-// Read an exchanged pair written by some rank (L2, so a peer's store is seen), re-reading
-// until it carries `number`; on time-out it records the error and returns what is there.
+// Exchange accesses. A pair is one naturally aligned 64-bit element, stored and loaded as a
+// single relaxed system-scope access (peers write it over NVLink), so a reader that sees the
+// expected number also sees the value stored with it: a pair cannot tear, and no fence is
+// needed because nothing else is read on the strength of it.
+__device__ __forceinline__ void tp_store(long long* p, long long v) {
+  asm volatile("st.relaxed.sys.global.b64 [%0], %1;\n" ::"l"(p), "l"(v) : "memory");
+}
+
+__device__ __forceinline__ long long tp_load(const long long* p) {
+  long long v;
+  asm volatile("ld.relaxed.sys.global.b64 %0, [%1];\n" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Two adjacent pairs in one 16-byte load; each 64-bit element is its own single-copy-atomic
+// access (the vector form does not make the two elements one access, nor does it need to).
+__device__ __forceinline__ void tp_load2(const long long* p, long long& a, long long& b) {
+  asm volatile("ld.relaxed.sys.global.v2.b64 {%0, %1}, [%2];\n" : "=l"(a), "=l"(b) : "l"(p) : "memory");
+}
+
+// Read an exchanged pair written by some rank, re-reading until it carries `number`; on
+// time-out it records the error and returns what is there.
 __device__ __forceinline__ float tp_read(const long long* p, int number, int* err) {
-  long long x = __ldcg(p);
+  long long x = tp_load(p);
   if ((int)(x >> 32) != number) {
     const unsigned long long t0 = global_ns();
     do {
       __nanosleep(32);
-      x = __ldcg(p);
+      x = tp_load(p);
       if (global_ns() - t0 > kTpWaitNs) {
         if (err) atomicExch(err, 2);
         break;
@@ -340,7 +360,7 @@ __device__ void tile_epilogue(const LinArgs& a, int tile, int gw, float acc_r, f
     a.y[row] = hv;
     if (a.tp_world && a.tp_out[0]) {  // this rank's fp32 rows into every rank's exchange buffer
       const long long pr = tp_pair(v, tp_number(a));
-      for (int r = 0; r < a.tp_world; ++r) a.tp_out[r][row] = pr;
+      for (int r = 0; r < a.tp_world; ++r) tp_store(a.tp_out[r] + row, pr);
     }
   }
   // all-or-nothing per warp: `have` is uniform across lanes 0..15 of the finishing warp
@@ -358,9 +378,9 @@ __device__ void tile_epilogue(const LinArgs& a, int tile, int gw, float acc_r, f
       if (a.tp_world && a.tp_stats[0]) {
         const int num = tp_number(a);
         for (int r = 0; r < a.tp_world; ++r) {
-          a.tp_stats[r][tile * 3 + 0] = tp_pair(s2, num);
-          a.tp_stats[r][tile * 3 + 1] = tp_pair(s4, num);
-          a.tp_stats[r][tile * 3 + 2] = tp_pair(s6, num);
+          tp_store(a.tp_stats[r] + tile * 3 + 0, tp_pair(s2, num));
+          tp_store(a.tp_stats[r] + tile * 3 + 1, tp_pair(s4, num));
+          tp_store(a.tp_stats[r] + tile * 3 + 2, tp_pair(s6, num));
         }
       }
     }
@@ -435,16 +455,15 @@ __device__ void stage_x(const LinArgs& a, __half* xp_s, float* xsum_s, float* co
       float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll 4
       for (int r = 0; r < a.tp_world; ++r) {
-        // 8 pairs = four 16-byte L2 loads; a pair not yet carrying this number is re-read alone
+        // 8 pairs = four 16-byte loads of two 64-bit pairs each; a pair not yet carrying this
+        // number is re-read alone
         const long long* p = a.tp_in + (int64_t)r * K + (int64_t)w * 8;
-        int4 q[4];
+        long long q[8];
 #pragma unroll
-        for (int j = 0; j < 4; ++j) q[j] = __ldcg(reinterpret_cast<const int4*>(p) + j);
+        for (int j = 0; j < 4; ++j) tp_load2(p + 2 * j, q[2 * j], q[2 * j + 1]);
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          acc[2 * j] += q[j].y == num ? __int_as_float(q[j].x) : tp_read(p + 2 * j, num, a.err);
-          acc[2 * j + 1] += q[j].w == num ? __int_as_float(q[j].z) : tp_read(p + 2 * j + 1, num, a.err);
-        }
+        for (int j = 0; j < 8; ++j)
+          acc[j] += (int)(q[j] >> 32) == num ? __uint_as_float((uint32_t)q[j]) : tp_read(p + j, num, a.err);
       }
       store_vec<__half, 8>(delta_s + (int64_t)w * 8, acc);
     }

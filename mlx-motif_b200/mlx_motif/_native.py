@@ -22,6 +22,8 @@ LIB_PATH = Path(__file__).resolve().parent / "libmotif_b200.so"
 
 OK, ERR_NULL, ERR_BAD_SHAPE, ERR_BAD_CONTRACT, ERR_DTYPE, ERR_CUDA, ERR_WORKSPACE = range(7)
 F16, BF16, F32 = 0, 1, 2
+ATTN_KERNEL_SPLIT, ATTN_KERNEL_TCGEN05 = 1, 2
+ATTN_KERNEL_NAMES = {ATTN_KERNEL_SPLIT: "split", ATTN_KERNEL_TCGEN05: "tcgen05"}
 
 _DTYPE_CODES = {torch.float16: F16, torch.bfloat16: BF16, torch.float32: F32}
 
@@ -118,6 +120,7 @@ SIGNATURES = {
         _I,
         [_P, _P, _KV, _P, _F, _L, _L, _P, _P, _F, _F, _P, _P, _S, _P],
     ),
+    "motif_decode_step_kernel": (_I, [_KV]),
     "motif_gda_decode_attention": (
         _I,
         [_P, _KV, _F, _L, _L, _L, _P, _P, _P, _L, _F, _F, _P, _P, _S, _P],

@@ -15,7 +15,8 @@ groups never cross the head axis).
 
 Capacity: by default slots grow in ``step``-row increments like the reference
 (``cache.py:245-265``). Passing ``max_size`` preallocates the whole capacity
-once, so the buffers never move — the form a captured CUDA graph needs.
+once, rounded up to whole ``step`` blocks, so the buffers never move — the
+form a captured CUDA graph needs.
 """
 
 from __future__ import annotations
@@ -102,12 +103,16 @@ class MotifGroupedKVCacheBase:
         if self.k1 is not None and prev + S <= self._slot_capacity(self.k1):
             return
         if self.max_size is not None:
-            if self.k1 is None and prev + S <= self.max_size:
+            # Whole `step`-row blocks, the reference's growth unit: every capacity is then a
+            # multiple of 256, which the tensor-core decode step's q4 tiles (four rows of scales
+            # per 16-byte line) and 128-row TMA boxes rely on. Reads stay bounded by the offset.
+            cap = -(-self.max_size // self.step) * self.step
+            if self.k1 is None and prev + S <= cap:
                 self.k1, self.k2, self.v1, self.v2 = (
-                    self._init_storage(B, H, self.max_size, D, dtype, device) for _ in range(4)
+                    self._init_storage(B, H, cap, D, dtype, device) for _ in range(4)
                 )
                 return
-            raise ValueError(f"cache capacity {self.max_size} exceeded (offset {prev} + {S} rows)")
+            raise ValueError(f"cache capacity {cap} exceeded (offset {prev} + {S} rows)")
         new_len = ((self.step + S - 1) // self.step) * self.step
         if self.k1 is None:
             self.k1, self.k2, self.v1, self.v2 = (

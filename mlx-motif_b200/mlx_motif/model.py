@@ -458,6 +458,15 @@ class MotifDecoder:
         return dict(embed=self.embed, final_norm=self.final_norm, lm_head=self.lm_head,
                     layers=[dict(L) for L in self.layers])
 
+    def attention_kernel(self) -> str:
+        """Which kernel the fused decode step launches for this decoder's caches: "tcgen05" (the
+        tensor-core long-cache step) or "split" (the CUDA-core split-KV step); from
+        ``motif_decode_step_kernel``, so it is the library's own choice, not a re-derivation."""
+        k = lib.motif_decode_step_kernel(self._slots[0])
+        if k < 0:
+            check(-k, "decode_step_kernel")
+        return {1: "split", 2: "tcgen05"}[k]
+
     def kv_bytes_per_token(self, kv_len: int) -> int:
         """KV-cache bytes the attention reads at one step (4 slots, all layers)."""
         d = self.d

@@ -84,3 +84,60 @@ def test_workspace_queries():
     assert N.lib.motif_quantized_linear_workspace_bytes(1, 4096, 512, 4, 64) == 0
     assert N.lib.motif_linear_fused_workspace_bytes(8192, 4096) > 0
     assert N.lib.motif_argmax_workspace_bytes(219520) >= 8
+
+
+def _fake_slots(bits: int, capacity: int, heads: int = 8, base: int = 1 << 20):
+    """A 4-slot view over fake, 16-byte aligned addresses (the query never dereferences them)."""
+    from mlx_motif import _native as N
+
+    s = N.motif_kv4_slots()
+    for i in range(4):
+        s.data[i] = base + i * (1 << 28)
+        s.scales[i] = None if bits == 16 else base + (4 + i) * (1 << 28)
+        s.biases[i] = None if bits == 16 else base + (8 + i) * (1 << 28)
+    s.bits, s.group_size, s.batch, s.heads, s.capacity, s.head_dim = bits, 64, 1, heads, capacity, 128
+    return s
+
+
+def test_decode_step_kernel_query(monkeypatch):
+    """The decode step's kernel choice, answered without a GPU: the tensor-core step for long fp16
+    caches and for q4 caches whose capacity is a multiple of 4; the CUDA-core split step below
+    the length threshold, for q8, and for a q4 capacity the tensor-core tiles cannot address."""
+    from mlx_motif import _native as N
+
+    monkeypatch.delenv("MOTIF_LONG_ATTN_MIN_CAP", raising=False)
+    q = N.lib.motif_decode_step_kernel
+    assert q(_fake_slots(16, 16128)) == N.ATTN_KERNEL_TCGEN05
+    assert q(_fake_slots(4, 16128)) == N.ATTN_KERNEL_TCGEN05
+    assert q(_fake_slots(4, 16033)) == N.ATTN_KERNEL_SPLIT  # a raw, unrounded capacity
+    assert q(_fake_slots(8, 16128)) == N.ATTN_KERNEL_SPLIT
+    assert q(_fake_slots(16, 512)) == N.ATTN_KERNEL_SPLIT
+    bad = _fake_slots(16, 4096)
+    bad.data[2] = (1 << 20) + 8  # not 16-byte aligned: no TMA
+    assert q(bad) == N.ATTN_KERNEL_SPLIT
+    monkeypatch.setenv("MOTIF_LONG_ATTN_MIN_CAP", "0")
+    assert q(_fake_slots(16, 512)) == N.ATTN_KERNEL_TCGEN05
+    wrong = _fake_slots(16, 4096)
+    wrong.head_dim = 64
+    assert q(wrong) < 0
+    assert q(None) == -N.ERR_NULL
+
+
+def test_preallocated_capacity_rounds_to_whole_steps():
+    """max_size preallocation rounds the capacity up to whole 256-row steps (the reference's
+    growth unit), so a bench or decoder sizing the cache as prompt + steps + margin (16033 rows)
+    still gets a capacity the tensor-core q4 step takes."""
+    import torch
+
+    from mlx_motif.cache import MotifGroupedKVCache, MotifGroupedQuantizedKVCache
+
+    c = MotifGroupedQuantizedKVCache(64, 4, max_size=16033)
+    c._grow(1, 8, 1, 128, torch.float16, "cpu")
+    assert c.k1[0].shape == (1, 8, 16128, 16) and c.k1[1].shape == (1, 8, 16128, 2)
+    f = MotifGroupedKVCache(max_size=256)
+    f._grow(1, 8, 1, 128, torch.float16, "cpu")
+    assert f.k1.shape[2] == 256
+    with pytest.raises(ValueError, match="capacity 256 exceeded"):
+        f.offset = 200
+        f.k1 = None
+        f._grow(1, 8, 100, 128, torch.float16, "cpu")

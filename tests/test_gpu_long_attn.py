@@ -108,3 +108,43 @@ def test_long_decode_step_matches_oracle_and_short_path(cuda, monkeypatch, kind,
         ref = O.vanilla_attention_reference(qr, K, V_paired, O.OracleVanillaKVCache(), lam, 0.35, subln, 1e-5,
                                             kv_dtype=np.float16 if kind == "fp16" else np.float32)
     assert_close(down(outs["long"]), ref.reshape(-1).astype(np.float64), "float16", what="long step vs oracle")
+
+
+def test_q4_cache_of_unrounded_length_takes_tensor_core_step(cuda, monkeypatch):
+    """A q4 cache sized like the bench's p16k run (16000 prompt rows + warm-up + steps + margin
+    = 16033 rows, not a multiple of 4) is preallocated in whole 256-row steps, so the decode step
+    takes the tensor-core kernel (reported by motif_decode_step_kernel), and its output matches the
+    CUDA-core split step on the same cache."""
+    from mlx_motif import _native as N
+    from mlx_motif.cache import MotifGroupedQuantizedKVCache
+    from mlx_motif.model import rope_inv_freq
+
+    monkeypatch.delenv("MOTIF_LONG_ATTN_MIN_CAP", raising=False)
+    G, gr, d, kv_len = 8, 3, 128, 16000
+    qh = G * (gr + 1)
+    rng = np.random.default_rng(5)
+    c = MotifGroupedQuantizedKVCache(64, 4, max_size=16033)
+    c.update_and_fetch_4_quantized(*(up(rounded(rng.standard_normal((1, G, kv_len - 1, d)) * 0.5, "float16"))
+                                     for _ in range(4)))
+    assert c.k1[0].shape[2] == 16128
+    assert N.lib.motif_decode_step_kernel(c.slots_struct()) == N.ATTN_KERNEL_TCGEN05
+    inv = rope_inv_freq(d, 10000.0, cuda)
+    pos_t = torch.tensor([kv_len - 1, kv_len], dtype=torch.int32, device=cuda)
+    tq = up(rounded(rng.standard_normal(qh * d + 4 * G * d), "float16"))
+    t_sub = up(rounded(1 + 0.02 * rng.standard_normal(2 * d), "float16"))
+    t_lam = torch.tensor([0.37], dtype=torch.float32, device=cuda)
+    wb = N.lib.motif_gda_decode_step_workspace_bytes(qh, d, 64)
+    outs = {}
+    for path, min_cap in (("tcgen05", None), ("split", str(1 << 40))):
+        if min_cap is None:
+            monkeypatch.delenv("MOTIF_LONG_ATTN_MIN_CAP", raising=False)
+        else:
+            monkeypatch.setenv("MOTIF_LONG_ATTN_MIN_CAP", min_cap)
+        want = N.ATTN_KERNEL_TCGEN05 if path == "tcgen05" else N.ATTN_KERNEL_SPLIT
+        assert N.lib.motif_decode_step_kernel(c.slots_struct()) == want
+        ws = torch.zeros(wb, dtype=torch.uint8, device=cuda)
+        out = torch.full((G * gr * 2 * d,), float("nan"), dtype=torch.float16, device=cuda)
+        N.check(_run_step(N, "gda", tq, inv, c.slots_struct(), pos_t, d, G, gr, t_sub, t_lam, 1, out, ws, wb), path)
+        torch.cuda.synchronize()
+        outs[path] = out
+    assert_close(down(outs["tcgen05"]), down(outs["split"]), "float16", what="tcgen05 vs split step at 16033")

@@ -44,8 +44,9 @@ def test_vanilla_cache_state_views_and_markers():
     assert c.offset == S and c.meta_state == ("slab",)
     assert torch.equal(c.keys, keys) and torch.equal(c.values, slab)
     assert torch.equal(c.hf_ordered_values(), paired)
-    # device form: k1/k2 = even/odd k heads, v1/v2 = the two slabs, capacity preallocated
-    assert c.k1.shape == (B, hk, 32, d)
+    # device form: k1/k2 = even/odd k heads, v1/v2 = the two slabs, capacity preallocated in
+    # whole 256-row steps
+    assert c.k1.shape == (B, hk, 256, d)
     assert torch.equal(c.k1[:, :, :S], keys[:, 0::2]) and torch.equal(c.k2[:, :, :S], keys[:, 1::2])
     assert torch.equal(c.v1[:, :, :S], slab[:, :hk]) and torch.equal(c.v2[:, :, :S], slab[:, hk:])
     # the oracle cache gives the same HF view
