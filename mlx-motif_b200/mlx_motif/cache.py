@@ -359,6 +359,8 @@ class MotifVanillaKVCache(MotifGroupedKVCache):
         B, h2, n, D = keys.shape
         hk = h2 // 2
         cap = max(n, self.max_size or 0)
+        if self.max_size is not None:  # preallocated: whole step blocks, as _grow allocates
+            cap = -(-cap // self.step) * self.step
         self.k1, self.k2, self.v1, self.v2 = (
             self._init_storage(B, hk, cap, D, keys.dtype, keys.device) for _ in range(4)
         )
