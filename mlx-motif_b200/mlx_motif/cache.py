@@ -4,7 +4,8 @@ API of ``src/mlx_motif/cache.py``: ``MotifGroupedKVCache`` (303-404) and
 ``MotifGroupedQuantizedKVCache`` (407-545) with ``update_and_fetch_4``,
 ``update_and_fetch_4_quantized``, ``offset``, ``step``, ``trim``,
 ``is_trimmable``, ``state`` / ``meta_state``, ``make_mask`` and
-``to_quantized``. Fetches return the FULL row-contiguous capacity buffers;
+``to_quantized``; ``MotifVanillaKVCache`` (85-175); and mlx-lm's stock
+``KVCache`` for a grouped model run without the 4-slot cache. Fetches return the FULL row-contiguous capacity buffers;
 consumers bound reads by ``offset`` (the attention kernels take it as
 ``kv_len``).
 
@@ -394,3 +395,122 @@ class MotifVanillaKVCache(MotifGroupedKVCache):
         c.state = state
         c.meta_state = meta_state
         return c
+
+
+# --------------------------------------------------------------------------- #
+# Stock single-slot cache (mlx-lm KVCache) for the grouped model without the 4-slot cache
+# --------------------------------------------------------------------------- #
+
+
+class KVCache:
+    """mlx-lm's stock ``KVCache`` contract: ``keys``/``values`` (B, n_kv_heads, capacity, D) in the
+    projection's head order, ``update_and_fetch(keys, values)`` returns the live rows, ``offset``,
+    ``step``-row growth, ``trim``, ``state``/``meta_state``.
+
+    The reference's ``make_cache`` hands a grouped model this cache when
+    ``MLX_MOTIF_4SLOT_CACHE=0`` (``model.py:983-989``); its attention then slices k1 = heads[0::2],
+    k2 = heads[1::2] (and v1/v2 alike) from the fetched buffers (``model.py:670-683``). Here the
+    kernels read those slices in place: with k_ratio 1 the even and odd heads are k1 and k2, so
+    ``slots_struct`` describes the buffers as four slots of n_kv_heads/2 heads and capacity
+    2·capacity whose rows [0, capacity) are exactly the sliced heads' rows (slot k2 starts one
+    head later). Appends, the decode step and the attention kernels then work unchanged, and
+    every read stays below ``offset``.
+    """
+
+    step = 256
+
+    def __init__(self, max_size: int | None = None):
+        self.keys = self.values = None
+        self.offset = 0
+        self.max_size = max_size
+
+    def is_trimmable(self):
+        return True
+
+    def trim(self, n):
+        n = min(self.offset, n)
+        self.offset -= n
+        return n
+
+    def make_mask(self, N, return_array: bool = False, window_size=None):
+        return create_attention_mask(N, offset=self.offset, return_array=return_array, window_size=window_size)
+
+    @staticmethod
+    def _alloc(B: int, H2: int, cap: int, D: int, dtype, device) -> torch.Tensor:
+        """Zeroed (B, H2, cap, D) storage followed by one spare head of padding: the odd-head slot
+        of ``slots_struct`` begins one head into the buffer, so its last head's view (capacity
+        2·cap) ends one head past the buffer; the padding keeps that span allocated."""
+        flat = torch.zeros(B * H2 * cap * D + cap * D, dtype=dtype, device=device)
+        return flat[: B * H2 * cap * D].view(B, H2, cap, D)
+
+    def _grow(self, B: int, H2: int, S: int, D: int, dtype, device) -> None:
+        prev = self.offset
+        if self.keys is not None and prev + S <= self.keys.shape[2]:
+            return
+        if self.max_size is not None:
+            cap = -(-self.max_size // self.step) * self.step
+            if self.keys is None and prev + S <= cap:
+                self.keys = self._alloc(B, H2, cap, D, dtype, device)
+                self.values = self._alloc(B, H2, cap, D, dtype, device)
+                return
+            raise ValueError(f"cache capacity {cap} exceeded (offset {prev} + {S} rows)")
+        new_len = ((self.step + S - 1) // self.step) * self.step
+        cap = new_len if self.keys is None else prev + new_len
+        keys = self._alloc(B, H2, cap, D, dtype, device)
+        values = self._alloc(B, H2, cap, D, dtype, device)
+        if self.keys is not None:
+            keys[..., :prev, :].copy_(self.keys[..., :prev, :])
+            values[..., :prev, :].copy_(self.values[..., :prev, :])
+        self.keys, self.values = keys, values
+
+    def slots_struct(self) -> motif_kv4_slots:
+        """The four-slot view of the kernels (valid until the next growth): k1 = even key heads,
+        k2 = odd key heads, v1 = even value heads, v2 = odd value heads."""
+        B, H2, cap, D = self.keys.shape
+        s = _slots_struct((self.keys, self.keys, self.values, self.values), 16, 64, B, H2 // 2, 2 * cap, D)
+        row_bytes = cap * D * self.keys.element_size()
+        s.data[1] = s.data[1] + row_bytes
+        s.data[3] = s.data[3] + row_bytes
+        return s
+
+    def update_and_fetch(self, keys, values):
+        """Append (B, n_kv_heads, S, D) keys/values at ``offset``; return the live rows."""
+        B, H2, S, D = keys.shape
+        if H2 % 2 or values.shape != keys.shape:
+            raise ValueError(f"KVCache: keys {tuple(keys.shape)} / values {tuple(values.shape)} need an even, "
+                             "equal head count")
+        prev = self.offset
+        self._grow(B, H2, S, D, keys.dtype, keys.device)
+        ins = [t.to(self.keys.dtype).contiguous() for t in (keys[:, 0::2], keys[:, 1::2], values[:, 0::2],
+                                                               values[:, 1::2])]
+        check(lib.motif_kv4_append(dtype_code(self.keys), self.slots_struct(), *(ptr(t) for t in ins), S, prev,
+                                   None, stream(keys.device)), "kv4_append")
+        self.offset += S
+        return self.keys[..., : self.offset, :], self.values[..., : self.offset, :]
+
+    @property
+    def state(self):
+        if self.keys is None:
+            return None, None
+        return self.keys[..., : self.offset, :], self.values[..., : self.offset, :]
+
+    @state.setter
+    def state(self, v):
+        keys, values = v
+        B, H2, n, D = keys.shape
+        cap = max(n, self.max_size or 0)
+        cap = -(-cap // self.step) * self.step
+        self.keys = self._alloc(B, H2, cap, D, keys.dtype, keys.device)
+        self.values = self._alloc(B, H2, cap, D, keys.dtype, keys.device)
+        self.keys[..., :n, :].copy_(keys)
+        self.values[..., :n, :].copy_(values)
+        self.offset = n
+
+    @property
+    def meta_state(self):
+        return ""
+
+    @meta_state.setter
+    def meta_state(self, v):
+        if v not in (None, ""):
+            raise ValueError(f"KVCache carries no meta state; got {v!r}")

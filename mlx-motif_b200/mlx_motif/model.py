@@ -28,7 +28,7 @@ from dataclasses import dataclass
 import torch
 
 from ._native import check, lib, motif_linear_io, ptr, stream
-from .cache import MotifGroupedKVCache, MotifGroupedQuantizedKVCache, MotifVanillaKVCache
+from .cache import KVCache, MotifGroupedKVCache, MotifGroupedQuantizedKVCache, MotifVanillaKVCache
 from .linear import QuantizedLinear
 from .quantization import quantize
 
@@ -176,6 +176,70 @@ def _resolve_attention_path(cache, S: int, kv_repeat: int, kr: int, fused_rope: 
     return AttnPath.FALLBACK
 
 
+def make_cache(args: ModelArgs, max_size: int | None = None, env=os.environ) -> list:
+    """One cache per layer, chosen by ``MLX_MOTIF_4SLOT_CACHE`` as ``Model.make_cache`` does
+    (``model.py:922-991``): unset or "1" -> ``MotifGroupedKVCache`` (4 fp16 slots), "q4"/"4" and
+    "q8"/"8" -> ``MotifGroupedQuantizedKVCache`` (group 64), "0"/""/"false"/"off" -> the stock
+    ``KVCache``; a vanilla model always gets ``MotifVanillaKVCache``. A grouped model with
+    k_ratio > 1 cannot use the 4-slot caches: an explicit request raises ``ValueError``, the
+    default quietly falls back to the stock cache. ``max_size`` preallocates (graph-safe)."""
+    raw = env.get("MLX_MOTIF_4SLOT_CACHE")
+    explicit = raw is not None
+    val = (raw if explicit else "1").lower()
+    use_4slot = val not in ("0", "", "false", "off")
+    if use_4slot and args.is_grouped and args.k_ratio != 1:
+        if explicit:
+            raise ValueError(
+                "MLX_MOTIF_4SLOT_CACHE is not supported with k_ratio > 1 "
+                f"(got k_ratio={args.k_ratio}): the 4-slot grouped KV cache allocates every slot with k1's "
+                "head count, which differs from k2/v1/v2 when k_ratio > 1. Unset MLX_MOTIF_4SLOT_CACHE for "
+                "this model configuration.")
+        use_4slot = False
+    caches = []
+    for _ in range(args.num_hidden_layers):
+        if not args.is_grouped:
+            caches.append(MotifVanillaKVCache(max_size=max_size))
+        elif not use_4slot:
+            caches.append(KVCache(max_size=max_size))
+        elif val in ("q4", "4"):
+            caches.append(MotifGroupedQuantizedKVCache(group_size=64, bits=4, max_size=max_size))
+        elif val in ("q8", "8"):
+            caches.append(MotifGroupedQuantizedKVCache(group_size=64, bits=8, max_size=max_size))
+        else:
+            caches.append(MotifGroupedKVCache(max_size=max_size))
+    return caches
+
+
+def decode_attention_mode(args: ModelArgs, cache, env=os.environ) -> tuple[AttnPath, str]:
+    """The grouped decode step's path (``_resolve_attention_path`` with S = 1) and the launches
+    that realise it: "fused" for QUANT_SDPA and for DUAL_V on fp16 rows (fp16 or stock cache),
+    "bridge" for DUAL_V or FALLBACK on a packed cache (its rows dequantized to fp16 first, as
+    ``update_and_fetch_4`` returns them, ``cache.py:448-465``), "two_call" for FALLBACK on fp16
+    rows. MOTIF_FUSED_ATTN=0 turns "fused" into "two_call" (for comparisons)."""
+    path = _resolve_attention_path(cache, 1, args.kv_repeat, args.k_ratio, args.fused_rope, env=env)
+    packed = isinstance(cache, MotifGroupedQuantizedKVCache)
+    if path is AttnPath.FALLBACK:
+        mode = "bridge" if packed else "two_call"
+    elif path is AttnPath.DUAL_V and packed:
+        mode = "bridge"
+    else:
+        mode = "fused"
+    if mode == "fused" and env.get("MOTIF_FUSED_ATTN", "1") == "0":
+        mode = "two_call"
+    return path, mode
+
+
+def cache_kind(cache) -> str:
+    """The decoder's name for a cache object: "fp16", "q4", "q8" or "stock"."""
+    if isinstance(cache, MotifGroupedQuantizedKVCache):
+        return f"q{cache.bits}"
+    if isinstance(cache, KVCache):
+        return "stock"
+    if isinstance(cache, MotifGroupedKVCache):
+        return "fp16"
+    raise TypeError(f"not a cache of this package: {type(cache).__name__}")
+
+
 # --------------------------------------------------------------------------- #
 # λ and the origin-first permutation
 # --------------------------------------------------------------------------- #
@@ -282,14 +346,28 @@ class MotifDecoder:
     run ``_forward_vanilla`` (``model.py:486-559``) on a ``MotifVanillaKVCache``
     (one GPU; its 4-slot form holds k1, k2 and the two V slabs).
 
-    ``cache``: "fp16" (4-slot fp16 rows) or "q4"/"q8" (packed 4-slot cache,
-    group 64). ``max_seq`` is the preallocated KV capacity. With a process
-    group ``tp_group`` the weights passed in must already be this rank's shard
-    (q groups and MLP columns); the engine all-reduces the o_proj and
-    down_proj outputs and the PolyNorm statistics.
+    ``cache``: "fp16" (4-slot fp16 rows), "q4"/"q8" (packed 4-slot cache, group 64),
+    "stock" (mlx-lm's single-slot ``KVCache``), or None to take the kind ``make_cache``
+    picks from ``MLX_MOTIF_4SLOT_CACHE`` (the reference's default: 4-slot fp16).
+    ``max_seq`` is the preallocated KV capacity (rounded up to whole 256-row steps).
+
+    The attention of each decode step follows ``_resolve_attention_path`` (``model.py:302-344``,
+    ``MLX_MOTIF_QUANT_SDPA`` / ``MLX_MOTIF_DUAL_V``), as ``_forward_grouped`` does at
+    ``model.py:608-614`` and ``716-768``:
+      * QUANT_SDPA (packed cache) and DUAL_V (fp16 or stock cache): the one-launch step
+        ``motif_gda_decode_step`` (RoPE, append, dual-V attention over the cache as stored,
+        gda_post_split);
+      * DUAL_V on a packed cache (``MLX_MOTIF_QUANT_SDPA=0``): the dequant bridge — RoPE + the
+        quantized append, the slots dequantized to fp16 rows (``update_and_fetch_4``'s bridge,
+        ``cache.py:448-465``), then the split-KV attention on those rows;
+      * FALLBACK (``MLX_MOTIF_DUAL_V=0``, or ``fused_rope``): separate launches — RoPE + append,
+        then the split-KV attention and merge (over the dequantized rows for a packed cache).
+    With a process group ``tp_group`` the weights passed in must already be this rank's shard
+    (q groups and MLP columns); the engine all-reduces the o_proj and down_proj outputs and the
+    PolyNorm statistics.
     """
 
-    def __init__(self, args: ModelArgs, weights: dict, cache: str = "fp16", max_seq: int = 4096,
+    def __init__(self, args: ModelArgs, weights: dict, cache: str | None = None, max_seq: int = 4096,
                  device="cuda", tp_group=None):
         self.vanilla = not args.is_grouped
         if self.vanilla:
@@ -320,6 +398,10 @@ class MotifDecoder:
         self.H = a.hidden_size
         self.V = a.vocab_size
         self.max_seq = max_seq
+        if cache is None:
+            cache = "fp16" if self.vanilla else cache_kind(make_cache(args, env=os.environ)[0])
+        if cache not in ("fp16", "q4", "q8", "stock") or (cache == "stock" and self.vanilla):
+            raise ValueError(f"cache must be fp16, q4, q8 (or stock for a grouped model); got {cache!r}")
         self.cache_kind = cache
         dev = self.device
 
@@ -359,14 +441,15 @@ class MotifDecoder:
         if cache == "fp16":
             kind = MotifVanillaKVCache if self.vanilla else MotifGroupedKVCache
             self.caches = [kind(max_size=max_seq) for _ in self.layers]
-        elif cache in ("q4", "q8"):
+        elif cache == "stock":
+            self.caches = [KVCache(max_size=max_seq) for _ in self.layers]
+        else:
             bits = 4 if cache == "q4" else 8
             self.caches = [MotifGroupedQuantizedKVCache(64, bits, max_size=max_seq) for _ in self.layers]
-        else:
-            raise ValueError(f"cache must be fp16, q4 or q8; got {cache!r}")
         for c in self.caches:
-            c._grow(1, self.kv_heads, 1, self.d, torch.float16, dev)
+            c._grow(1, (2 if cache == "stock" else 1) * self.kv_heads, 1, self.d, torch.float16, dev)
         self._slots = [c.slots_struct() for c in self.caches]
+        self._resolve_attn_mode()
 
         f16 = torch.float16
         H, d = self.H, self.d
@@ -405,13 +488,18 @@ class MotifDecoder:
         if self.inter % 16:
             raise ValueError("intermediate size per rank must be a multiple of 16")
         self.lin_ws = torch.zeros(max(lin_ws, 16), dtype=torch.uint8, device=dev)
-        # MOTIF_FUSED_ATTN=0 runs RoPE/append and the attention as two calls (for comparisons).
-        self.fused_attn = self.vanilla or os.environ.get("MOTIF_FUSED_ATTN", "1") != "0"
         if self.fused_attn:
             self.attn_ws_bytes = lib.motif_gda_decode_step_workspace_bytes(self.q_heads, d, 64)
         else:
             self.attn_ws_bytes = lib.motif_gda_decode_attention_workspace_bytes(self.q_heads, d, 64)
         self.attn_ws = torch.zeros(self.attn_ws_bytes, dtype=torch.uint8, device=dev)
+        self._bridge = None
+        if self.attn_mode == "bridge":  # fp16 rows of the dequant bridge, shared by the layers in turn
+            from .cache import _slots_struct
+
+            cap = self._slots[0].capacity
+            self._bridge = [torch.zeros((1, self.kv_heads, cap, d), dtype=f16, device=dev) for _ in range(4)]
+            self._bridge_slots = _slots_struct(self._bridge, 16, 64, 1, self.kv_heads, cap, d)
         self.argmax_ws_bytes = lib.motif_argmax_workspace_bytes(self.V_local)
         self.argmax_ws = torch.zeros(self.argmax_ws_bytes, dtype=torch.uint8, device=dev)
         self.offset = 0  # host mirror of pos_len[0]
@@ -434,6 +522,22 @@ class MotifDecoder:
             self._setup_exchange()
 
     # ------------------------------------------------------------------ #
+    def _resolve_attn_mode(self) -> None:
+        """The decode step's attention launches: "fused" (one launch), "two_call" (RoPE + append,
+        then the split-KV attention and merge) or "bridge" (two_call over fp16 rows dequantized
+        from a packed cache), from ``_resolve_attention_path`` (vanilla models: "fused").
+        MOTIF_FUSED_ATTN=0 turns "fused" into "two_call" (for comparisons)."""
+        self.attn_path, mode = (None, "fused") if self.vanilla else decode_attention_mode(self.args, self.caches[0])
+        self.attn_mode = mode
+        self.fused_attn = mode == "fused"
+        # kernels per layer: one step / RoPE+append, split attention, merge / + four dequantizes
+        self.attn_launches = {"fused": 1, "two_call": 3, "bridge": 7}[mode]
+
+    def make_cache(self) -> list:
+        """Fresh caches for this decoder's model as the environment asks (``Model.make_cache``,
+        ``model.py:922-991``), preallocated to this decoder's capacity."""
+        return make_cache(self.args, max_size=self.max_seq, env=os.environ)
+
     def _check_shapes(self) -> None:
         L0 = self.layers[0]
         d = self.d
@@ -470,7 +574,8 @@ class MotifDecoder:
     def kv_bytes_per_token(self, kv_len: int) -> int:
         """KV-cache bytes the attention reads at one step (4 slots, all layers)."""
         d = self.d
-        per_row = 2 * d if self.cache_kind == "fp16" else (d * (4 if self.cache_kind == "q4" else 8) // 8 + 4 * d // 64)
+        per_row = 2 * d if self.cache_kind in ("fp16", "stock") else \
+            (d * (4 if self.cache_kind == "q4" else 8) // 8 + 4 * d // 64)
         return len(self.layers) * 4 * self.kv_heads * kv_len * per_row
 
     # ------------------------------------------------------------------ #
@@ -654,7 +759,10 @@ class MotifDecoder:
             else:
                 check(lib.motif_rope_qkv_append(ptr(self.qkv), ptr(self.inv_freq), self.q_heads, self._slots[li],
                                                 pos_p, ptr(self.q), st), "rope_qkv_append")
-                check(lib.motif_gda_decode_attention(ptr(self.q), self._slots[li], self.scale, self.q_groups, self.gr,
+                slots = self._slots[li]
+                if self.attn_mode == "bridge":
+                    slots = self._dequant_bridge(li, st)
+                check(lib.motif_gda_decode_attention(ptr(self.q), slots, self.scale, self.q_groups, self.gr,
                                                      0, kvl_p, ptr(L["subln"]), ptr(L["lambda_full"]),
                                                      L["lambda_full"].numel(), L["lambda_init"],
                                                      self.args.attn_rms_norm_eps, ptr(self.attn), ptr(self.attn_ws),
@@ -671,6 +779,18 @@ class MotifDecoder:
             if not self.tp_exchange:
                 self._allreduce(self.dn)
         self._head(with_head, head_io, st)
+
+    def _dequant_bridge(self, li: int, st: int):
+        """Layer li's packed slots dequantized to fp16 rows in the shared bridge buffers (every
+        capacity row, so the launch does not depend on the length; rows past the length are
+        zeros and never read) — the fetch of ``update_and_fetch_4`` on a quantized cache."""
+        c = self.caches[li]
+        rows = self.kv_heads * self._slots[li].capacity
+        for i, slot in enumerate((c.k1, c.k2, c.v1, c.v2)):
+            data, scales, biases = slot
+            check(lib.motif_dequantize(0, c.bits, c.group_size, ptr(data), ptr(scales), ptr(biases), rows, self.d,
+                                       ptr(self._bridge[i]), st), "dequantize")
+        return self._bridge_slots
 
     def _head(self, with_head: bool, head_io, st: int) -> None:
         """lm_head + greedy token + position advance (one launch when the argmax is fused)."""
@@ -828,7 +948,7 @@ class MotifDecoder:
         """The fp16 4-slot view the prompt attention reads: the cache itself, or (q4/q8 cache) its
         rows [0, rows) dequantized into a scratch fp16 cache — the reference's prompt path also
         attends over the dequantized fetch (cache.py:448-465)."""
-        if self.cache_kind == "fp16":
+        if self.cache_kind in ("fp16", "stock"):
             return self._slots[li]
         from .cache import _slots_struct
 
@@ -1054,6 +1174,11 @@ class MotifDecoder:
         gen = torch.Generator(device=self.device)
         gen.manual_seed(seed)
         for c in self.caches:
+            if self.cache_kind == "stock":
+                for buf in (c.keys, c.values):
+                    buf[:, :, :n].copy_((torch.randn((1, 2 * self.kv_heads, n, self.d), generator=gen,
+                                                     device=self.device) * std).half())
+                continue
             for slot_name in ("k1", "k2", "v1", "v2"):
                 rows = torch.randn((1, self.kv_heads, n, self.d), generator=gen, device=self.device) * std
                 rows = rows.half()

@@ -97,7 +97,7 @@ def _rows_worker(rank, world, port, q):
         dev = f"cuda:{rank}"
         m = MotifDecoder.random(_args(), seed=5, std=0.05, max_seq=256, device=dev, tp_group=dist.group.WORLD,
                                 rank=rank, world=world)
-        m.prefill(ROW_PROMPT)  # a 169-row block: GEMMs (TP2) or the multi-row GEMV (TP4), all-reduced
+        m.prefill(ROW_PROMPT)  # a 169-row block: GEMMs (TP2) or the multi-row GEMV (TP4, TP8), all-reduced
         first = int(m.token.item())
         rows = m.forward_rows(VERIFY_IDS).float().cpu().numpy()
         draft = MotifDecoder.random(_draft_args(), seed=12, std=0.05, max_seq=256, device=dev)
@@ -112,7 +112,7 @@ def _rows_worker(rank, world, port, q):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world", [2, 4])
+@pytest.mark.parametrize("world", [2, 4, 8])
 def test_tp_row_blocks_and_speculative_verify(world):
     """Prompt ingestion in row blocks and the [1, K+1] verify under tensor parallelism (NCCL
     all-reduce of the row-parallel outputs and of the PolyNorm statistics, the lm_head shards

@@ -57,6 +57,61 @@ def test_resolve_attention_path_truth_table():
     assert R(None, 1, 1, 1, False, env={}) is AttnPath.DUAL_V
 
 
+def test_make_cache_env_routing():
+    """MLX_MOTIF_4SLOT_CACHE picks the cache as the reference's Model.make_cache does
+    (model.py:922-991): 4-slot fp16 by default, q4/q8 packed, the stock cache when off; a vanilla
+    model always gets the slab-ordered cache; k_ratio > 1 raises on an explicit request and quietly
+    takes the stock cache otherwise."""
+    from mlx_motif.cache import KVCache, MotifGroupedKVCache, MotifGroupedQuantizedKVCache, MotifVanillaKVCache
+    from mlx_motif.model import ModelArgs, cache_kind, make_cache
+
+    g = ModelArgs(num_hidden_layers=3)
+    cases = {None: (MotifGroupedKVCache, "fp16"), "1": (MotifGroupedKVCache, "fp16"),
+             "true": (MotifGroupedKVCache, "fp16"), "q4": (MotifGroupedQuantizedKVCache, "q4"),
+             "4": (MotifGroupedQuantizedKVCache, "q4"), "Q8": (MotifGroupedQuantizedKVCache, "q8"),
+             "8": (MotifGroupedQuantizedKVCache, "q8"), "0": (KVCache, "stock"), "": (KVCache, "stock"),
+             "false": (KVCache, "stock"), "OFF": (KVCache, "stock")}
+    for val, (cls, kind) in cases.items():
+        env = {} if val is None else {"MLX_MOTIF_4SLOT_CACHE": val}
+        caches = make_cache(g, env=env)
+        assert len(caches) == 3 and all(type(c) is cls for c in caches), val
+        assert cache_kind(caches[0]) == kind
+        if kind in ("q4", "q8"):
+            assert caches[0].group_size == 64 and caches[0].bits == int(kind[1])
+    v = ModelArgs(hidden_size=2048, num_hidden_layers=2, intermediate_size=8192, num_attention_heads=16,
+                  num_key_value_heads=4, num_noise_heads=None)
+    for val in (None, "q4", "0"):
+        env = {} if val is None else {"MLX_MOTIF_4SLOT_CACHE": val}
+        assert all(type(c) is MotifVanillaKVCache for c in make_cache(v, env=env))
+    kr2 = ModelArgs(num_attention_heads=40, num_key_value_heads=24, num_noise_heads=8, k_ratio=2)
+    assert all(type(c) is KVCache for c in make_cache(kr2, env={}))
+    for val in ("1", "q4", "q8"):
+        with pytest.raises(ValueError, match="not supported with k_ratio > 1"):
+            make_cache(kr2, env={"MLX_MOTIF_4SLOT_CACHE": val})
+    assert all(type(c) is KVCache for c in make_cache(kr2, env={"MLX_MOTIF_4SLOT_CACHE": "0"}))
+
+
+def test_decode_attention_mode_follows_the_resolved_path():
+    """The decoder's attention launches per resolved path: one fused launch for QUANT_SDPA and
+    for DUAL_V on fp16 rows; the dequant bridge for DUAL_V/FALLBACK on a packed cache; RoPE/append
+    + split attention for FALLBACK on fp16 rows."""
+    from mlx_motif.cache import KVCache, MotifGroupedKVCache, MotifGroupedQuantizedKVCache
+    from mlx_motif.model import AttnPath, ModelArgs, decode_attention_mode
+
+    a = ModelArgs(num_hidden_layers=1)
+    q, f, s = MotifGroupedQuantizedKVCache(64, 4), MotifGroupedKVCache(), KVCache()
+    M = decode_attention_mode
+    assert M(a, q, env={}) == (AttnPath.QUANT_SDPA, "fused")
+    assert M(a, q, env={"MLX_MOTIF_QUANT_SDPA": "0"}) == (AttnPath.DUAL_V, "bridge")
+    assert M(a, q, env={"MLX_MOTIF_QUANT_SDPA": "0", "MLX_MOTIF_DUAL_V": "0"}) == (AttnPath.FALLBACK, "bridge")
+    assert M(a, q, env={"MLX_MOTIF_DUAL_V": "0"}) == (AttnPath.QUANT_SDPA, "fused")
+    for c in (f, s):
+        assert M(a, c, env={}) == (AttnPath.DUAL_V, "fused")
+        assert M(a, c, env={"MLX_MOTIF_DUAL_V": "False"}) == (AttnPath.FALLBACK, "two_call")
+        assert M(a, c, env={"MOTIF_FUSED_ATTN": "0"}) == (AttnPath.DUAL_V, "two_call")
+    assert M(ModelArgs(num_hidden_layers=1, fused_rope=True), f, env={}) == (AttnPath.FALLBACK, "two_call")
+
+
 def test_lambda_helpers_match_oracle():
     from mlx_motif.model import lambda_full, lambda_init_for_layer, origin_first_perm
 
