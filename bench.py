@@ -310,8 +310,9 @@ def _graph_time(fn, reps: int = 5) -> float:
 
 
 def time_gemvs(model) -> dict:
-    """CUDA-event time of one step's GEMV launches (every layer's qkv, o, gate|up, down + lm_head),
-    replayed from a CUDA graph so host launch cost is excluded."""
+    """CUDA-event time of one step's q4 GEMV launches (every layer's qkv, o, gate|up, down + lm_head),
+    replayed from a CUDA graph so host launch cost is excluded. Bytes: every linear's packed
+    weights, scales and biases plus its x and y vectors."""
     import torch
 
     lins = [(L[k], inp) for L in model.layers for k, inp in
@@ -327,7 +328,8 @@ def time_gemvs(model) -> dict:
     best = _graph_time(run)
     n = len(lins)
     return {"launches": n, "ms_total": best, "ms_per_launch": best / n, "bytes_total": alg,
-            "bytes_per_launch": alg / n, "gbs": alg / (best / 1e3) / 1e9}
+            "bytes_per_launch": alg / n, "gbs": alg / (best / 1e3) / 1e9,
+            "kernel": "q4_gemv_tma_kernel (motif_quantized_linear, one launch per linear)"}
 
 
 def time_attention(model) -> dict:
@@ -466,7 +468,7 @@ def run_b200(a) -> None:
     gem = time_gemvs(model)
     peak, peak_kind = peaks()
     traffic = read_traffic()
-    roofline = {"bound": "hbm", "kernel": "motif_quantized_linear (q4 GEMV, all 193 launches of a step)",
+    roofline = {"bound": "hbm", "kernel": gem["kernel"] + f", all {gem['launches']} launches of a step",
                 "achieved": round(gem["gbs"], 1), "peak": peak, "peak_kind": peak_kind, "unit": "GB/s",
                 "frac": round(gem["gbs"] / peak, 4), "traffic": traffic,
                 "bytes_per_launch": round(gem["bytes_per_launch"]), "ms_per_launch": round(gem["ms_per_launch"], 5)}

@@ -413,7 +413,9 @@ MOTIF_API int motif_prefill_post(const void* o, int64_t seq, int64_t q_heads, in
  * hold per-tile counters at a fixed place, so one workspace sized for the
  * largest shape serves GEMVs of every shape in turn; launched with programmatic
  * stream serialization, it starts streaming weights while the previous kernel
- * finishes. */
+ * finishes. Before it waits for that kernel it also reads the weights and the
+ * prologue's constants (norm_w, poly_w, poly_b), so the previous kernel in the
+ * stream must not write those. */
 typedef struct motif_linear_io {
   int32_t mode;
   const void* x;

@@ -438,9 +438,36 @@ struct StageWords {
 
 // `after_issue` runs on every thread once the input loads are in flight (the TMA
 // kernel issues the rest of its weight prefetch there, behind the staging loads).
+// A prologue's constant inputs — the RMSNorm weight words a thread stages (mode 1) and the
+// PolyNorm weights and bias (mode 2) — read before the kernel waits for the previous one: they
+// are model weights that no kernel of the step writes, and reading them after the wait put a
+// DRAM miss on the staging's critical path.
+template <int MODE>
+struct StageConst {
+  uint4 norm[StageWords<MODE>::value];
+  float poly[4];
+};
+
+template <int MODE>
+__device__ __forceinline__ void stage_const_load(const LinArgs& a, StageConst<MODE>& c) {
+  if constexpr (MODE == kModeAddRms) {
+    const int words = (int)(a.K / 8);
+#pragma unroll
+    for (int i = 0; i < StageWords<MODE>::value; ++i) {
+      const int wi = threadIdx.x + i * blockDim.x;
+      if (wi < words) c.norm[i] = *reinterpret_cast<const uint4*>(a.norm_w + (int64_t)wi * 8);
+    }
+  } else if constexpr (MODE == kModePoly) {
+    c.poly[0] = __half2float(a.poly_w[0]);
+    c.poly[1] = __half2float(a.poly_w[1]);
+    c.poly[2] = __half2float(a.poly_w[2]);
+    c.poly[3] = __half2float(a.poly_b[0]);
+  }
+}
+
 template <int MODE, bool V2, typename AfterIssue>
 __device__ void stage_x(const LinArgs& a, __half* xp_s, float* xsum_s, float* corr_s, float* red, __half* delta_s,
-                        AfterIssue&& after_issue) {
+                        AfterIssue&& after_issue, const StageConst<MODE>* pre = nullptr) {
   constexpr int kMaxStageWords = StageWords<MODE>::value;
   const int64_t K = a.K;
   const int words = (int)(K / 8);
@@ -488,7 +515,7 @@ __device__ void stage_x(const LinArgs& a, __half* xp_s, float* xsum_s, float* co
       } else if constexpr (MODE == kModeAddRms) {
         in0[i] = *reinterpret_cast<const uint4*>(hsrc + (int64_t)wi * 8);
         in1[i] = delta ? *reinterpret_cast<const uint4*>(delta + (int64_t)wi * 8) : make_uint4(0, 0, 0, 0);
-        in2[i] = *reinterpret_cast<const uint4*>(a.norm_w + (int64_t)wi * 8);
+        in2[i] = pre ? pre->norm[i] : *reinterpret_cast<const uint4*>(a.norm_w + (int64_t)wi * 8);
       } else {
         in0[i] = *reinterpret_cast<const uint4*>(a.gate + (int64_t)wi * 8);
         in1[i] = *reinterpret_cast<const uint4*>(a.up + (int64_t)wi * 8);
@@ -535,10 +562,10 @@ __device__ void stage_x(const LinArgs& a, __half* xp_s, float* xsum_s, float* co
     r2 = rsqrtf(stats_acc[0] * a.poly_inv_dim + a.poly_eps);
     r4 = rsqrtf(stats_acc[1] * a.poly_inv_dim + a.poly_eps);
     r6 = rsqrtf(stats_acc[2] * a.poly_inv_dim + a.poly_eps);
-    pw0 = __half2float(a.poly_w[0]);
-    pw1 = __half2float(a.poly_w[1]);
-    pw2 = __half2float(a.poly_w[2]);
-    pb = __half2float(a.poly_b[0]);
+    pw0 = pre ? pre->poly[0] : __half2float(a.poly_w[0]);
+    pw1 = pre ? pre->poly[1] : __half2float(a.poly_w[1]);
+    pw2 = pre ? pre->poly[2] : __half2float(a.poly_w[2]);
+    pb = pre ? pre->poly[3] : __half2float(a.poly_b[0]);
   }
   const bool write_h = MODE == kModeAddRms && a.h_out && blockIdx.x == 0;
   // ---- build x, permute, group sums ----
@@ -732,19 +759,31 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
   return false;
 }
 
-__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int x, int y, uint32_t bar) {
+// A 2D tiled TMA load with an L2 eviction-priority policy (createpolicy): the weight stream is read once
+// per step, so its lines are marked first to be evicted and the small vectors the kernels read
+// and write between launches (activations, norm weights, statistics, counters) stay in L2.
+__device__ __forceinline__ void tma_load_2d_stream(uint32_t dst, const CUtensorMap* map, int x, int y, uint32_t bar,
+                                                   uint64_t policy) {
   asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];\n" ::"r"(dst),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar)
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint "
+      "[%0], [%1, {%2, %3}], [%4], %5;\n" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar), "l"(policy)
       : "memory");
 }
 
+__device__ __forceinline__ uint64_t evict_first_policy() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;\n" : "=l"(p));
+  return p;
+}
+
 __device__ __forceinline__ void issue_unit(const LinArgs& a, int tile, int blk, uint32_t slot, uint32_t bar) {
+  const uint64_t pol = evict_first_policy();
   mbar_expect_tx(bar, 4096 + 256 + 256);
-  tma_load_2d(slot, &a.tm_w, blk * 256, tile * kTileRows, bar);
-  tma_load_2d(slot + 2048, &a.tm_w, blk * 256 + 128, tile * kTileRows, bar);
-  tma_load_2d(slot + 4096, &a.tm_s, blk * 16, tile * kTileRows, bar);
-  tma_load_2d(slot + 4352, &a.tm_b, blk * 16, tile * kTileRows, bar);
+  tma_load_2d_stream(slot, &a.tm_w, blk * 256, tile * kTileRows, bar, pol);
+  tma_load_2d_stream(slot + 2048, &a.tm_w, blk * 256 + 128, tile * kTileRows, bar, pol);
+  tma_load_2d_stream(slot + 4096, &a.tm_s, blk * 16, tile * kTileRows, bar, pol);
+  tma_load_2d_stream(slot + 4352, &a.tm_b, blk * 16, tile * kTileRows, bar, pol);
 }
 
 __device__ __forceinline__ uint2 lds64(const unsigned char* p) { return *reinterpret_cast<const uint2*>(p); }
@@ -864,23 +903,31 @@ __global__ void __launch_bounds__(kTmaThreads, kTmaMinBlocks) q4_gemv_tma_kernel
   // (tile, blk) of the next unit to fetch. Weights do not depend on the previous
   // kernel: the first slot is filled before waiting for it, the others right after
   // the x inputs are requested, so the staging loads queue behind one unit per warp
-  // instead of the whole ring.
+  // instead of the whole ring. A plain-x linear (mode 0: the o projection after the
+  // attention step) fills the whole ring before waiting: its staging is one L2-resident
+  // vector, and its CTAs start on the SMs the attention step leaves free, so most of
+  // its weights arrive while the attention still runs.
+  constexpr int kPreSlots = MODE == kModeX ? kStages : 1;
   int it = u0 / nblk, ib = u0 - (u0 / nblk) * nblk;
-  if (lane == 0 && u0 < u1) {
-    issue_unit(a, it, ib, smem_u32(my_ring), smem_u32(&my_bars[0]));
-    if (++ib == nblk) { ib = 0; ++it; }
+  if (lane == 0) {
+    for (int i = 0; i < kPreSlots && u0 + i < u1; ++i) {
+      issue_unit(a, it, ib, smem_u32(my_ring + i * kSlotBytes), smem_u32(&my_bars[i]));
+      if (++ib == nblk) { ib = 0; ++it; }
+    }
   }
+  StageConst<MODE> cst;
+  stage_const_load<MODE>(a, cst);
   for (int i = threadIdx.x; i < kZeroBytes / 16; i += blockDim.x) reinterpret_cast<uint4*>(zero_s)[i] = make_uint4(0, 0, 0, 0);
   grid_dep_wait();
   grid_dep_launch();
   stage_x<MODE, true>(a, xp_s, xsum_s, corr_s, red, delta_s, [&] {
     if (lane == 0) {
-      for (int i = 1; i < kStages && u0 + i < u1; ++i) {
+      for (int i = kPreSlots; i < kStages && u0 + i < u1; ++i) {
         issue_unit(a, it, ib, smem_u32(my_ring + i * kSlotBytes), smem_u32(&my_bars[i]));
         if (++ib == nblk) { ib = 0; ++it; }
       }
     }
-  });
+  }, &cst);
   // Per-lane operand addresses (see compute_unit_tma).
   const uint32_t o0 = r * 128 + (((2 * c) ^ r) * 16), o1 = r * 128 + (((2 * c + 1) ^ r) * 16);
   const bool diag = r == c;
