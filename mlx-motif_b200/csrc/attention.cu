@@ -432,6 +432,105 @@ __global__ void gda_combine_kernel(const float* __restrict__ ws, int nsplit, int
   gda_merge_group<D, GR>(ws, nsplit, n_active, blockIdx.x, q_origin, subln_w, lam, lam_mode, out_scale, eps, out);
 }
 
+// ---- split partials merged through distributed shared memory ---------------------------------
+//
+// For short caches the splits of one group run as ONE thread-block cluster (grid.x = nsplit =
+// cluster size). Each CTA stores its split's partial (m, l, o1|o2 per head) straight into the
+// shared memory of the cluster's rank-0 CTA, arrives on the cluster barrier and exits — its SM
+// is free for the next kernel at once; rank 0 waits on the barrier and merges the partials from
+// its own shared memory: no global partials, fence, arrival counter or second pass through L2.
+// The merge arithmetic and its summation order are gda_merge_group's, so both paths give the
+// same bits. The cluster barrier is a hardware barrier over co-scheduled CTAs: no spinning.
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;\n" : "=r"(r));
+  return r;
+}
+
+__device__ __forceinline__ void cluster_arrive_release() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n" ::: "memory");
+}
+
+__device__ __forceinline__ void cluster_wait_acquire() {
+  asm volatile("barrier.cluster.wait.acquire.aligned;\n" ::: "memory");
+}
+
+// Store to the shared-memory word at `p` (an address in this CTA's layout) of cluster rank `rank`.
+__device__ __forceinline__ void st_dsmem(float* p, uint32_t rank, float v) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;\n"
+               : "=r"(r)
+               : "r"((uint32_t)__cvta_generic_to_shared(p)), "r"(rank));
+  asm volatile("st.shared::cluster.f32 [%0], %1;\n" ::"r"(r), "f"(v) : "memory");
+}
+
+// gda_merge_group with the partials in this CTA's shared memory: all[s][h][2D + 2] holds split s
+// (heads: GR origin heads, then the noise head).
+template <int D, int GR>
+__device__ __forceinline__ void gda_merge_group_smem(const float* all, int n_active, int g,
+                                                     const __half* __restrict__ subln_w,
+                                                     const float* __restrict__ lam, int lam_mode, float out_scale,
+                                                     float eps, __half* __restrict__ out) {
+  __shared__ float scratch[32 * GR];
+  __shared__ float f_s[GR + 1][kMaxSplits];
+  __shared__ float L_s[GR + 1];
+  const bool act = threadIdx.x < 2 * D;
+  const int ch = act ? threadIdx.x : 0;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  constexpr int stride = 2 * D + 2, split_stride = (GR + 1) * stride;
+  if (warp <= GR) {  // split_weights over the splits held here (at most 32 of them)
+    const float* base = all + warp * stride;
+    const float m0 = lane < n_active ? base[lane * split_stride] : -INFINITY;
+    const float m1 = -INFINITY;
+    const float l0 = lane < n_active ? base[lane * split_stride + 1] : 0.f;
+    const float l1 = 0.f;
+    const float M = warp_max(fmaxf(m0, m1));
+    const float f0 = (M != -INFINITY && m0 != -INFINITY) ? exp2f(m0 - M) : 0.f;
+    const float f1 = 0.f;
+    const float L = warp_sum(l0 * f0 + l1 * f1);
+    f_s[warp][lane] = f0;
+    f_s[warp][lane + 32] = f1;
+    if (lane == 0) L_s[warp] = L;
+  }
+  __syncthreads();
+  float acc[GR + 1];
+#pragma unroll
+  for (int j = 0; j <= GR; ++j) acc[j] = 0.f;
+  int s = 0;
+  for (; s + 2 <= n_active; s += 2) {
+    float a0[GR + 1], a1[GR + 1];
+#pragma unroll
+    for (int j = 0; j <= GR; ++j) {
+      a0[j] = all[s * split_stride + j * stride + 2 + ch];
+      a1[j] = all[(s + 1) * split_stride + j * stride + 2 + ch];
+    }
+#pragma unroll
+    for (int j = 0; j <= GR; ++j) acc[j] += f_s[j][s] * a0[j] + f_s[j][s + 1] * a1[j];
+  }
+  if (s < n_active) {
+#pragma unroll
+    for (int j = 0; j <= GR; ++j) acc[j] += f_s[j][s] * all[s * split_stride + j * stride + 2 + ch];
+  }
+  float val[GR + 1];
+#pragma unroll
+  for (int j = 0; j <= GR; ++j) val[j] = round_through<__half>(L_s[j] > 0.f ? acc[j] / L_s[j] : 0.f);
+  float d[GR], ssq[GR];
+#pragma unroll
+  for (int j = 0; j < GR; ++j) {
+    const int h_o = g * GR + j;
+    const float l = lam[lam_mode == 0 ? 0 : (lam_mode == 1 ? g : h_o)];
+    d[j] = val[j] - l * val[GR];
+    ssq[j] = act ? d[j] * d[j] : 0.f;
+  }
+  block_sum<GR>(ssq, scratch);
+  const float w = __half2float(subln_w[ch]);
+#pragma unroll
+  for (int j = 0; j < GR; ++j) {
+    const float inv = rsqrtf(ssq[j] / (float)(2 * D) + eps);
+    if (act) out[(int64_t)(g * GR + j) * 2 * D + ch] = __float2half_rn(d[j] * inv * w * out_scale);
+  }
+}
+
 // ---- fused decode step: RoPE + 4-slot append + split-KV dual-V attention + GDA merge ----
 //
 // One launch per layer replaces rope_qkv_append, attn_split and gda_combine. Grid
@@ -472,7 +571,7 @@ __device__ __forceinline__ int fused_head(int g, int h, int q_origin) {
   return h < NA ? g * NA + h : q_origin + g;
 }
 
-template <int BITS, int NA, int NB, bool PAIRED, int PPW, int LPG>
+template <int BITS, int NA, int NB, bool PAIRED, int PPW, int LPG, bool CLUSTER>
 __global__ void __launch_bounds__(kAttnThreads) gda_fused_kernel(FusedArgs f) {
   constexpr int D = 128, CPL = D / 32, NH = NA + NB, half = D / 2;
   constexpr int kPosPerWarp = PPW, kRoundPositions = kAttnWarps * PPW;
@@ -488,7 +587,10 @@ __global__ void __launch_bounds__(kAttnThreads) gda_fused_kernel(FusedArgs f) {
   int p0, p1, n_active;
   split_range(kv_len, nsplit, split, p0, p1, n_active);
   if (n_active < 1) n_active = 1;  // kv_len 0: split 0 still merges (to zeros)
-  if (split >= n_active) return;
+  // A split past the last active one has no rows. On the global path it leaves at once; in a
+  // cluster it stays (every CTA takes part in the cluster barriers) with an empty range.
+  if (!CLUSTER && split >= n_active) return;
+  if (CLUSTER && split >= n_active) p0 = p1 = kv_len;
   const motif_kv4_slots& kv = f.cache;
   const int64_t row0 = (int64_t)g * cap;
   float ka[kPosPerWarp][CPL], kb[kPosPerWarp][CPL], x1[kPosPerWarp][CPL], x2[kPosPerWarp][CPL];
@@ -625,6 +727,7 @@ __global__ void __launch_bounds__(kAttnThreads) gda_fused_kernel(FusedArgs f) {
   extern __shared__ float smem[];
   float* sm_ml = smem;                       // [warp][h][2]
   float* sm_o = smem + kAttnWarps * NH * 2;  // [warp][h][2D]
+  float* part_s = sm_o + kAttnWarps * NH * 2 * D;  // cluster path, rank 0: [split][h][2D + 2]
 #pragma unroll
   for (int h = 0; h < NH; ++h) {
     if (lane == 0) {
@@ -656,13 +759,30 @@ __global__ void __launch_bounds__(kAttnThreads) gda_fused_kernel(FusedArgs f) {
         O += sm_o[(int64_t)(w * NH + h) * 2 * D + ch] * fw;
       }
     }
-    const int hh = fused_head<NA, NB, PAIRED>(g, h, f.q_origin);
-    float* p = f.ws + ((int64_t)hh * nsplit + split) * (2 * D + 2);
-    p[2 + ch] = O;
-    if (ch == 0) {
-      p[0] = M;
-      p[1] = L;
+    if constexpr (CLUSTER) {  // into rank 0's shared memory, slot `split`
+      float* p = part_s + ((int64_t)split * NH + h) * (2 * D + 2);
+      st_dsmem(p + 2 + ch, 0, O);
+      if (ch == 0) {
+        st_dsmem(p, 0, M);
+        st_dsmem(p + 1, 0, L);
+      }
+    } else {
+      const int hh = fused_head<NA, NB, PAIRED>(g, h, f.q_origin);
+      float* p = f.ws + ((int64_t)hh * nsplit + split) * (2 * D + 2);
+      p[2 + ch] = O;
+      if (ch == 0) {
+        p[0] = M;
+        p[1] = L;
+      }
     }
+  }
+  if constexpr (CLUSTER) {
+    static_assert(!PAIRED && NB == 1, "the cluster merge is built for the GDA head layout");
+    cluster_arrive_release();  // this split's partial is in rank 0's shared memory
+    if (cluster_rank() != 0) return;
+    cluster_wait_acquire();  // every split's partial has arrived
+    gda_merge_group_smem<D, NA>(part_s, n_active, g, f.subln_w, f.lam, f.lam_mode, f.out_scale, f.eps, f.out);
+    return;
   }
 
   // ---- the last CTA of the group merges ----
@@ -1451,13 +1571,23 @@ int motif_gda_decode_attention(const void* q, const motif_kv4_slots* cache, floa
 namespace motif {
 namespace {
 
-template <int NA, int NB, bool PAIRED, int PPW, int BITS, int LPG>
+constexpr int kMaxClusterSplitsForSmem = 16;
+
+// Dynamic shared memory of gda_fused_kernel: the per-warp softmax states, and on the cluster
+// path rank 0's slots for every split's partial.
+size_t fused_smem_bytes(int heads, bool cluster) {
+  return sizeof(float) * ((size_t)kAttnWarps * heads * (2 + 2 * 128) +
+                          (cluster ? (size_t)kMaxClusterSplitsForSmem * heads * (2 + 2 * 128) : 0));
+}
+
+template <int NA, int NB, bool PAIRED, int PPW, int BITS, int LPG, bool CLUSTER>
 cudaError_t launch_fused_one(const FusedArgs& f, dim3 grid, cudaStream_t st) {
-  auto kern = gda_fused_kernel<BITS, NA, NB, PAIRED, PPW, LPG>;
-  const size_t smem = sizeof(float) * (size_t)kAttnWarps * (NA + NB) * (2 + 2 * 128);
+  auto kern = gda_fused_kernel<BITS, NA, NB, PAIRED, PPW, LPG, CLUSTER>;
+  const size_t smem = fused_smem_bytes(NA + NB, CLUSTER);
   static bool configured = false;  // one attribute call per instantiation
   if (!configured) {
-    const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e == cudaSuccess && CLUSTER) e = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
     if (e != cudaSuccess) return e;
     configured = true;
   }
@@ -1466,24 +1596,83 @@ cudaError_t launch_fused_one(const FusedArgs& f, dim3 grid, cudaStream_t st) {
   cfg.blockDim = dim3(kAttnThreads);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = grid.x;  // the group's splits form one cluster
+  attr[1].val.clusterDim.y = 1;
+  attr[1].val.clusterDim.z = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = CLUSTER ? 2 : 1;
   return cudaLaunchKernelEx(&cfg, kern, f);
 }
 
+// Largest cluster (splits of one group) the cluster merge takes: 16 CTAs, a non-portable size
+// that B200 schedules; MOTIF_ATTN_CLUSTER=0 turns the cluster merge off.
+constexpr int kMaxClusterSplits = kMaxClusterSplitsForSmem;
+
+bool cluster_merge_enabled() {
+  static int on = -1;
+  if (on < 0) {
+    const char* v = getenv("MOTIF_ATTN_CLUSTER");
+    on = (v && v[0] == '0') ? 0 : 1;
+  }
+  return on == 1;
+}
+
+// Whether a cluster of `nsplit` CTAs of this instantiation can be resident (cudaOccupancyMaxActiveClusters).
+template <int NA, int NB, bool PAIRED, int PPW, int BITS, int LPG>
+bool cluster_fits(int nsplit) {
+  auto kern = gda_fused_kernel<BITS, NA, NB, PAIRED, PPW, LPG, true>;
+  const size_t smem = fused_smem_bytes(NA + NB, true);
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess ||
+      cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess)
+    return false;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(nsplit, 1);
+  cfg.blockDim = dim3(kAttnThreads);
+  cfg.dynamicSmemBytes = smem;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = nsplit;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int clusters = 0;
+  if (cudaOccupancyMaxActiveClusters(&clusters, kern, &cfg) != cudaSuccess) {
+    cudaGetLastError();
+    return false;
+  }
+  return clusters >= 1;
+}
+
 // The one-launch attention step for one head layout, dispatched over the cache's bits and group size.
+// The launch of one (bits, group size) instantiation: the cluster merge when the splits fit one
+// cluster (GDA layout only), else the global merge.
+template <int NA, int NB, bool PAIRED, int PPW, int BITS, int LPG>
+cudaError_t launch_fused_bits(const FusedArgs& f, dim3 grid, cudaStream_t st) {
+  if constexpr (!PAIRED && NB == 1) {
+    if (grid.x >= 2 && grid.x <= (unsigned)kMaxClusterSplits && cluster_merge_enabled()) {
+      static int fits[kMaxClusterSplits + 1] = {};  // 0 unknown, 1 yes, 2 no (per split count)
+      int& fit = fits[grid.x];
+      if (!fit) fit = cluster_fits<NA, NB, PAIRED, PPW, BITS, LPG>((int)grid.x) ? 1 : 2;
+      if (fit == 1) return launch_fused_one<NA, NB, PAIRED, PPW, BITS, LPG, true>(f, grid, st);
+    }
+  }
+  return launch_fused_one<NA, NB, PAIRED, PPW, BITS, LPG, false>(f, grid, st);
+}
+
 template <int NA, int NB, bool PAIRED, int PPW>
 cudaError_t launch_fused(const FusedArgs& f, dim3 grid, int bits, int gs, cudaStream_t st) {
-  if (bits == 16) return launch_fused_one<NA, NB, PAIRED, PPW, 16, 8>(f, grid, st);
-  if (gs == 32) return bits == 4 ? launch_fused_one<NA, NB, PAIRED, PPW, 4, 4>(f, grid, st)
-                                 : launch_fused_one<NA, NB, PAIRED, PPW, 8, 4>(f, grid, st);
-  if (gs == 64) return bits == 4 ? launch_fused_one<NA, NB, PAIRED, PPW, 4, 8>(f, grid, st)
-                                 : launch_fused_one<NA, NB, PAIRED, PPW, 8, 8>(f, grid, st);
-  return bits == 4 ? launch_fused_one<NA, NB, PAIRED, PPW, 4, 16>(f, grid, st)
-                   : launch_fused_one<NA, NB, PAIRED, PPW, 8, 16>(f, grid, st);
+  if (bits == 16) return launch_fused_bits<NA, NB, PAIRED, PPW, 16, 8>(f, grid, st);
+  if (gs == 32) return bits == 4 ? launch_fused_bits<NA, NB, PAIRED, PPW, 4, 4>(f, grid, st)
+                                 : launch_fused_bits<NA, NB, PAIRED, PPW, 8, 4>(f, grid, st);
+  if (gs == 64) return bits == 4 ? launch_fused_bits<NA, NB, PAIRED, PPW, 4, 8>(f, grid, st)
+                                 : launch_fused_bits<NA, NB, PAIRED, PPW, 8, 8>(f, grid, st);
+  return bits == 4 ? launch_fused_bits<NA, NB, PAIRED, PPW, 4, 16>(f, grid, st)
+                   : launch_fused_bits<NA, NB, PAIRED, PPW, 8, 16>(f, grid, st);
 }
 
 template <int NA, int NB, bool PAIRED, int BITS>
