@@ -607,9 +607,11 @@ __global__ void __launch_bounds__(kAttnThreads) gda_fused_kernel(FusedArgs f) {
     }
   };
   const bool append = pos >= 0 && pos < cap && ((pos >= p0 && pos < p1) || (split == 0 && pos >= kv_len));
-  // The first round of this warp's rows does not depend on the RoPE work below (except in
-  // the CTA that writes row pos): start it now.
-  if (!append) load_round(p0 + warp * kPosPerWarp);
+  // The first round of this warp's rows does not depend on the RoPE work below, except in the
+  // warp of the appending CTA whose first round holds row pos: start the others now.
+  const int first = p0 + warp * kPosPerWarp;
+  const bool defer = append && pos >= first && pos < first + kPosPerWarp;
+  if (!defer) load_round(first);
   // RoPE angles of this position, shared by every head of the CTA
   if (threadIdx.x < half) rope_angle(threadIdx.x, pos, f.inv_freq, s_cs[threadIdx.x], s_sn[threadIdx.x]);
   // Launched with programmatic serialization: everything above reads only data that
@@ -685,7 +687,7 @@ __global__ void __launch_bounds__(kAttnThreads) gda_fused_kernel(FusedArgs f) {
 #pragma unroll
     for (int c = 0; c < CPL; ++c) o1[h][c] = o2[h][c] = 0.f;
   }
-  if (append) load_round(p0 + warp * kPosPerWarp);  // after the new row is written
+  if (defer) load_round(first);  // after the new row is written
   for (int base = p0 + warp * kPosPerWarp; base < p1; base += kRoundPositions) {
     if (base != p0 + warp * kPosPerWarp) load_round(base);
 #pragma unroll
@@ -741,24 +743,45 @@ __global__ void __launch_bounds__(kAttnThreads) gda_fused_kernel(FusedArgs f) {
       dst[D + c] = o2[h][c];
     }
   }
-  __syncthreads();
-  for (int it = threadIdx.x; it < NH * 2 * D; it += kAttnThreads) {
-    const int h = it / (2 * D);
-    const int ch = it - h * 2 * D;
+  // Per head: the running maximum over the warps and each warp's rescale factor, once (the
+  // channel loop below then needs one factor load per warp); same arithmetic and order as
+  // rescaling in the channel loop itself.
+  __shared__ float s_fw[kAttnWarps][NH];
+  __shared__ float s_M[NH], s_L[NH];
+  __shared__ unsigned s_live[NH];
+  __syncthreads();  // every warp's state is in shared memory
+  if (threadIdx.x < NH) {
+    const int h = threadIdx.x;
     float M = -INFINITY;
 #pragma unroll
     for (int w = 0; w < kAttnWarps; ++w) M = fmaxf(M, sm_ml[(w * NH + h) * 2]);
-    float L = 0.f, O = 0.f;
+    float L = 0.f;
+    unsigned live = 0;
     if (M != -INFINITY) {
 #pragma unroll
       for (int w = 0; w < kAttnWarps; ++w) {
         const float mw = sm_ml[(w * NH + h) * 2];
         if (mw == -INFINITY) continue;
         const float fw = exp2f(mw - M);
+        s_fw[w][h] = fw;
+        live |= 1u << w;
         L += sm_ml[(w * NH + h) * 2 + 1] * fw;
-        O += sm_o[(int64_t)(w * NH + h) * 2 * D + ch] * fw;
       }
     }
+    s_M[h] = M;
+    s_L[h] = L;
+    s_live[h] = live;
+  }
+  __syncthreads();
+  for (int it = threadIdx.x; it < NH * 2 * D; it += kAttnThreads) {
+    const int h = it / (2 * D);
+    const int ch = it - h * 2 * D;
+    const float M = s_M[h], L = s_L[h];
+    const unsigned live = s_live[h];
+    float O = 0.f;
+#pragma unroll
+    for (int w = 0; w < kAttnWarps; ++w)
+      if (live & (1u << w)) O += sm_o[(int64_t)(w * NH + h) * 2 * D + ch] * s_fw[w][h];
     if constexpr (CLUSTER) {  // into rank 0's shared memory, slot `split`
       float* p = part_s + ((int64_t)split * NH + h) * (2 * D + 2);
       st_dsmem(p + 2 + ch, 0, O);
@@ -1571,7 +1594,7 @@ int motif_gda_decode_attention(const void* q, const motif_kv4_slots* cache, floa
 namespace motif {
 namespace {
 
-constexpr int kMaxClusterSplitsForSmem = 16;
+constexpr int kMaxClusterSplitsForSmem = 8;
 
 // Dynamic shared memory of gda_fused_kernel: the per-warp softmax states, and on the cluster
 // path rank 0's slots for every split's partial.
@@ -1586,8 +1609,7 @@ cudaError_t launch_fused_one(const FusedArgs& f, dim3 grid, cudaStream_t st) {
   const size_t smem = fused_smem_bytes(NA + NB, CLUSTER);
   static bool configured = false;  // one attribute call per instantiation
   if (!configured) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e == cudaSuccess && CLUSTER) e = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+    const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
     configured = true;
   }
@@ -1608,8 +1630,8 @@ cudaError_t launch_fused_one(const FusedArgs& f, dim3 grid, cudaStream_t st) {
   return cudaLaunchKernelEx(&cfg, kern, f);
 }
 
-// Largest cluster (splits of one group) the cluster merge takes: 16 CTAs, a non-portable size
-// that B200 schedules; MOTIF_ATTN_CLUSTER=0 turns the cluster merge off.
+// Largest cluster (splits of one group) the cluster merge takes: 8 CTAs, the portable size;
+// MOTIF_ATTN_CLUSTER=0 turns the cluster merge off.
 constexpr int kMaxClusterSplits = kMaxClusterSplitsForSmem;
 
 bool cluster_merge_enabled() {
@@ -1626,9 +1648,7 @@ template <int NA, int NB, bool PAIRED, int PPW, int BITS, int LPG>
 bool cluster_fits(int nsplit) {
   auto kern = gda_fused_kernel<BITS, NA, NB, PAIRED, PPW, LPG, true>;
   const size_t smem = fused_smem_bytes(NA + NB, true);
-  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess ||
-      cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess)
-    return false;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess) return false;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(nsplit, 1);
   cfg.blockDim = dim3(kAttnThreads);
@@ -1654,11 +1674,15 @@ bool cluster_fits(int nsplit) {
 template <int NA, int NB, bool PAIRED, int PPW, int BITS, int LPG>
 cudaError_t launch_fused_bits(const FusedArgs& f, dim3 grid, cudaStream_t st) {
   if constexpr (!PAIRED && NB == 1) {
-    if (grid.x >= 2 && grid.x <= (unsigned)kMaxClusterSplits && cluster_merge_enabled()) {
+    // Caches of up to 2·kMaxClusterSplits·kMinChunk rows (at most two rounds of rows per
+    // split): the splits shrink to one portable cluster of at most 8 CTAs. Larger clusters were
+    // slower to schedule than the global merge they replace.
+    if (grid.x >= 2 && grid.x <= 2u * kMaxClusterSplits && cluster_merge_enabled()) {
+      const dim3 cgrid(grid.x < (unsigned)kMaxClusterSplits ? grid.x : kMaxClusterSplits, grid.y);
       static int fits[kMaxClusterSplits + 1] = {};  // 0 unknown, 1 yes, 2 no (per split count)
-      int& fit = fits[grid.x];
-      if (!fit) fit = cluster_fits<NA, NB, PAIRED, PPW, BITS, LPG>((int)grid.x) ? 1 : 2;
-      if (fit == 1) return launch_fused_one<NA, NB, PAIRED, PPW, BITS, LPG, true>(f, grid, st);
+      int& fit = fits[cgrid.x];
+      if (!fit) fit = cluster_fits<NA, NB, PAIRED, PPW, BITS, LPG>((int)cgrid.x) ? 1 : 2;
+      if (fit == 1) return launch_fused_one<NA, NB, PAIRED, PPW, BITS, LPG, true>(f, cgrid, st);
     }
   }
   return launch_fused_one<NA, NB, PAIRED, PPW, BITS, LPG, false>(f, grid, st);

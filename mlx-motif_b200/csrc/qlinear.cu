@@ -531,7 +531,28 @@ __device__ void stage_x(const LinArgs& a, __half* xp_s, float* xsum_s, float* co
         stats_acc[2] += tp_read(a.tp_stats_in + i * 3 + 2, num, a.err);
       }
     } else {
-      for (int i = tid; i < a.stats_count; i += nthr) {
+      // The first rounds' loads all go out before any is summed (one L2 round trip instead of
+      // one per round); the summation order is the plain loop's.
+      constexpr int kRounds = 4;
+      float sv[kRounds][3];
+#pragma unroll
+      for (int j = 0; j < kRounds; ++j) {
+        const int i = tid + j * nthr;
+        if (i < a.stats_count) {
+          sv[j][0] = a.stats[i * 3 + 0];
+          sv[j][1] = a.stats[i * 3 + 1];
+          sv[j][2] = a.stats[i * 3 + 2];
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < kRounds; ++j) {
+        if (tid + j * nthr < a.stats_count) {
+          stats_acc[0] += sv[j][0];
+          stats_acc[1] += sv[j][1];
+          stats_acc[2] += sv[j][2];
+        }
+      }
+      for (int i = tid + kRounds * nthr; i < a.stats_count; i += nthr) {
         stats_acc[0] += a.stats[i * 3 + 0];
         stats_acc[1] += a.stats[i * 3 + 1];
         stats_acc[2] += a.stats[i * 3 + 2];
