@@ -480,8 +480,7 @@ def run_b200(a) -> None:
              "step_hbm_gbs_per_gpu": round(bytes_per_step / world / (ms / a.steps / 1e3) / 1e9, 1),
              "step_frac_of_peak": round(step_frac, 4), "attention_p164": attn_p164,
              "prefill_p164": {"ms": round(prefill_ms, 3), "tok_s": round(PROMPT_LEN / (prefill_ms / 1e3), 1),
-                              "path": "one 163-row tensor-core block + the decode step for the last token"
-                              if world == 1 else "decode steps (tensor parallel)"},
+                              "path": prefill_path(model, PROMPT_LEN)},
              "gemv": {k: (round(v, 4) if isinstance(v, float) else v) for k, v in gem.items()}}
 
     # ---- config[2]: p16k with q4 and fp16 caches ----
@@ -572,8 +571,8 @@ def run_b200(a) -> None:
         if not a.no_spec:
             extra["speculative"] = speculative_extra(a, args, van, dev, st, e0, e1, group, rank, world)
 
-    # config[4] under tensor parallelism, at the rank counts its tests cover
-    if world in (2, 4) and not a.no_spec:
+    # config[4] under tensor parallelism (target sharded, draft replicated)
+    if world > 1 and not a.no_spec:
         if model is not None:
             model._graphs.clear()
             del model
@@ -609,6 +608,17 @@ def run_b200(a) -> None:
         import torch.distributed as dist
 
         dist.destroy_process_group()
+
+
+def prefill_path(model, n: int) -> str:
+    """How MotifDecoder.prefill ingests an n-token prompt on this model (one GPU or a TP rank)."""
+    rows = n - 1
+    if rows < model.min_rows_block or not model._block_ok():
+        return "decode steps"
+    big = rows >= model.min_block_rows and model._gemm_ok()
+    kind = "tensor-core q4 GEMMs" if big else "multi-row q4 GEMVs (the shard shapes leave the GEMM contract)"
+    tp = f", tensor parallel over {model.tp} ranks with NCCL all-reduces" if model.tp > 1 else ""
+    return f"one {rows}-row block ({kind}{tp}) + the decode step for the last token"
 
 
 def prefill_flops(model, n: int) -> float:

@@ -499,6 +499,18 @@ MOTIF_API int motif_sample(const void* logits, int64_t rows, int64_t n, int64_t 
                            uint64_t seed, const int32_t* pos_dev, int64_t pos_host, uint32_t stream_id,
                            int32_t* tokens, void* pos_len_inc, void* stream);
 
+/* motif_sample for one shard of a vocabulary split over tensor-parallel ranks
+ * (no reference counterpart: the reference samples on one device through
+ * mlx-lm's generate_step). logits: this rank's n values, global vocabulary
+ * indices row_offset .. row_offset + n - 1; the Gumbel noise is drawn for the
+ * global index, so the ranks together draw exactly what motif_sample draws for
+ * the whole row. key_out (int64, device): the largest order-preserving key of
+ * l/T + g in the shard as a signed value; an int64 MAX all-reduce of the ranks'
+ * keys followed by motif_argmax_key_decode yields the token. */
+MOTIF_API int motif_sample_key(const void* logits, int64_t n, float temperature, uint64_t seed,
+                               const int32_t* pos_dev, int64_t pos_host, uint32_t stream_id, int64_t row_offset,
+                               int64_t* key_out, void* stream);
+
 /* Speculative acceptance of k draft tokens (rejection sampling, the reference's
  * MotifSpeculativeDecoding): p_logits are the target's k+1 rows (positions of
  * the draft tokens and the bonus position), q_logits the draft's k rows, both

@@ -1575,20 +1575,25 @@ int motif_quantized_linear(int dtype, int bits, int group_size, const void* x, i
       }
       if (row == m) return MOTIF_OK;
     }
-    for (int64_t i = 0; i < m; ++i) {
-      LinArgs a{};
-      a.w = w;
-      a.sc = static_cast<const __half*>(scales);
-      a.bi = static_cast<const __half*>(biases);
-      a.N = n;
-      a.K = k;
-      a.y = static_cast<__half*>(y) + i * n;
-      a.mode = kModeX;
-      a.x = static_cast<const __half*>(x) + i * k;
-      int rc = launch_q4(a, workspace, workspace_bytes, st);
-      if (rc) return rc;
+    // Shapes the multi-row kernel does not take (k not a multiple of 512, as the o and down
+    // shards of an 8-way tensor-parallel split): a few rows run the one-row GEMV each; a longer
+    // block runs the general kernel below in one launch instead of one launch per row.
+    if (m <= 4 || rows_need) {
+      for (int64_t i = 0; i < m; ++i) {
+        LinArgs a{};
+        a.w = w;
+        a.sc = static_cast<const __half*>(scales);
+        a.bi = static_cast<const __half*>(biases);
+        a.N = n;
+        a.K = k;
+        a.y = static_cast<__half*>(y) + i * n;
+        a.mode = kModeX;
+        a.x = static_cast<const __half*>(x) + i * k;
+        int rc = launch_q4(a, workspace, workspace_bytes, st);
+        if (rc) return rc;
+      }
+      return MOTIF_OK;
     }
-    return MOTIF_OK;
   }
   const int warps = 8;
   const int64_t blocks = ceil_div(m * n, warps);

@@ -109,6 +109,30 @@ __global__ void __launch_bounds__(kSampleThreads) sample_kernel(const __half* __
   }
 }
 
+// One shard of a vocabulary split over tensor-parallel ranks: the largest key of (l / T + g) over
+// this shard's n logits, the noise drawn for the GLOBAL index row_offset + i (the same numbers
+// one GPU draws for the whole row), written as a signed int64 so an int64 MAX all-reduce over
+// the ranks yields the key of the whole row.
+__global__ void __launch_bounds__(kSampleThreads) sample_key_kernel(const __half* __restrict__ logits, int n,
+                                                                    float inv_t, uint64_t seed,
+                                                                    const int32_t* __restrict__ pos_dev, int pos_host,
+                                                                    uint32_t stream_id, uint32_t row_offset,
+                                                                    long long* __restrict__ key_out) {
+  __shared__ unsigned long long sm[32];
+  const uint32_t pos = (uint32_t)(pos_dev ? *pos_dev : pos_host);
+  unsigned long long best = 0;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    float v = __half2float(logits[i]);
+    if (isnan(v)) v = -INFINITY;
+    const uint32_t gi = row_offset + (uint32_t)i;
+    if (inv_t > 0.f) v = v * inv_t + gumbel(seed, gi, pos, 0u, stream_id);
+    const unsigned long long k = sample_key(v, gi);
+    best = k > best ? k : best;
+  }
+  best = block_max_u64(best, sm);
+  if (threadIdx.x == 0) *key_out = (long long)(best ^ 0x8000000000000000ull);
+}
+
 // Speculative acceptance over K draft tokens: p rows 0..K (target), q rows 0..K-1 (draft).
 // out[0] = accepted count n, out[1] = the token that follows them.
 constexpr int kMaxDraft = 16;
@@ -233,6 +257,18 @@ int motif_sample(const void* logits, int64_t rows, int64_t n, int64_t row_stride
       static_cast<const __half*>(logits), row_stride, (int)n, temperature > 0.f ? 1.f / temperature : 0.f, seed,
       pos_dev, (int)pos_host, stream_id, tokens, static_cast<int32_t*>(pos_len_inc));
   return check_launch("sample");
+}
+
+int motif_sample_key(const void* logits, int64_t n, float temperature, uint64_t seed, const int32_t* pos_dev,
+                     int64_t pos_host, uint32_t stream_id, int64_t row_offset, int64_t* key_out, void* stream) {
+  MOTIF_REQUIRE(logits && key_out, MOTIF_ERR_NULL, "sample_key: null pointer");
+  MOTIF_REQUIRE(n > 0 && row_offset >= 0 && row_offset + n <= 0xFFFFFFFFll, MOTIF_ERR_BAD_SHAPE,
+                "sample_key: n=%lld row_offset=%lld", (long long)n, (long long)row_offset);
+  MOTIF_REQUIRE(temperature >= 0.f, MOTIF_ERR_BAD_CONTRACT, "sample_key: temperature %f", temperature);
+  sample_key_kernel<<<1, kSampleThreads, 0, as_stream(stream)>>>(
+      static_cast<const __half*>(logits), (int)n, temperature > 0.f ? 1.f / temperature : 0.f, seed, pos_dev,
+      (int)pos_host, stream_id, (uint32_t)row_offset, reinterpret_cast<long long*>(key_out));
+  return check_launch("sample_key");
 }
 
 int motif_speculative_accept(const void* p_logits, const void* q_logits, int64_t row_stride,

@@ -108,6 +108,7 @@ SIGNATURES = {
     "motif_q4_gemm": (_I, [_P, _L, _L, _P, _P, _P, _L, _P, _P, _P, _P]),
     "motif_sample": (_I, [_P, _L, _L, _L, _F, C.c_uint64, _P, _L, C.c_uint32, _P, _P, _P]),
     "motif_speculative_accept": (_I, [_P, _P, _L, _P, _L, _L, _F, C.c_uint64, _P, _L, _P, _P]),
+    "motif_sample_key": (_I, [_P, _L, _F, C.c_uint64, _P, _L, C.c_uint32, _L, _P, _P]),
     "motif_embed_rms_norm_rows": (_I, [_I, _P, _L, _P, _L, _L, _P, _F, _P, _P, _P]),
     "motif_rope_qkv_append_rows": (_I, [_P, _L, _P, _L, _KV, _L, _P, _P, _P]),
     "motif_prefill_attention": (_I, [_P, _L, _L, _KV, _L, _I, _L, _F, _P, _P, _P]),

@@ -706,9 +706,12 @@ class MotifDecoder:
             plan.append((qkv_io, o_io, gu_io, dn_io))
         # The lm_head GEMV also picks the greedy token and advances pos_len (MOTIF_FUSED_ARGMAX=0: separate
         # argmax launches).
-        self.fused_argmax = tp or (os.environ.get("MOTIF_FUSED_ARGMAX", "1") != "0" and self.temperature == 0)
-        if tp:  # this rank's key; the ranks' keys are combined by an all-reduce
+        self.fused_argmax = (tp and self.temperature == 0) or (
+            os.environ.get("MOTIF_FUSED_ARGMAX", "1") != "0" and self.temperature == 0)
+        if tp and self.temperature == 0:  # this rank's key; the ranks' keys are combined by an all-reduce
             extra = dict(argmax_key_out=ptr(self.amax_key), argmax_row_offset=self.v0)
+        elif tp:  # temperature: this rank's logits shard, then its Gumbel-max key (motif_sample_key)
+            extra = {}
         elif self.fused_argmax:
             extra = dict(argmax_out=ptr(self.token), pos_len_inc=ptr(self.pos_len))
         else:
@@ -797,6 +800,10 @@ class MotifDecoder:
         if with_head:
             self._linear(head_io, self.lm_head, self.logits, st)
             if self.tp_group is not None:
+                if self.temperature > 0:  # this shard's Gumbel-max key, noise drawn per global index
+                    check(lib.motif_sample_key(ptr(self.logits), self.V_local, self.temperature, self.seed,
+                                               ptr(self.pos_len), 0, self.stream_id, self.v0, ptr(self.amax_key), st),
+                          "sample_key")
                 torch.distributed.all_reduce(self.amax_key, op=torch.distributed.ReduceOp.MAX, group=self.tp_group)
                 check(lib.motif_argmax_key_decode(ptr(self.amax_key), ptr(self.token), ptr(self.pos_len), st),
                       "argmax_key_decode")
@@ -831,9 +838,10 @@ class MotifDecoder:
 
     def set_sampling(self, temperature: float, seed: int = 0, stream_id: int = 0) -> None:
         """Head mode for the following steps: greedy (temperature 0) or a Gumbel-max draw from
-        softmax(logits / temperature), seeded and counted by position (``motif_sample``)."""
-        if temperature > 0 and self.tp_group is not None:
-            raise ValueError("temperature sampling runs on one GPU (the sharded head picks greedily)")
+        softmax(logits / temperature), seeded and counted by position (``motif_sample``; under
+        tensor parallelism each rank draws the noise of its vocabulary shard by global index,
+        ``motif_sample_key``, and the ranks' keys meet in the MAX all-reduce of the greedy head,
+        so the draw equals one GPU's)."""
         self.temperature = float(temperature)
         self.seed = int(seed)
         self.stream_id = int(stream_id)

@@ -80,6 +80,27 @@ def test_quantized_linear_row_chunks_match_oracle(cuda, M, N, K):
         assert_close(down(got), ref, "float16", what=f"{M}-row linear {N}x{K} call {call}")
 
 
+@pytest.mark.parametrize("M", [3, 5, 37, 163])
+@pytest.mark.parametrize("N,K", [(4096, 768), (4096, 1792)])
+def test_quantized_linear_rows_of_tp8_shard_shapes(cuda, M, N, K):
+    """Row blocks of the 8-way tensor-parallel o and down shards (k = 768, 1792: not multiples of
+    512, so neither the multi-row GEMV nor the GEMM takes them): a few rows run the one-row GEMV,
+    a longer block the general kernel in one launch; both match the oracle."""
+    from mlx_motif._native import lib
+    from mlx_motif.linear import quantized_matmul
+    from mlx_motif.quantization import quantize
+
+    rng = np.random.default_rng(M * 7 + K)
+    w = rounded(rng.standard_normal((N, K)) * 0.02, "float16")
+    x = rounded(rng.standard_normal((M, K)), "float16")
+    d, s, b = quantize(up(w), 64, 4)
+    ref = O.quantized_matmul(x, d.cpu().numpy().view(np.uint32), down(s), down(b), 64, 4)
+    ws = torch.zeros(max(lib.motif_quantized_linear_workspace_bytes(M, N, K, 4, 64), 16), dtype=torch.uint8,
+                     device="cuda")
+    got = quantized_matmul(up(x), d, s, b, workspace=ws)
+    assert_close(down(got), ref, "float16", what=f"{M}-row linear {N}x{K}")
+
+
 # ---------------------------------------------------------------- rope / norms / argmax
 @pytest.mark.parametrize("offset", [0, 5, 16000])
 def test_rope_matches_oracle(cuda, offset):

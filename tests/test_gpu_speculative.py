@@ -47,6 +47,31 @@ def _accept(N, p, q, draft, T, pos=0, seed=3):
     return out.tolist()
 
 
+@pytest.mark.parametrize("shards", [2, 4, 8])
+@pytest.mark.parametrize("T", [0.0, 0.7, 1.3])
+def test_sample_key_over_vocabulary_shards_equals_whole_row(cuda, shards, T):
+    """Tensor-parallel sampling: each shard's motif_sample_key (noise drawn per global index), the
+    largest key over the shards (the int64 MAX all-reduce) and motif_argmax_key_decode give the
+    token motif_sample draws from the whole row, at every position tried."""
+    from mlx_motif import _native as N
+
+    V = 219520
+    g = torch.Generator(device=cuda).manual_seed(shards)
+    logits = (torch.randn((1, V), generator=g, device=cuda) * 2).half()
+    per = V // shards
+    keys = torch.zeros(shards, dtype=torch.int64, device=cuda)
+    tok = torch.zeros(1, dtype=torch.int32, device=cuda)
+    for pos in (0, 5, 163):
+        want = _sample(N, logits, T, seed=11, pos=pos).item()
+        for r in range(shards):
+            N.check(N.lib.motif_sample_key(logits.data_ptr() + 2 * r * per, per, T, 11, None, pos, 0, r * per,
+                                           keys[r:].data_ptr(), N.stream()), "sample_key")
+        best = keys.max().reshape(1).contiguous()
+        N.check(N.lib.motif_argmax_key_decode(best.data_ptr(), tok.data_ptr(), None, N.stream()), "key_decode")
+        torch.cuda.synchronize()
+        assert tok.item() == want, f"pos {pos}: shards give {tok.item()}, the whole row {want}"
+
+
 def test_speculative_accept_rules(cuda):
     from mlx_motif import _native as N
 

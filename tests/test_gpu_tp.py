@@ -50,6 +50,53 @@ def _worker(rank, world, port, q, nccl_only=False):
         dist.destroy_process_group()
 
 
+def _sample_worker(rank, world, port, q):
+    import torch.distributed as dist
+    from mlx_motif.model import MotifDecoder
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60))
+    try:
+        m = MotifDecoder.random(_args(), seed=5, std=0.05, max_seq=64, device=f"cuda:{rank}",
+                                tp_group=dist.group.WORLD, rank=rank, world=world)
+        m.set_sampling(0.8, seed=21)
+        toks = m.generate(PROMPT, N_TOKENS)
+        m._graphs.clear()
+        torch.cuda.synchronize()
+        dist.barrier()
+        m.release_exchange()
+        q.put((rank, toks))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_tp_temperature_sampling_equals_single_gpu(world):
+    """Temperature sampling under tensor parallelism (each rank's Gumbel-max key over its
+    vocabulary shard, noise drawn per global index, combined by the MAX all-reduce) draws the
+    same tokens as one GPU with the same seed."""
+    from mlx_motif.model import MotifDecoder
+
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = 29880 + (os.getpid() % 40) + 5 * world
+    procs = [ctx.Process(target=_sample_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    got = dict(q.get(timeout=300) for _ in procs)
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    ref = MotifDecoder.random(_args(), seed=5, std=0.05, max_seq=64, device="cuda:0")
+    ref.set_sampling(0.8, seed=21)
+    want = ref.generate(PROMPT, N_TOKENS)
+    for r in range(world):
+        assert got[r] == want, f"rank {r}: TP{world} sampled {got[r]}, one GPU {want}"
+
+
 @pytest.mark.parametrize("world,exchange", [(2, "peer"), (2, "nccl"), (4, "peer"), (8, "peer")])
 def test_tp_decode_equals_single_gpu(world, exchange):
     """Peer-memory exchange inside the GEMVs (default) and the NCCL all-reduce path."""
