@@ -431,6 +431,8 @@ def run_b200(a) -> None:
     sampler = ClockSampler(local) if rank == 0 else None
     if sampler:
         sampler.start()
+    torch.cuda.synchronize()
+    model.exchange_read_ns(reset=True)
     st = torch.cuda.current_stream()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier(world)
@@ -446,6 +448,7 @@ def run_b200(a) -> None:
         sampler.mark("t1")
     barrier(world)
     ms = max_over_ranks(e0.elapsed_time(e1), world)
+    xchg_ms = max_over_ranks(model.exchange_read_ns() / 1e6 / a.steps, world)
     clocks = sampler.stop() if sampler else None
     value = a.steps / (ms / 1e3)
     launches = model_launches(model) * a.steps
@@ -482,6 +485,12 @@ def run_b200(a) -> None:
              "prefill_p164": {"ms": round(prefill_ms, 3), "tok_s": round(PROMPT_LEN / (prefill_ms / 1e3), 1),
                               "path": prefill_path(model, PROMPT_LEN)},
              "gemv": {k: (round(v, 4) if isinstance(v, float) else v) for k, v in gem.items()}}
+    if world > 1:
+        extra["tp_exchange"] = {
+            "read_ms_per_step": round(xchg_ms, 4), "share_of_step": round(xchg_ms / (ms / a.steps), 4),
+            "note": "time CTA 0 of the consuming GEMVs spent reading the peers' exchanged rows and PolyNorm "
+                    "statistics (waits for slower ranks included), summed over the exchanges of a step, max "
+                    "over ranks"}
 
     # ---- config[2]: p16k with q4 and fp16 caches ----
     if not a.no_long:

@@ -415,7 +415,9 @@ MOTIF_API int motif_prefill_post(const void* o, int64_t seq, int64_t q_heads, in
  * stream serialization, it starts streaming weights while the previous kernel
  * finishes. Before it waits for that kernel it also reads the weights and the
  * prologue's constants (norm_w, poly_w, poly_b), so the previous kernel in the
- * stream must not write those. */
+ * stream must not write those. With a tensor-parallel exchange, CTA 0 adds the
+ * nanoseconds its exchange reads took (waits for the peers included) to the
+ * int64 at byte 65504 of the workspace; the caller reads and zeroes it. */
 typedef struct motif_linear_io {
   int32_t mode;
   const void* x;

@@ -97,7 +97,8 @@ constexpr size_t kCounterBytes = sizeof(int) * kCounterTiles;
 constexpr int64_t kErrSlot = kCounterTiles - 1;
 constexpr int64_t kAmaxTilesSlot = kCounterTiles - 2;
 constexpr int64_t kAmaxKeySlot = kCounterTiles - 4;
-constexpr int64_t kTileCounterCap = kCounterTiles - 4;  // split-tile counters: N up to 262080 rows
+constexpr int64_t kTpWaitSlot = kCounterTiles - 8;     // [-8 .. -7] exchange-read time, ns (int64)
+constexpr int64_t kTileCounterCap = kCounterTiles - 8;  // split-tile counters: N up to 262016 rows
 
 enum : int { kModeX = 0, kModeAddRms = 1, kModePoly = 2 };
 
@@ -156,6 +157,7 @@ struct LinArgs {
   long long* tp_stats[8];
   const long long* tp_in;
   const long long* tp_stats_in;
+  unsigned long long* tp_wait_ns;  // CTA 0 adds the time its exchange reads took (tp_world > 0)
 };
 
 constexpr unsigned long long kTpWaitNs = 2000ull * 1000 * 1000;  // exchange wait limit (2 s)
@@ -477,6 +479,7 @@ __device__ void stage_x(const LinArgs& a, __half* xp_s, float* xsum_s, float* co
   if (MODE == kModeAddRms && a.tp_in) {
     // Tensor-parallel consumer: delta = fp16(Σ_r partial_r) over the ranks' exchanged rows,
     // summed in rank order so every rank gets the same bits.
+    const unsigned long long t_read = global_ns();
     const int num = tp_number(a);
     for (int w = tid; w < words; w += nthr) {
       float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
@@ -495,6 +498,7 @@ __device__ void stage_x(const LinArgs& a, __half* xp_s, float* xsum_s, float* co
       store_vec<__half, 8>(delta_s + (int64_t)w * 8, acc);
     }
     __syncthreads();
+    if (blockIdx.x == 0 && tid == 0 && a.tp_wait_ns) atomicAdd(a.tp_wait_ns, global_ns() - t_read);
     delta = delta_s;
   }
   uint4 in0[kMaxStageWords], in1[kMaxStageWords], in2[kMaxStageWords];
@@ -524,12 +528,14 @@ __device__ void stage_x(const LinArgs& a, __half* xp_s, float* xsum_s, float* co
   }
   if (MODE == kModePoly) {
     if (a.tp_stats_in) {  // all ranks' tile statistics, exchanged as pairs
+      const unsigned long long t_read = global_ns();
       const int num = tp_number(a);
       for (int i = tid; i < a.stats_count; i += nthr) {
         stats_acc[0] += tp_read(a.tp_stats_in + i * 3 + 0, num, a.err);
         stats_acc[1] += tp_read(a.tp_stats_in + i * 3 + 1, num, a.err);
         stats_acc[2] += tp_read(a.tp_stats_in + i * 3 + 2, num, a.err);
       }
+      if (blockIdx.x == 0 && tid == 0 && a.tp_wait_ns) atomicAdd(a.tp_wait_ns, global_ns() - t_read);
     } else {
       // The first rounds' loads all go out before any is summed (one L2 round trip instead of
       // one per round); the summation order is the plain loop's.
@@ -1404,6 +1410,7 @@ int launch_q4(LinArgs& a, void* workspace, size_t ws_bytes, cudaStream_t st) {
       return fail(MOTIF_ERR_WORKSPACE, "linear_fused: tensor-parallel exchange needs a workspace of >= %zu bytes",
                   kCounterBytes);
     a.err = static_cast<int*>(workspace) + kErrSlot;
+    a.tp_wait_ns = reinterpret_cast<unsigned long long*>(static_cast<int*>(workspace) + kTpWaitSlot);
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(p.ctas);

@@ -644,6 +644,19 @@ class MotifDecoder:
         torch.cuda.synchronize(self.device)
         torch.distributed.barrier(group=self.tp_group)
 
+    _TP_WAIT_BYTE = 65504  # the GEMV workspace's int64 of exchange-read nanoseconds (CTA 0)
+
+    def exchange_read_ns(self, reset: bool = False) -> int:
+        """Nanoseconds CTA 0 of the consuming GEMVs spent reading exchanged values (waits for the
+        peers included) since the last reset; 0 without a peer-memory exchange."""
+        if not self.tp_exchange:
+            return 0
+        word = self.lin_ws[self._TP_WAIT_BYTE:self._TP_WAIT_BYTE + 8].view(torch.int64)
+        v = int(word.item())
+        if reset:
+            word.zero_()
+        return v
+
     def release_exchange(self) -> None:
         """Close the peers' buffers and free this rank's (call on every rank, after a barrier)."""
         if self._xbuf is None:
