@@ -134,14 +134,13 @@ MOTIF_API int motif_sdpa_dual_v(int dtype, const void* q, const void* k, const v
 
 /* Allocation-free variant of motif_sdpa_dual_v, for callers that cannot call
  * cudaMalloc (a plugin whose device memory belongs to its host framework's
- * allocator, code running during someone else's stream capture, hot paths
- * that must not take cudaMalloc's device-wide synchronisation). It has no
+ * allocator, hot paths that must not take cudaMalloc's device-wide
+ * synchronisation). It has no
  * counterpart in the reference. Its split-KV partials live in one
  * file-scope __device__ array of motif_sdpa_dual_v_static_scratch_bytes()
  * (4 MiB) that each GPU loading the library keeps until exit. The first
- * call on a device resolves the array's device address (call it once
- * before any stream capture; concurrent first calls from several host
- * threads are safe). Shapes whose two-split partials
+ * call on a device resolves the array's device address (concurrent first
+ * calls from several host threads are safe). Shapes whose two-split partials
  * (batch*h_q*(2*head_dim+2)*4*2 bytes) exceed the array are rejected with
  * MOTIF_ERR_WORKSPACE. The rejection is deliberate: this entry is the
  * split-KV kernel with its partials in the array, and a shape too large for

@@ -1942,10 +1942,8 @@ int motif_vanilla_decode_step(const void* qkv, const float* inv_freq, const moti
 // Allocation-free variant of motif_sdpa_dual_v.
 //
 // Some callers cannot call cudaMalloc at all: a plugin whose device memory
-// belongs to the host framework's own allocator, code that runs while
-// someone else's stream is being captured into a CUDA graph (an allocation
-// there breaks or escapes the capture), and hot paths that must not take
-// cudaMalloc's implicit device synchronisation. For them the split-KV
+// belongs to the host framework's own allocator, and hot paths that must
+// not take cudaMalloc's implicit device synchronisation. For them the split-KV
 // partials live in this file-scope device array instead of a caller
 // workspace. It is sized once for the library (kStaticScratchBytes) and
 // every GPU that loads the library holds it until the process exits.
@@ -1963,7 +1961,7 @@ static std::atomic<void*> g_scratch_ptr[kMaxDevices];
 
 // Host code may not use g_attn_scratch as a device address: it names the
 // host-side stand-in. Resolve the device address once per device, with that
-// device current (this first call must not sit inside a stream capture).
+// device current.
 int static_scratch(void** out) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);

@@ -1,9 +1,8 @@
 """The allocation-free attention entry point (``motif_sdpa_dual_v_static``).
 
 It serves callers that cannot allocate device memory — a plugin whose memory
-belongs to its host framework's allocator, code that runs while another
-component captures a CUDA graph, or a hot path that must not pay cudaMalloc's
-device-wide synchronisation — by keeping the split-KV partials in one
+belongs to its host framework's allocator, or a hot path that must not pay
+cudaMalloc's device-wide synchronisation — by keeping the split-KV partials in one
 static device array instead of a caller workspace. These tests call it through
 the C ABI and hold it to the regular ``motif_sdpa_dual_v`` (which takes a
 caller workspace) on two calls in a row, then check the size limit.
