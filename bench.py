@@ -495,7 +495,7 @@ def run_b200(a) -> None:
     # ---- config[2]: p16k with q4 and fp16 caches ----
     if not a.no_long:
         weights = model.weights_dict()
-        model._graphs.clear()  # graphs may hold NCCL calls: released before the communicator
+        model.release_graphs()  # graphs may hold NCCL calls: released before the communicator
         del model
         model = None
         torch.cuda.empty_cache()
@@ -531,14 +531,14 @@ def run_b200(a) -> None:
                 "peak_hbm_bytes": int(torch.cuda.max_memory_allocated(dev)),
                 "prefill_16000": pre,
             }
-            m._graphs.clear()
+            m.release_graphs()
             del m
             torch.cuda.empty_cache()
 
     # ---- config[3]: the 2.6B-class vanilla decoder (one GPU: the vanilla path has no TP) ----
     if world == 1 and not a.no_vanilla:
         if model is not None:
-            model._graphs.clear()
+            model.release_graphs()
             del model
             model = None
             torch.cuda.empty_cache()
@@ -574,7 +574,7 @@ def run_b200(a) -> None:
             "kernels_per_step": model_launches(m),
         }
         # ---- config[4]: speculative decoding, this 2.6B-class draft + the 12.7B-class target ----
-        m._graphs.clear()
+        m.release_graphs()
         del m
         torch.cuda.empty_cache()
         if not a.no_spec:
@@ -583,7 +583,7 @@ def run_b200(a) -> None:
     # config[4] under tensor parallelism (target sharded, draft replicated)
     if world > 1 and not a.no_spec:
         if model is not None:
-            model._graphs.clear()
+            model.release_graphs()
             del model
             model = None
             torch.cuda.empty_cache()
@@ -611,7 +611,7 @@ def run_b200(a) -> None:
         }
         print(json.dumps(line), flush=True)
     if model is not None:
-        model._graphs.clear()
+        model.release_graphs()
     torch.cuda.synchronize()
     if world > 1:
         import torch.distributed as dist
@@ -702,11 +702,12 @@ def speculative_extra(a, args, van, dev, st, e0, e1, group, rank, world) -> dict
         **rows_ms,
         "note": "draft and target are independent random-init models, so few draft tokens match "
                 "the target's distribution; the verify forward streams the target's weights once for "
-                "its K+1 rows (multi-row GEMV); on one GPU the verify replays a CUDA graph (positions "
-                "read from the device offset), under TP it runs eagerly with NCCL all-reduces; "
-                "verify_forward_ms and decode_step_ms also cover the host's rewind between calls",
+                "its K+1 rows (multi-row GEMV); the verify replays a CUDA graph (positions read from "
+                "the device offset; under TP the graph also holds the NCCL all-reduces and the "
+                "lm_head all-gather); verify_forward_ms and decode_step_ms also cover the host's "
+                "rewind between calls (under TP: a device sync, two barriers and the exchange reset)",
     }
-    target._graphs.clear()  # graphs may hold NCCL calls: released before the communicator
+    target.release_graphs()  # graphs may hold NCCL calls: released before the communicator
     torch.cuda.synchronize()
     barrier(world)
     del spec, draft, target

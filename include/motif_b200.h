@@ -296,7 +296,11 @@ MOTIF_API int motif_rope(int dtype, const void* x, int64_t batch, int64_t heads,
  * tensor-core GEMM (motif_q4_gemm); other bits/groups/dtypes take a
  * CUDA-core path. The
  * workspace (motif_quantized_linear_workspace_bytes) must be zero-filled
- * before its first use; the kernel leaves it zeroed. */
+ * before its first use; the kernel leaves it zeroed. Rows of a tile split
+ * between warps are reduced by the tile's first warp, which waits for the
+ * others' partials: the one-row GEMV's grid is at most one CTA per SM and
+ * relies on all of them becoming resident (a wait that runs out after 200 ms
+ * sets the workspace's error word). */
 MOTIF_API size_t motif_quantized_linear_workspace_bytes(int64_t m, int64_t n, int64_t k, int bits,
                                               int group_size);
 MOTIF_API int motif_quantized_linear(int dtype, int bits, int group_size, const void* x, int64_t m,
@@ -408,7 +412,8 @@ MOTIF_API int motif_prefill_post(const void* o, int64_t seq, int64_t q_heads, in
  * stats_out (optional): for output rows [0, stats_rows) (a multiple of 16),
  * one (Σy², Σy⁴, Σy⁶) triplet per 16-row tile of the fp16-rounded outputs.
  * workspace: motif_linear_fused_workspace_bytes(n, k) bytes, zero-filled
- * before first use (the kernel leaves its counters zeroed). Its first 64 KiB
+ * before first use (the kernel leaves it zeroed; split tiles are reduced as in
+ * motif_quantized_linear). Its first 64 KiB
  * hold per-tile counters at a fixed place, so one workspace sized for the
  * largest shape serves GEMVs of every shape in turn; launched with programmatic
  * stream serialization, it starts streaming weights while the previous kernel

@@ -116,8 +116,9 @@ struct LinArgs {
   int64_t units;
   int total_warps;
   __half* y;
-  float* partial;  // [ntiles][maxc][16]
-  int* counters;   // [ntiles], zero between calls
+  float* partial;  // multi-row kernel: [ntiles][maxc][16 * rows] floats
+  long long* ppair;  // one-row kernels: [ntiles][maxc][16] (value, 1) pairs, zero between calls
+  int* counters;   // [ntiles], zero between calls (multi-row kernel)
   int maxc;
   // prologue
   int mode;
@@ -210,6 +211,71 @@ __device__ __forceinline__ float tp_read(const long long* p, int number, int* er
     } while ((int)(x >> 32) != number);
   }
   return __uint_as_float((uint32_t)x);
+}
+
+// Split-tile partials of the one-row kernels. A warp that shares a tile with others stores
+// its 16 row sums as 8-byte (fp32 value, kPartMark) pairs and moves on — no fence, no counter, no
+// round trip. The tile's first warp (slot 0), whose range ends with the tile and which
+// therefore finishes it last, keeps its own sums in registers, reads the other slots until
+// each carries the marker, adds them in slot order and clears them (the region is zero
+// between launches). Each pair is one naturally aligned 64-bit access, so a reader that sees
+// the marker sees the value stored with it. The waits point only at warps of higher index,
+// which never wait on lower ones, and the grid is at most one CTA per SM, so every wait
+// ends; a wait that still runs out (200 ms) sets the error word.
+constexpr unsigned long long kPartWaitNs = 200ull * 1000 * 1000;
+// The marker word: a NaN pattern that no arithmetic produces (CUDA's NaN results are
+// 0x7FFFFFFF), so a float left in the region by some other use cannot pass for it.
+constexpr uint32_t kPartMark = 0x7FF0A001u;
+
+__device__ __forceinline__ void part_store(long long* p, float v) {
+  const long long q = (long long)(((unsigned long long)kPartMark << 32) | __float_as_uint(v));
+  asm volatile("st.relaxed.gpu.global.b64 [%0], %1;\n" ::"l"(p), "l"(q) : "memory");
+}
+
+__device__ __forceinline__ long long part_load(const long long* p) {
+  long long v;
+  asm volatile("ld.relaxed.gpu.global.b64 %0, [%1];\n" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// s (slot 0's sum) + slots 1..nc-1 of one row, in slot order. The loads of kChunk slots go out
+// together; slots not yet carrying the marker are re-read together until all do (bounded).
+template <int kChunk>
+__device__ __forceinline__ float part_reduce(long long* p, int nc, float s, int* err) {
+  for (int i0 = 1; i0 < nc; i0 += kChunk) {
+    long long q[kChunk];
+    uint32_t pending = 0;
+#pragma unroll
+    for (int j = 0; j < kChunk; ++j)
+      if (i0 + j < nc) q[j] = part_load(p + (int64_t)(i0 + j) * kTileRows);
+#pragma unroll
+    for (int j = 0; j < kChunk; ++j)
+      if (i0 + j < nc && (uint32_t)((unsigned long long)q[j] >> 32) != kPartMark) pending |= 1u << j;
+    if (pending) {
+      const unsigned long long t0 = global_ns();
+      while (pending) {
+#pragma unroll
+        for (int j = 0; j < kChunk; ++j)
+          if (pending & (1u << j)) q[j] = part_load(p + (int64_t)(i0 + j) * kTileRows);
+#pragma unroll
+        for (int j = 0; j < kChunk; ++j)
+          if ((pending & (1u << j)) && (uint32_t)((unsigned long long)q[j] >> 32) == kPartMark) pending &= ~(1u << j);
+        if (pending && global_ns() - t0 > kPartWaitNs) {
+          if (err) atomicExch(err, 3);
+          break;
+        }
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < kChunk; ++j) {
+      if (i0 + j < nc) {
+        s += __uint_as_float((uint32_t)q[j]);
+        asm volatile("st.relaxed.gpu.global.b64 [%0], %1;\n" ::"l"(p + (int64_t)(i0 + j) * kTileRows), "l"(0ll)
+                     : "memory");
+      }
+    }
+  }
+  return s;
 }
 
 struct UnitRegs {
@@ -306,8 +372,9 @@ __device__ __forceinline__ int warp_of_unit(uint32_t u, uint32_t units, uint32_t
   return (int)(((u + 1) * tw - 1) / units);
 }
 
-// Finish this warp's share of a tile: write it, or publish a partial and let the last
-// contributing warp reduce. Also emits the tile's PolyNorm statistics when asked.
+// Finish this warp's share of a tile: write it, or publish a partial (the tile's first warp
+// reduces, see part_store). Also emits the tile's PolyNorm statistics when asked.
+template <int kChunk>
 __device__ void tile_epilogue(const LinArgs& a, int tile, int gw, float acc_r, float acc_r8, int lane) {
   const int r = lane >> 2, c = lane & 3;
   acc_r += __shfl_xor_sync(0xffffffffu, acc_r, 1);
@@ -330,30 +397,21 @@ __device__ void tile_epilogue(const LinArgs& a, int tile, int gw, float acc_r, f
     have = lane < kTileRows;
   } else {
     const int slot = gw - w_first;
-    float* p = a.partial + ((int64_t)tile * a.maxc + slot) * kTileRows;
-    if (c == 0) {
-      p[r] = acc_r;
-      p[r + 8] = acc_r8;
-    }
-    // Publish: the warp barrier orders the lanes' stores before lane 0's release
-    // fence and counter increment (the last contributor acquires before reading).
-    __syncwarp();
-    int old = 0;
-    if (lane == 0) {
-      __threadfence();
-      old = atomicAdd(a.counters + tile, 1);
-    }
-    old = __shfl_sync(0xffffffffu, old, 0);
-    if (old == nc - 1) {
-      __threadfence();
+    long long* p = a.ppair + (int64_t)tile * a.maxc * kTileRows;
+    if (slot > 0) {
+      if (c == 0) {
+        part_store(p + slot * kTileRows + r, acc_r);
+        part_store(p + slot * kTileRows + r + 8, acc_r8);
+      }
+    } else {
+      const float a_r = __shfl_sync(0xffffffffu, acc_r, (lane & 7) * 4);
+      const float a_r8 = __shfl_sync(0xffffffffu, acc_r8, (lane & 7) * 4);
       if (lane < kTileRows) {
-        const float* base = a.partial + (int64_t)tile * a.maxc * kTileRows + lane;
         float s = 0.f;
-        for (int i = 0; i < nc; ++i) s += __ldcg(base + i * kTileRows);
-        v = s;
+        s += lane < 8 ? a_r : a_r8;  // slot 0: this warp's sums
+        v = part_reduce<kChunk>(p + lane, nc, s, a.err);
         have = true;
       }
-      if (lane == 0) a.counters[tile] = 0;
     }
   }
   const int64_t row = row0 + lane;
@@ -706,7 +764,7 @@ __global__ void __launch_bounds__(kThreads, 2) q4_gemv_kernel(LinArgs a) {
     if (has1) load_unit(B, a, t1, b1, r, c);
     compute_unit(A, a, blk, xp_s, xsum_s, c, q_lane, acc_r, acc_r8);
     if (!has1 || t1 != tile) {
-      tile_epilogue(a, tile, gw, acc_r, acc_r8, lane);
+      tile_epilogue<2>(a, tile, gw, acc_r, acc_r8, lane);
       acc_r = acc_r8 = 0.f;
     }
     if (has1) {
@@ -715,7 +773,7 @@ __global__ void __launch_bounds__(kThreads, 2) q4_gemv_kernel(LinArgs a) {
       if (u + 2 < u1) load_unit(A, a, t2, b2, r, c);
       compute_unit(B, a, b1, xp_s, xsum_s, c, q_lane, acc_r, acc_r8);
       if (u + 2 >= u1 || t2 != t1) {
-        tile_epilogue(a, t1, gw, acc_r, acc_r8, lane);
+        tile_epilogue<2>(a, t1, gw, acc_r, acc_r8, lane);
         acc_r = acc_r8 = 0.f;
       }
       tile = t2;
@@ -983,7 +1041,7 @@ __global__ void __launch_bounds__(kTmaThreads, kTmaMinBlocks) q4_gemv_tma_kernel
       if (++ib == nblk) { ib = 0; ++it; }
     }
     if (u + 1 >= u1 || blk + 1 == nblk) {
-      tile_epilogue(a, tile, gw, acc_r, acc_r8, lane);
+      tile_epilogue<16>(a, tile, gw, acc_r, acc_r8, lane);
       acc_r = acc_r8 = 0.f;
     }
     if (++blk == nblk) { blk = 0; ++tile; }
@@ -1201,6 +1259,12 @@ __global__ void __launch_bounds__(512, 1) q4_gemv_rows_kernel(const __grid_const
             for (int i = 0; i < nc; ++i) sum += __ldcg(base + i * (kTileRows * kRowsMax) + idx);
             if (n < R && row0 + row < a.N) a.y[(int64_t)n * a.N + row0 + row] = __float2half_rn(sum);
           }
+          // leave the partial region zero: the one-row kernels' reduction shares it
+          float* clr = a.partial + (int64_t)tile * a.maxc * (kTileRows * kRowsMax);
+          for (int i = 0; i < nc; ++i) {
+#pragma unroll
+            for (int q = 0; q < 4; ++q) clr[i * (kTileRows * kRowsMax) + lane * 4 + q] = 0.f;
+          }
           if (lane == 0) a.counters[tile] = 0;
         }
       }
@@ -1283,7 +1347,7 @@ Plan make_plan(int64_t N, int64_t K, int sms, int warps_per_cta) {
   p.maxc = min_units > 0 ? (int)(ceil_div(p.nblk, min_units) + 1) : p.nblk + 1;
   if (p.maxc > p.nblk + 1) p.maxc = p.nblk + 1;
   p.smem = (size_t)K * sizeof(__half) + (size_t)(K / 64) * sizeof(float) + 32 * 3 * sizeof(float);
-  p.ws_partial = sizeof(float) * (size_t)p.ntiles * p.maxc * kTileRows;
+  p.ws_partial = sizeof(long long) * (size_t)p.ntiles * p.maxc * kTileRows;
   p.ws_counters = sizeof(int) * (size_t)p.ntiles;
   return p;
 }
@@ -1376,11 +1440,11 @@ int launch_q4(LinArgs& a, void* workspace, size_t ws_bytes, cudaStream_t st) {
       return fail(MOTIF_ERR_BAD_SHAPE, "quantized_linear: n=%lld rows exceed %lld", (long long)a.N,
                   (long long)(kTileCounterCap * kTileRows));
     a.counters = static_cast<int*>(workspace);
-    a.partial = reinterpret_cast<float*>(static_cast<char*>(workspace) + kCounterBytes);
+    a.ppair = reinterpret_cast<long long*>(static_cast<char*>(workspace) + kCounterBytes);
     a.err = a.counters + kErrSlot;
   } else {
     a.counters = nullptr;
-    a.partial = nullptr;
+    a.ppair = nullptr;
   }
   if (a.argmax_out || a.argmax_key_out) {  // the argmax state lives in the workspace's control words
     if (!workspace || ws_bytes < kCounterBytes)

@@ -861,6 +861,14 @@ class MotifDecoder:
         self._plan = None
         self._graphs.clear()
 
+    def release_graphs(self) -> None:
+        """Drop every captured CUDA graph (decode steps and row blocks). Under tensor parallelism
+        the graphs hold NCCL calls, so every rank calls this before the process group is
+        destroyed."""
+        self._graphs.clear()
+        self._row_graphs.clear()
+        self._rows_seen.clear()
+
     def rewind(self, offset: int) -> None:
         """Drop cache rows at and after ``offset`` (the reference cache's ``trim``): the next step
         writes position ``offset``."""
@@ -1142,8 +1150,10 @@ class MotifDecoder:
     def _rows_graph_ok(self, S: int) -> bool:
         """A row block replays as a CUDA graph when its launches take no host-side offset: an fp16
         cache (a quantized cache is dequantized up to the block's rows) and a short block (the
-        multi-row GEMV and split attention path). MOTIF_ROWS_GRAPH=0 keeps every call eager."""
-        return (self.cache_kind == "fp16" and self.tp_group is None and 1 <= S < min(self.min_block_rows, 129)
+        multi-row GEMV and split attention path). Under tensor parallelism the graph also holds
+        the block's NCCL all-reduces and the lm_head all-gather; every rank captures at the same
+        call. MOTIF_ROWS_GRAPH=0 keeps every call eager."""
+        return (self.cache_kind == "fp16" and 1 <= S < min(self.min_block_rows, 129)
                 and os.environ.get("MOTIF_ROWS_GRAPH", "1") != "0")
 
     def check_rows_error(self) -> None:

@@ -41,7 +41,7 @@ def _worker(rank, world, port, q, nccl_only=False):
         toks = m.generate(PROMPT, N_TOKENS)
         m.reset()
         again = m.generate(PROMPT, N_TOKENS)  # rewound position: the exchange flags were reset
-        m._graphs.clear()  # graphs holding NCCL calls go before the process group
+        m.release_graphs()  # graphs holding NCCL calls go before the process group
         torch.cuda.synchronize()
         dist.barrier()
         m.release_exchange()
@@ -62,7 +62,7 @@ def _sample_worker(rank, world, port, q):
                                 tp_group=dist.group.WORLD, rank=rank, world=world)
         m.set_sampling(0.8, seed=21)
         toks = m.generate(PROMPT, N_TOKENS)
-        m._graphs.clear()
+        m.release_graphs()
         torch.cuda.synchronize()
         dist.barrier()
         m.release_exchange()
@@ -146,15 +146,31 @@ def _rows_worker(rank, world, port, q):
                                 rank=rank, world=world)
         m.prefill(ROW_PROMPT)  # a 169-row block: GEMMs (TP2) or the multi-row GEMV (TP4, TP8), all-reduced
         first = int(m.token.item())
+        # The verify block replays a CUDA graph (NCCL calls included) from its second call on:
+        # eager first, then captured and replayed at the same offset, and at an earlier one.
+        base = m.offset
+        buf = torch.empty((len(VERIFY_IDS), m.V_local * world), dtype=torch.float16, device=dev)
+        m.forward_rows(VERIFY_IDS, buf)
+        eager = buf.float().cpu().numpy()
+        graph_err = []
+        for off in (base, base - 30):
+            m.rewind(off)
+            m.forward_rows(VERIFY_IDS, buf)
+            if off == base:
+                graph_err.append(float(abs(buf.float().cpu().numpy() - eager).max()))
+            graph_err.append(int(m.offset == off + len(VERIFY_IDS)))
+        m.check_rows_error()
+        graphs = len(m._row_graphs)
+        m.rewind(base)
         rows = m.forward_rows(VERIFY_IDS).float().cpu().numpy()
         draft = MotifDecoder.random(_draft_args(), seed=12, std=0.05, max_seq=256, device=dev)
         spec = SpeculativeDecoder(m, draft, k=4, temperature=0.0)
         toks = spec.generate(ROW_PROMPT[:40], 12)
-        m._graphs.clear()
+        m.release_graphs()
         torch.cuda.synchronize()
         dist.barrier()
         m.release_exchange()
-        q.put((rank, (first, rows, toks)))
+        q.put((rank, (first, rows, toks, graph_err, graphs)))
     finally:
         dist.destroy_process_group()
 
@@ -190,3 +206,7 @@ def test_tp_row_blocks_and_speculative_verify(world):
         err = float(abs(got[r][1] - rows).max())
         assert err < 5e-2, f"rank {r}: verify logits differ by {err}"
         assert got[r][2] == greedy, f"rank {r}: speculative tokens {got[r][2]} != greedy {greedy}"
+        graph_err, graphs = got[r][3], got[r][4]
+        assert graphs == 1, f"rank {r}: {graphs} row-block graphs captured"
+        assert graph_err[0] < 5e-2, f"rank {r}: graph replay logits differ from eager by {graph_err[0]}"
+        assert graph_err[1] == 1 and graph_err[2] == 1, f"rank {r}: offsets after replay {graph_err}"
