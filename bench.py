@@ -702,10 +702,10 @@ def speculative_extra(a, args, van, dev, st, e0, e1, group, rank, world) -> dict
         **rows_ms,
         "note": "draft and target are independent random-init models, so few draft tokens match "
                 "the target's distribution; the verify forward streams the target's weights once for "
-                "its K+1 rows (multi-row GEMV); the verify replays a CUDA graph (positions read from "
-                "the device offset; under TP the graph also holds the NCCL all-reduces and the "
-                "lm_head all-gather); verify_forward_ms and decode_step_ms also cover the host's "
-                "rewind between calls (under TP: a device sync, two barriers and the exchange reset)",
+                "its K+1 rows (multi-row GEMV); on one GPU the verify replays a CUDA graph (positions "
+                "read from the device offset), under TP it runs eagerly with NCCL all-reduces; "
+                "verify_forward_ms and decode_step_ms also cover the host's rewind between calls "
+                "(under TP: a device sync, two barriers and the exchange reset)",
     }
     target.release_graphs()  # graphs may hold NCCL calls: released before the communicator
     torch.cuda.synchronize()

@@ -1150,10 +1150,9 @@ class MotifDecoder:
     def _rows_graph_ok(self, S: int) -> bool:
         """A row block replays as a CUDA graph when its launches take no host-side offset: an fp16
         cache (a quantized cache is dequantized up to the block's rows) and a short block (the
-        multi-row GEMV and split attention path). Under tensor parallelism the graph also holds
-        the block's NCCL all-reduces and the lm_head all-gather; every rank captures at the same
-        call. MOTIF_ROWS_GRAPH=0 keeps every call eager."""
-        return (self.cache_kind == "fp16" and 1 <= S < min(self.min_block_rows, 129)
+        multi-row GEMV and split attention path) on one GPU; under tensor parallelism row blocks
+        run eagerly. MOTIF_ROWS_GRAPH=0 keeps every call eager."""
+        return (self.cache_kind == "fp16" and self.tp_group is None and 1 <= S < min(self.min_block_rows, 129)
                 and os.environ.get("MOTIF_ROWS_GRAPH", "1") != "0")
 
     def check_rows_error(self) -> None:
