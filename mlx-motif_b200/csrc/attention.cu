@@ -607,10 +607,13 @@ __global__ void __launch_bounds__(kAttnThreads) gda_fused_kernel(FusedArgs f) {
     }
   };
   const bool append = pos >= 0 && pos < cap && ((pos >= p0 && pos < p1) || (split == 0 && pos >= kv_len));
-  // The first round of this warp's rows does not depend on the RoPE work below, except in the
-  // warp of the appending CTA whose first round holds row pos: start the others now.
+  // The first round of this warp's rows does not depend on the RoPE work below, so it starts
+  // now. In the appending CTA the warp whose first round holds row pos either loads it later
+  // (quantized caches: the row is read back as stored) or, for fp16 rows, takes the new row
+  // from shared memory after the append (the value it would read back, without the round trip).
   const int first = p0 + warp * kPosPerWarp;
-  const bool defer = append && pos >= first && pos < first + kPosPerWarp;
+  const bool holds_new = append && pos >= first && pos < first + kPosPerWarp && pos < p1;
+  const bool defer = BITS != 16 && holds_new;
   if (!defer) load_round(first);
   // RoPE angles of this position, shared by every head of the CTA
   if (threadIdx.x < half) rope_angle(threadIdx.x, pos, f.inv_freq, s_cs[threadIdx.x], s_sn[threadIdx.x]);
@@ -619,6 +622,20 @@ __global__ void __launch_bounds__(kAttnThreads) gda_fused_kernel(FusedArgs f) {
   // row comes from the previous kernel (the qkv projection): wait for it here.
   asm volatile("griddepcontrol.wait;\n" ::: "memory");
   __syncthreads();
+
+  // ---- rotated q of the group's GR origin heads and its noise head (its loads go out
+  // before the append below, so the appending CTA waits for one round trip, not two) ----
+  float q[NH][CPL];
+#pragma unroll
+  for (int h = 0; h < NH; ++h) {
+    const int head = fused_head<NA, NB, PAIRED>(g, h, f.q_origin);
+    const __half* src = f.qkv + (int64_t)head * D;
+#pragma unroll
+    for (int j = 0; j < CPL; ++j) {
+      const int c = lane * CPL + j, k = c < half ? c : c - half;
+      q[h][j] = __half2float(__float2half_rn(rope_rotate(src, c, half, s_cs[k], s_sn[k]))) * f.scale_log2;
+    }
+  }
 
   // ---- append the new row of this group (k1, k2, v1, v2 by warps 0..3) ----
   if (append) {
@@ -636,7 +653,10 @@ __global__ void __launch_bounds__(kAttnThreads) gda_fused_kernel(FusedArgs f) {
       if constexpr (BITS == 16) {
         __half* dst = static_cast<__half*>(f.cache.data[warp]) + row * D + lane * CPL;
 #pragma unroll
-        for (int j = 0; j < CPL; ++j) dst[j] = hv[j];
+        for (int j = 0; j < CPL; ++j) {
+          dst[j] = hv[j];
+          s_row[warp][lane * CPL + j] = __half2float(hv[j]);
+        }
       } else {
 #pragma unroll
         for (int j = 0; j < CPL; ++j) s_row[warp][lane * CPL + j] = __half2float(hv[j]);
@@ -666,19 +686,6 @@ __global__ void __launch_bounds__(kAttnThreads) gda_fused_kernel(FusedArgs f) {
     __syncthreads();  // the row is read back below (global writes ordered for the CTA)
   }
 
-  // ---- rotated q of the group's GR origin heads and its noise head ----
-  float q[NH][CPL];
-#pragma unroll
-  for (int h = 0; h < NH; ++h) {
-    const int head = fused_head<NA, NB, PAIRED>(g, h, f.q_origin);
-    const __half* src = f.qkv + (int64_t)head * D;
-#pragma unroll
-    for (int j = 0; j < CPL; ++j) {
-      const int c = lane * CPL + j, k = c < half ? c : c - half;
-      q[h][j] = __half2float(__float2half_rn(rope_rotate(src, c, half, s_cs[k], s_sn[k]))) * f.scale_log2;
-    }
-  }
-
   float m[NH], l[NH], o1[NH][CPL], o2[NH][CPL];
 #pragma unroll
   for (int h = 0; h < NH; ++h) {
@@ -688,6 +695,20 @@ __global__ void __launch_bounds__(kAttnThreads) gda_fused_kernel(FusedArgs f) {
     for (int c = 0; c < CPL; ++c) o1[h][c] = o2[h][c] = 0.f;
   }
   if (defer) load_round(first);  // after the new row is written
+  if (BITS == 16 && holds_new) {  // the new row, as stored, from shared memory
+#pragma unroll
+    for (int u = 0; u < kPosPerWarp; ++u) {
+      if (first + u == pos) {
+#pragma unroll
+        for (int j = 0; j < CPL; ++j) {
+          ka[u][j] = s_row[0][lane * CPL + j];
+          kb[u][j] = s_row[1][lane * CPL + j];
+          x1[u][j] = s_row[2][lane * CPL + j];
+          x2[u][j] = s_row[3][lane * CPL + j];
+        }
+      }
+    }
+  }
   for (int base = p0 + warp * kPosPerWarp; base < p1; base += kRoundPositions) {
     if (base != p0 + warp * kPosPerWarp) load_round(base);
 #pragma unroll
