@@ -631,12 +631,13 @@ __device__ void stage_x(const LinArgs& a, __half* xp_s, float* xsum_s, float* co
 #pragma unroll
     for (int i = 0; i < kMaxStageWords; ++i) {
       if (tid + i * nthr < words) {
-        const __half* hv = reinterpret_cast<const __half*>(&in0[i]);
-        const __half* dv = reinterpret_cast<const __half*>(&in1[i]);
+        const __half2* hv = reinterpret_cast<const __half2*>(&in0[i]);
+        const __half2* dv = reinterpret_cast<const __half2*>(&in1[i]);
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const float v = delta ? round_through<__half>(__half2float(hv[j]) + __half2float(dv[j])) : __half2float(hv[j]);
-          acc[0] += v * v;
+        for (int j = 0; j < 4; ++j) {
+          const float2 v = __half22float2(delta ? __hadd2(hv[j], dv[j]) : hv[j]);
+          acc[0] += v.x * v.x;
+          acc[0] += v.y * v.y;
         }
       }
     }
@@ -654,63 +655,69 @@ __device__ void stage_x(const LinArgs& a, __half* xp_s, float* xsum_s, float* co
   }
   const bool write_h = MODE == kModeAddRms && a.h_out && blockIdx.x == 0;
   // ---- build x, permute, group sums ----
+  // In half2 pairs: the fp16 residual add (__hadd2) and PolyNorm·up product (__hmul2) equal
+  // rounding the fp32 sum/product once (fp32 holds the exact product of two fp16 values, and
+  // its 24 bits make the fp32-then-fp16 rounding of a sum innocuous), and pairs of floats are
+  // rounded to fp16 with one packed conversion.
 #pragma unroll
   for (int i = 0; i < kMaxStageWords; ++i) {
     const int wi = tid + i * nthr;
     if (i * nthr >= words) break;  // uniform across the block
     const bool act = wi < words;
-    __half h[8];
+    __half2 h2[4];
     if (act) {
-      const __half* e0 = reinterpret_cast<const __half*>(&in0[i]);
-      const __half* e1 = reinterpret_cast<const __half*>(&in1[i]);
-      const __half* e2 = reinterpret_cast<const __half*>(&in2[i]);
+      const __half2* e0 = reinterpret_cast<const __half2*>(&in0[i]);
+      const __half2* e1 = reinterpret_cast<const __half2*>(&in1[i]);
+      const __half2* e2 = reinterpret_cast<const __half2*>(&in2[i]);
       if constexpr (MODE == kModeX) {
 #pragma unroll
-        for (int j = 0; j < 8; ++j) h[j] = e0[j];
+        for (int j = 0; j < 4; ++j) h2[j] = e0[j];
       } else if constexpr (MODE == kModeAddRms) {
-        float v[8];
+        __half2 vh[4];
 #pragma unroll
-        for (int j = 0; j < 8; ++j)
-          v[j] = delta ? round_through<__half>(__half2float(e0[j]) + __half2float(e1[j])) : __half2float(e0[j]);
-        if (write_h) store_vec<__half, 8>(a.h_out + (int64_t)wi * 8, v);
+        for (int j = 0; j < 4; ++j) vh[j] = delta ? __hadd2(e0[j], e1[j]) : e0[j];
+        if (write_h) *reinterpret_cast<uint4*>(a.h_out + (int64_t)wi * 8) = *reinterpret_cast<const uint4*>(vh);
 #pragma unroll
-        for (int j = 0; j < 8; ++j) h[j] = __float2half_rn(v[j] * inv * __half2float(e2[j]));
+        for (int j = 0; j < 4; ++j) {
+          const float2 v = __half22float2(vh[j]);
+          const float2 w = __half22float2(e2[j]);
+          h2[j] = __floats2half2_rn(v.x * inv * w.x, v.y * inv * w.y);
+        }
       } else {
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const float g = __half2float(e0[j]);
-          const float g2 = g * g;
-          const float g3 = g2 * g;
-          const float p = pw0 * (g3 * r6) + pw1 * (g2 * r4) + pw2 * (g * r2) + pb;
-          h[j] = __float2half_rn(round_through<__half>(p) * __half2float(e1[j]));
+        for (int j = 0; j < 4; ++j) {
+          const float2 g = __half22float2(e0[j]);
+          const float gx2 = g.x * g.x, gy2 = g.y * g.y;
+          const float gx3 = gx2 * g.x, gy3 = gy2 * g.y;
+          const float px = pw0 * (gx3 * r6) + pw1 * (gx2 * r4) + pw2 * (g.x * r2) + pb;
+          const float py = pw0 * (gy3 * r6) + pw1 * (gy2 * r4) + pw2 * (g.y * r2) + pb;
+          h2[j] = __hmul2(__floats2half2_rn(px, py), e1[j]);
         }
       }
-      if (V2) {
-        const __half sixteenth = __float2half_rn(0.0625f);
+      if (V2) {  // odd k (the .y halves) pre-scaled by 1/16, an exact power of two
+        const __half2 scale = __halves2half2(__float2half_rn(1.f), __float2half_rn(0.0625f));
 #pragma unroll
-        for (int j = 1; j < 8; j += 2) h[j] = __hmul(h[j], sixteenth);
+        for (int j = 0; j < 4; ++j) h2[j] = __hmul2(h2[j], scale);
       }
+      // dequant order of the 8 values: 0,4,1,5,2,6,3,7
       uint4 o;
-      __half* oe = reinterpret_cast<__half*>(&o);
-      oe[0] = h[0];
-      oe[1] = h[4];
-      oe[2] = h[1];
-      oe[3] = h[5];
-      oe[4] = h[2];
-      oe[5] = h[6];
-      oe[6] = h[3];
-      oe[7] = h[7];
+      __half2* oe = reinterpret_cast<__half2*>(&o);
+      oe[0] = __lows2half2(h2[0], h2[2]);
+      oe[1] = __highs2half2(h2[0], h2[2]);
+      oe[2] = __lows2half2(h2[1], h2[3]);
+      oe[3] = __highs2half2(h2[1], h2[3]);
       *reinterpret_cast<uint4*>(xp_s + (int64_t)wi * 8 + (V2 ? (int64_t)(wi >> 3) * (kXGroupBytes / 2 - 64) : 0)) = o;
     } else {
 #pragma unroll
-      for (int j = 0; j < 8; ++j) h[j] = __float2half_rn(0.f);
+      for (int j = 0; j < 4; ++j) h2[j] = __float2half2_rn(0.f);
     }
     // even-k (lo) and odd-k (hi) sums of this word, reduced over the group's 8 threads
     float lo = 0.f, hi = 0.f;
 #pragma unroll
-    for (int j = 0; j < 8; j += 2) {
-      lo += __half2float(h[j]);
-      hi += __half2float(h[j + 1]);
+    for (int j = 0; j < 4; ++j) {
+      const float2 f = __half22float2(h2[j]);
+      lo += f.x;
+      hi += f.y;
     }
 #pragma unroll
     for (int o = 1; o < 8; o <<= 1) {
