@@ -20,6 +20,7 @@ fused gate|up GEMV, PolyNorm·up, down GEMV, residual+RMSNorm.
 
 from __future__ import annotations
 
+import contextlib
 import enum
 import math
 import os
@@ -31,6 +32,18 @@ from ._native import check, lib, motif_linear_io, ptr, stream
 from .cache import KVCache, MotifGroupedKVCache, MotifGroupedQuantizedKVCache, MotifVanillaKVCache
 from .linear import QuantizedLinear
 from .quantization import quantize
+
+# MOTIF_NVTX=1: NVTX ranges around every op a decoder launches (per layer and op name) and around
+# graph replays and prompt blocks, for Nsight timelines. Ranges are host-side markers: a replayed
+# CUDA graph shows as one "decode_step" range, its kernels inside it.
+_NVTX = os.environ.get("MOTIF_NVTX", "0") not in ("", "0")
+
+
+def nvtx_range(name: str):
+    """An NVTX range named ``name`` while MOTIF_NVTX is set, else a no-op context."""
+    if not _NVTX:
+        return contextlib.nullcontext()
+    return torch.cuda.nvtx.range(name)
 
 # --------------------------------------------------------------------------- #
 # Config (model.py:48-204)
@@ -758,8 +771,17 @@ class MotifDecoder:
         kvl_p = pos_p + 4
         tp = self.tp_group is not None
         for li, L in enumerate(self.layers):
-            qkv_io, o_io, gu_io, dn_io = plan[li]
+            with nvtx_range(f"layer {li}"):
+                self._launch_layer(li, L, plan[li], st, pos_p, kvl_p, tp)
+        with nvtx_range("head"):
+            self._head(with_head, head_io, st)
+
+    def _launch_layer(self, li: int, L: dict, ios, st: int, pos_p: int, kvl_p: int, tp: bool) -> None:
+        """One layer of ``_launch_step``."""
+        qkv_io, o_io, gu_io, dn_io = ios
+        with nvtx_range("qkv"):
             self._linear(qkv_io, L["qkv"], self.qkv, st)
+        with nvtx_range("attention"):
             if self.vanilla:
                 check(lib.motif_vanilla_decode_step(ptr(self.qkv), ptr(self.inv_freq), self._slots[li], pos_p,
                                                     self.scale, self.kv_heads, self.gr, ptr(L["subln"]),
@@ -783,18 +805,20 @@ class MotifDecoder:
                                                      L["lambda_full"].numel(), L["lambda_init"],
                                                      self.args.attn_rms_norm_eps, ptr(self.attn), ptr(self.attn_ws),
                                                      self.attn_ws_bytes, st), "gda_decode_attention")
+        with nvtx_range("o_proj"):
             self._linear(o_io, L["o"], self.o, st)
             if not self.tp_exchange:
                 self._allreduce(self.o)
+        with nvtx_range("gate_up"):
             self._linear(gu_io, L["gate_up"], self.gu, st)
             if tp and not self.tp_exchange:
                 # Full-row PolyNorm statistics across ranks (12 bytes over NCCL).
                 torch.sum(self.stats.view(-1, 3), dim=0, out=self.stats_sum)
                 self._allreduce(self.stats_sum)
+        with nvtx_range("down"):
             self._linear(dn_io, L["down"], self.dn, st)
             if not self.tp_exchange:
                 self._allreduce(self.dn)
-        self._head(with_head, head_io, st)
 
     def _dequant_bridge(self, li: int, st: int):
         """Layer li's packed slots dequantized to fp16 rows in the shared bridge buffers (every
@@ -896,7 +920,8 @@ class MotifDecoder:
         """One decode step from ``self.token`` (device); the argmax lands back in ``self.token``."""
         if self.offset >= self.max_seq:
             raise ValueError(f"KV capacity {self.max_seq} exhausted")
-        self._graph(with_head).replay()
+        with nvtx_range("decode_step"):
+            self._graph(with_head).replay()
         self._bump_host()
 
     def step_eager(self, with_head: bool = True) -> None:
@@ -1012,7 +1037,8 @@ class MotifDecoder:
         S = ids_d.numel()
         if self.offset + S + 1 > self.max_seq:
             raise ValueError(f"KV capacity {self.max_seq} exhausted by a {S}-row block at {self.offset}")
-        b = self._launch_block(ids_d, logits_out, device_offset=False)
+        with nvtx_range(f"prompt block {S} rows"):
+            b = self._launch_block(ids_d, logits_out, device_offset=False)
         self._bump_host(S)
         self.pos_len.copy_(torch.tensor([self.offset, self.offset + 1], dtype=torch.int32))
         if int(b["err"].item()) != 0:

@@ -492,6 +492,24 @@ def test_decoder_graph_equals_eager(cuda):
     assert a.offset == 3 and int(a.pos_len[0]) == 3 and int(a.pos_len[1]) == 4
 
 
+def test_decoder_with_nvtx_ranges_equals_without(cuda, monkeypatch):
+    """MOTIF_NVTX ranges around every op change no launch: the same logits and tokens, eager
+    and graph-replayed."""
+    import mlx_motif.model as M
+
+    oa = _tiny_args()
+    w = O.make_synthetic_weights(oa, seed=2, std=0.05)
+    plain = M.MotifDecoder(_to_model_args(oa), w, max_seq=256, device=cuda)
+    monkeypatch.setattr(M, "_NVTX", True)
+    marked = M.MotifDecoder(_to_model_args(oa), w, max_seq=256, device=cuda)
+    for t in (7, 8, 9):
+        plain.token.fill_(t)
+        marked.token.fill_(t)
+        plain.step_eager()
+        (marked.step_eager if t == 7 else marked.step_device)()
+        assert torch.equal(plain.logits, marked.logits) and torch.equal(plain.token, marked.token)
+
+
 def test_decoder_host_api_and_generate(cuda):
     from mlx_motif.model import MotifDecoder
 

@@ -272,3 +272,26 @@ def test_vocab_parallel_argmax_keys_over_gloo():
         p.join(timeout=60)
         assert p.exitcode == 0
     assert toks == [9, 9]
+
+
+def test_nvtx_ranges_follow_the_env_switch(monkeypatch):
+    """MOTIF_NVTX off: the decoder's op ranges are no-op contexts; on: each opens an NVTX range
+    with its name (the launches inside are the same either way)."""
+    import contextlib
+
+    import mlx_motif.model as M
+
+    monkeypatch.setattr(M, "_NVTX", False)
+    assert isinstance(M.nvtx_range("qkv"), contextlib.nullcontext)
+    opened = []
+
+    def fake_range(name):
+        opened.append(name)
+        return contextlib.nullcontext()
+
+    monkeypatch.setattr(M, "_NVTX", True)
+    monkeypatch.setattr(torch.cuda.nvtx, "range", fake_range)
+    with M.nvtx_range("layer 0"):
+        with M.nvtx_range("qkv"):
+            pass
+    assert opened == ["layer 0", "qkv"]
