@@ -536,6 +536,18 @@ MOTIF_API size_t motif_argmax_workspace_bytes(int64_t n);
 /* Token (and optional pos_len int32[2] += 1) from a key of argmax_key_out,
  * after the shards' keys were combined with an int64 MAX all-reduce. */
 MOTIF_API int motif_argmax_key_decode(const int64_t* key, int32_t* token, int32_t* pos_len_inc, void* stream);
+/* The same token without a collective: the ranks' keys meet over peer memory (no reference
+ * counterpart: the reference is single-device). key: this rank's key (argmax_key_out or
+ * motif_sample_key). slots (host array of `world` device pointers): each rank's key area of
+ * 2*world int64 in its peer-visible buffer (motif_ipc_alloc / motif_ipc_open), zeroed whenever
+ * the position is rewound. One launch tags the key with the step read from pos_dev[0], stores it
+ * into slot [(pos & 1) * world + rank] of every rank's area, waits (at most 2 s, then err = 2)
+ * until its own area holds all ranks' keys of this step, writes the token of the largest and
+ * advances pos_len_inc. Global rows must be below 2^24 - 1. Every rank launches it once per
+ * step, in the same step order. */
+MOTIF_API int motif_argmax_key_exchange(const int64_t* key, int64_t* const* slots, int world, int rank,
+                                        const int32_t* pos_dev, int32_t* token, int32_t* pos_len_inc,
+                                        int32_t* err, void* stream);
 MOTIF_API int motif_argmax(int dtype, const void* logits, int64_t n, int32_t* out_index, void* workspace,
                  size_t workspace_bytes, void* stream);
 

@@ -290,6 +290,72 @@ __global__ void argmax_key_decode_kernel(const long long* __restrict__ key, int3
   }
 }
 
+// The tensor-parallel greedy/sampled token over peer memory. Each rank's key (value bits << 32 |
+// (2^32 - 1 - row), as the lm_head epilogue or motif_sample_key writes it, sign-flipped) is
+// re-packed with a step number in bits 24..31 of its low word — (value bits << 32) | number << 24 |
+// (2^24 - 1 - row) — and stored, one 8-byte element, into slot [parity * world + rank] of every
+// rank's key area. Keys of one step all carry the same number, so the largest packed key is still
+// the largest value at its first row. Each rank then reads its own area until all `world` slots
+// carry this step's number (bounded), and decodes the largest. number = pos % 255 + 1 is never 0
+// (a zeroed area) and a slot is rewritten every second step, so a stale key never matches.
+struct KeySlots {
+  long long* p[8];
+};
+__device__ __forceinline__ unsigned long long global_timer_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+constexpr unsigned long long kKeyWaitNs = 2000ull * 1000 * 1000;
+
+__global__ void argmax_key_exchange_kernel(const long long* __restrict__ key, KeySlots slots, int world, int rank,
+                                           const int32_t* __restrict__ pos_dev, int32_t* __restrict__ token,
+                                           int32_t* __restrict__ pos_len, int32_t* __restrict__ err) {
+  const int i = threadIdx.x;
+  const int pos = pos_dev[0];
+  const unsigned long long number = (unsigned long long)(((pos % 255) + 255) % 255 + 1);
+  const int par = pos & 1;
+  const unsigned long long k = (unsigned long long)key[0] ^ 0x8000000000000000ull;
+  const uint32_t row = 0xFFFFFFFFu - (uint32_t)k;
+  const unsigned long long packed =
+      k == 0 ? (number << 24) : ((k & 0xFFFFFFFF00000000ull) | (number << 24) | (0xFFFFFFu - (row & 0xFFFFFFu)));
+  if (i < world) {
+    long long* dst = slots.p[i] + par * world + rank;
+    asm volatile("st.relaxed.sys.global.b64 [%0], %1;\n" ::"l"(dst), "l"((long long)packed) : "memory");
+  }
+  unsigned long long v = 0;
+  if (i < world) {
+    const long long* src = slots.p[rank] + par * world + i;
+    long long x;
+    asm volatile("ld.relaxed.sys.global.b64 %0, [%1];\n" : "=l"(x) : "l"(src) : "memory");
+    if ((((unsigned long long)x >> 24) & 0xFFu) != number) {
+      const unsigned long long t0 = global_timer_ns();
+      do {
+        __nanosleep(64);
+        asm volatile("ld.relaxed.sys.global.b64 %0, [%1];\n" : "=l"(x) : "l"(src) : "memory");
+        if (global_timer_ns() - t0 > kKeyWaitNs) {
+          if (err) atomicExch(err, 2);
+          break;
+        }
+      } while ((((unsigned long long)x >> 24) & 0xFFu) != number);
+    }
+    v = (unsigned long long)x;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const unsigned long long other = __shfl_xor_sync(0xffffffffu, v, o);
+    v = other > v ? other : v;
+  }
+  if (i == 0) {
+    const uint32_t field = (uint32_t)(v & 0xFFFFFFu);
+    token[0] = ((v >> 32) == 0 && field == 0) ? 0 : (int32_t)(0xFFFFFFu - field);
+    if (pos_len) {
+      pos_len[0] += 1;
+      pos_len[1] += 1;
+    }
+  }
+}
+
 constexpr int kArgmaxThreads = 256;
 int argmax_parts(int64_t n) {
   int64_t p = ceil_div(n, kArgmaxThreads * 8);
@@ -448,6 +514,22 @@ int motif_argmax_key_decode(const int64_t* key, int32_t* token, int32_t* pos_len
   MOTIF_REQUIRE(key && token, MOTIF_ERR_NULL, "argmax_key_decode: null pointer");
   argmax_key_decode_kernel<<<1, 1, 0, as_stream(stream)>>>(reinterpret_cast<const long long*>(key), token, pos_len_inc);
   return check_launch("argmax_key_decode");
+}
+
+int motif_argmax_key_exchange(const int64_t* key, int64_t* const* slots, int world, int rank, const int32_t* pos_dev,
+                              int32_t* token, int32_t* pos_len_inc, int32_t* err, void* stream) {
+  MOTIF_REQUIRE(key && slots && pos_dev && token, MOTIF_ERR_NULL, "argmax_key_exchange: null pointer");
+  MOTIF_REQUIRE(world >= 1 && world <= 8 && rank >= 0 && rank < world, MOTIF_ERR_BAD_CONTRACT,
+                "argmax_key_exchange: rank %d of world %d (1..8)", rank, world);
+  KeySlots ks{};
+  for (int r = 0; r < world; ++r) {
+    MOTIF_REQUIRE(slots[r] && reinterpret_cast<uintptr_t>(slots[r]) % 8 == 0, MOTIF_ERR_NULL,
+                  "argmax_key_exchange: key area of rank %d", r);
+    ks.p[r] = reinterpret_cast<long long*>(slots[r]);
+  }
+  argmax_key_exchange_kernel<<<1, 32, 0, as_stream(stream)>>>(reinterpret_cast<const long long*>(key), ks, world,
+                                                               rank, pos_dev, token, pos_len_inc, err);
+  return check_launch("argmax_key_exchange");
 }
 
 int motif_argmax(int dtype, const void* logits, int64_t n, int32_t* out_index, void* workspace,

@@ -41,6 +41,6 @@ const char* motif_status_string(int status) {
 
 const char* motif_last_error(void) { return motif::g_last_error; }
 
-int motif_abi_version(void) { return 2; }
+int motif_abi_version(void) { return 3; }
 
 }  // extern "C"

@@ -141,6 +141,7 @@ SIGNATURES = {
     "motif_argmax_workspace_bytes": (_S, [_L]),
     "motif_argmax": (_I, [_I, _P, _L, _P, _P, _S, _P]),
     "motif_argmax_key_decode": (_I, [_P, _P, _P, _P]),
+    "motif_argmax_key_exchange": (_I, [_P, _P, _I, _I, _P, _P, _P, _P, _P]),
     "motif_ipc_handle_bytes": (_S, []),
     "motif_ipc_alloc": (_I, [_S, C.POINTER(C.c_void_p), _P]),
     "motif_ipc_open": (_I, [_P, C.POINTER(C.c_void_p)]),

@@ -530,6 +530,10 @@ class MotifDecoder:
         # Tensor parallelism exchanges the row-parallel outputs and the PolyNorm statistics through
         # peer memory inside the GEMVs (MOTIF_TP_NCCL=1: NCCL all-reduces instead).
         self.tp_exchange = self.tp_group is not None and os.environ.get("MOTIF_TP_NCCL", "0") != "1"
+        # MOTIF_TP_KEY_EXCHANGE=1: the head's token keys meet over the same buffers (rows below
+        # 2^24 - 1) instead of an NCCL MAX all-reduce.
+        self.key_exchange = (self.tp_exchange and self.V < (1 << 24) - 1
+                             and os.environ.get("MOTIF_TP_KEY_EXCHANGE", "0") == "1")
         self._xbuf = None
         if self.tp_exchange:
             self._setup_exchange()
@@ -595,8 +599,9 @@ class MotifDecoder:
     def _setup_exchange(self) -> None:
         """One peer-visible buffer per rank (CUDA IPC) holding, for the two layer parities, every
         rank's o_proj and down_proj partial rows and PolyNorm tile statistics, each value as an
-        8-byte (fp32, exchange number) pair. Ranks trade the IPC handles over the process group
-        and open each other's buffers."""
+        8-byte (fp32, exchange number) pair, and for the two step parities every rank's greedy /
+        sampled token key (motif_argmax_key_exchange). Ranks trade the IPC handles over the
+        process group and open each other's buffers."""
         import ctypes as C
 
         W, H = self.tp, self.H
@@ -604,7 +609,8 @@ class MotifDecoder:
         ntl = self.inter // 16
         part = W * H * 8
         off = dict(o=0, dn=2 * part, st=4 * part)
-        total = off["st"] + 2 * W * ntl * 3 * 8
+        off["key"] = off["st"] + 2 * W * ntl * 3 * 8
+        total = off["key"] + 2 * W * 8
         ptr = C.c_void_p()
         handle = (C.c_char * lib.motif_ipc_handle_bytes())()
         check(lib.motif_ipc_alloc(total, C.byref(ptr), handle), "ipc_alloc")
@@ -620,6 +626,8 @@ class MotifDecoder:
                 peers.append(q.value)
         self._xbuf, self._xpeers, self._xoff, self._xme, self._xntl = ptr.value, peers, off, me, ntl
         self._xbytes = total
+        # every rank's key area, for the head's token exchange
+        self._key_slots = (C.c_void_p * W)(*[base + off["key"] for base in peers])
 
     def _x_slot(self, kind: str, par: int, src: int) -> int:
         """Byte offset of source rank src's slot of exchange `kind` ("o", "dn", "st") at parity par."""
@@ -658,6 +666,7 @@ class MotifDecoder:
         torch.distributed.barrier(group=self.tp_group)
 
     _TP_WAIT_BYTE = 65504  # the GEMV workspace's int64 of exchange-read nanoseconds (CTA 0)
+    _ERR_BYTE = 65532  # the GEMV workspace's error word (exchange waits that ran out)
 
     def exchange_read_ns(self, reset: bool = False) -> int:
         """Nanoseconds CTA 0 of the consuming GEMVs spent reading exchanged values (waits for the
@@ -841,6 +850,14 @@ class MotifDecoder:
                     check(lib.motif_sample_key(ptr(self.logits), self.V_local, self.temperature, self.seed,
                                                ptr(self.pos_len), 0, self.stream_id, self.v0, ptr(self.amax_key), st),
                           "sample_key")
+                if self.key_exchange:  # the ranks' keys meet over peer memory
+                    import ctypes as C
+
+                    check(lib.motif_argmax_key_exchange(ptr(self.amax_key), C.cast(self._key_slots, C.c_void_p),
+                                                        self.tp, self._xme, ptr(self.pos_len), ptr(self.token),
+                                                        ptr(self.pos_len), ptr(self.lin_ws) + self._ERR_BYTE, st),
+                          "argmax_key_exchange")
+                    return
                 torch.distributed.all_reduce(self.amax_key, op=torch.distributed.ReduceOp.MAX, group=self.tp_group)
                 check(lib.motif_argmax_key_decode(ptr(self.amax_key), ptr(self.token), ptr(self.pos_len), st),
                       "argmax_key_decode")

@@ -33,7 +33,7 @@ def test_library_exports_every_declared_symbol():
 def test_status_strings_and_version():
     from mlx_motif import _native as N
 
-    assert N.lib.motif_abi_version() == 2  # motif_linear_io gained argmax_out, pos_len_inc
+    assert N.lib.motif_abi_version() == 3  # motif_argmax_key_exchange added
     assert N.lib.motif_status_string(0) == b"ok"
     assert N.lib.motif_status_string(3) == b"shape outside kernel contract"
 
