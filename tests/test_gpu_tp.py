@@ -50,14 +50,20 @@ def _args():
                      num_key_value_heads=16, vocab_size=2048, head_dim=128, num_noise_heads=8)
 
 
-def _worker(rank, world, port, q, nccl_only=False):
+def _head_env(head: str) -> None:
+    """How the ranks' token keys meet: "key" over peer memory, "allreduce" by NCCL MAX."""
+    os.environ["MOTIF_TP_KEY_EXCHANGE"] = "1" if head == "key" else "0"
+
+
+def _worker(rank, world, port, q, exchange="peer"):
     import torch.distributed as dist
     from mlx_motif.model import MotifDecoder
 
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
     _watchdog()
-    if nccl_only:
+    if exchange == "nccl":
         os.environ["MOTIF_TP_NCCL"] = "1"
+    _head_env("key" if exchange == "peer-key" else "allreduce")
     torch.cuda.set_device(rank)
     dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60))
     try:
@@ -75,12 +81,13 @@ def _worker(rank, world, port, q, nccl_only=False):
         dist.destroy_process_group()
 
 
-def _sample_worker(rank, world, port, q):
+def _sample_worker(rank, world, port, q, head="allreduce"):
     import torch.distributed as dist
     from mlx_motif.model import MotifDecoder
 
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
     _watchdog()
+    _head_env(head)
     torch.cuda.set_device(rank)
     dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60))
     try:
@@ -97,19 +104,20 @@ def _sample_worker(rank, world, port, q):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world", [2, 4, 8])
-def test_tp_temperature_sampling_equals_single_gpu(world):
+@pytest.mark.parametrize("world,head", [(2, "allreduce"), (4, "allreduce"), (8, "allreduce"), (2, "key"), (4, "key"),
+                                        (8, "key")])
+def test_tp_temperature_sampling_equals_single_gpu(world, head):
     """Temperature sampling under tensor parallelism (each rank's Gumbel-max key over its
-    vocabulary shard, noise drawn per global index, combined by the MAX all-reduce) draws the
-    same tokens as one GPU with the same seed."""
+    vocabulary shard, noise drawn per global index, combined by the MAX all-reduce or over peer
+    memory) draws the same tokens as one GPU with the same seed."""
     from mlx_motif.model import MotifDecoder
 
     if torch.cuda.device_count() < world:
         pytest.skip(f"needs {world} GPUs")
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    port = 29880 + (os.getpid() % 40) + 5 * world
-    procs = [ctx.Process(target=_sample_worker, args=(r, world, port, q)) for r in range(world)]
+    port = 29880 + (os.getpid() % 40) + 5 * world + (2 if head == "key" else 0)
+    procs = [ctx.Process(target=_sample_worker, args=(r, world, port, q, head)) for r in range(world)]
     for p in procs:
         p.start()
     got = _collect(procs, q)
@@ -120,17 +128,19 @@ def test_tp_temperature_sampling_equals_single_gpu(world):
         assert got[r] == want, f"rank {r}: TP{world} sampled {got[r]}, one GPU {want}"
 
 
-@pytest.mark.parametrize("world,exchange", [(2, "peer"), (2, "nccl"), (4, "peer"), (8, "peer")])
+@pytest.mark.parametrize("world,exchange", [(2, "peer"), (2, "nccl"), (4, "peer"), (8, "peer"), (2, "peer-key"),
+                                            (4, "peer-key"), (8, "peer-key")])
 def test_tp_decode_equals_single_gpu(world, exchange):
-    """Peer-memory exchange inside the GEMVs (default) and the NCCL all-reduce path."""
+    """Peer-memory exchange inside the GEMVs (default) and the NCCL all-reduce path; "peer-key"
+    also moves the token keys onto peer memory (motif_argmax_key_exchange)."""
     from mlx_motif.model import MotifDecoder
 
     if torch.cuda.device_count() < world:
         pytest.skip(f"needs {world} GPUs")
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    port = 29600 + (os.getpid() % 300) + 11 * world + (7 if exchange == "nccl" else 0)
-    procs = [ctx.Process(target=_worker, args=(r, world, port, q, exchange == "nccl")) for r in range(world)]
+    port = 29600 + (os.getpid() % 300) + 11 * world + {"peer": 0, "nccl": 7, "peer-key": 3}[exchange]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q, exchange)) for r in range(world)]
     for p in procs:
         p.start()
     got = _collect(procs, q)
