@@ -295,3 +295,34 @@ def test_nvtx_ranges_follow_the_env_switch(monkeypatch):
         with M.nvtx_range("qkv"):
             pass
     assert opened == ["layer 0", "qkv"]
+
+
+def test_key_exchange_packing_keeps_the_token():
+    """The packing motif_argmax_key_exchange applies to each rank's key — value bits above a step
+    number (bits 24..31) above 2^24 - 1 - row — keeps the largest key's token: over random
+    vocabulary shards, ties across shards included, the largest packed key decodes to the row
+    the plain keys' MAX names."""
+    import struct
+
+    def key_of(val, row):
+        b = struct.unpack("<I", struct.pack("<f", val))[0]
+        hi = (~b & 0xFFFFFFFF) if (b & 0x80000000) else (b | 0x80000000)
+        return (hi << 32) | (0xFFFFFFFF - row)
+
+    def pack(k, number):
+        row = 0xFFFFFFFF - (k & 0xFFFFFFFF)
+        return (k & 0xFFFFFFFF00000000) | (number << 24) | (0xFFFFFF - row)
+
+    rng = np.random.default_rng(3)
+    for _ in range(3000):
+        world = int(rng.integers(1, 9))
+        vocab = int(rng.integers(world, 219521))
+        shard = vocab // world
+        vals = np.round(rng.normal(0, 3, world), int(rng.integers(1, 7))).astype(np.float32).tolist()
+        if rng.random() < 0.3:
+            vals = [vals[0]] * world
+        rows = [r * shard + int(rng.integers(0, shard)) for r in range(world)]
+        keys = [key_of(v, w) for v, w in zip(vals, rows)]
+        want = 0xFFFFFFFF - (max(keys) & 0xFFFFFFFF)
+        number = int(rng.integers(1, 256))
+        assert 0xFFFFFF - (max(pack(k, number) for k in keys) & 0xFFFFFF) == want
