@@ -106,16 +106,9 @@ def load_tensors(model_dir) -> dict[str, torch.Tensor]:
     return {k: v for k, v in tensors.items() if "rotary_emb.inv_freq" not in k and "rope.inv_freq" not in k}
 
 
-_ARG_KEYS = ("model_type", "hidden_size", "num_hidden_layers", "intermediate_size", "num_attention_heads",
-             "num_key_value_heads", "vocab_size", "rms_norm_eps", "rope_theta", "max_position_embeddings",
-             "head_dim", "num_noise_heads", "k_ratio", "attn_rms_norm_eps", "tie_word_embeddings")
-
-
 def args_from_config(cfg: dict) -> ModelArgs:
     """``ModelArgs`` from a converted ``config.json`` (unknown keys ignored, as ``ModelArgs.from_dict``)."""
-    kw = {k: cfg[k] for k in _ARG_KEYS if k in cfg}
-    kw.setdefault("num_noise_heads", None)
-    return ModelArgs(**kw)
+    return ModelArgs.from_dict(cfg)
 
 
 def _f16(t: torch.Tensor) -> torch.Tensor:

@@ -68,6 +68,31 @@ class ModelArgs:
     attn_rms_norm_eps: float = 1e-5
     tie_word_embeddings: bool = False
     fused_rope: bool = False
+    # The reference's remaining config fields (model.py:65-76), accepted so its configs construct;
+    # MotifDecoder rejects the values its decode path does not implement.
+    rope_scaling: dict | None = None
+    hidden_act: str = "poly_norm"
+    use_bias: bool = False
+    expanded: bool = False
+    sliding_window: int | None = None
+    use_sliding_window: bool = False
+    max_window_layers: int | None = None
+    bos_token_id: int | None = None
+    eos_token_id: int | None = None
+
+    @classmethod
+    def from_dict(cls, params: dict) -> "ModelArgs":
+        """The fields of ``params`` that ModelArgs has (unknown keys ignored, as mlx-lm's
+        ``BaseModelArgs.from_dict``); absent optional fields take the reference's defaults
+        (head_dim and num_noise_heads None, max_position_embeddings 8192), not this class's
+        12.7B-class ones."""
+        import dataclasses
+
+        names = {f.name for f in dataclasses.fields(cls)}
+        kw = {k: v for k, v in params.items() if k in names}
+        for k, v in (("head_dim", None), ("num_noise_heads", None), ("max_position_embeddings", 8192)):
+            kw.setdefault(k, v)
+        return cls(**kw)
 
     def __post_init__(self) -> None:
         for name in ("hidden_size", "num_hidden_layers", "intermediate_size", "num_attention_heads",
@@ -382,6 +407,10 @@ class MotifDecoder:
 
     def __init__(self, args: ModelArgs, weights: dict, cache: str | None = None, max_seq: int = 4096,
                  device="cuda", tp_group=None):
+        if args.hidden_act != "poly_norm" or args.use_bias or args.rope_scaling is not None or args.use_sliding_window:
+            raise ValueError("MotifDecoder implements hidden_act='poly_norm', bias-free linears, unscaled RoPE and "
+                             f"full attention (got hidden_act={args.hidden_act!r}, use_bias={args.use_bias}, "
+                             f"rope_scaling={args.rope_scaling!r}, use_sliding_window={args.use_sliding_window})")
         self.vanilla = not args.is_grouped
         if self.vanilla:
             if tp_group is not None:

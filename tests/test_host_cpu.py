@@ -326,3 +326,38 @@ def test_key_exchange_packing_keeps_the_token():
         want = 0xFFFFFFFF - (max(keys) & 0xFFFFFFFF)
         number = int(rng.integers(1, 256))
         assert 0xFFFFFF - (max(pack(k, number) for k in keys) & 0xFFFFFF) == want
+
+
+def test_reference_config_fixtures_construct_model_args():
+    """The reference's own tiny config fixtures (copied by tests/golden/make_golden.py) build
+    ModelArgs — every field of its config, activation and bias included — with the shape
+    expectations its parity-fixture test checks (tests/test_swift_parity_fixtures.py:24-44), and
+    ModelArgs.from_dict gives the same arguments."""
+    import json
+    from pathlib import Path
+
+    from mlx_motif.model import ModelArgs
+
+    cases = json.loads((Path(__file__).parent / "golden" / "model_configs.json").read_text())["configs"]
+    assert len(cases) == 2
+    for case in cases:
+        args = ModelArgs(**case["python"])
+        want = case["expectations"]
+        assert args.is_grouped is want["is_grouped"]
+        assert (args.head_dim or args.hidden_size // args.num_attention_heads) == want["effective_head_dim"]
+        if args.is_grouped:
+            assert args.num_attention_heads // args.num_noise_heads == want["origin_heads_per_noise_head"]
+            assert args.num_key_value_heads // args.num_noise_heads == want["kv_heads_per_group"]
+        assert ModelArgs.from_dict(dict(case["python"], unknown_key=1)) == args
+
+
+@pytest.mark.parametrize("field,value", [("hidden_act", "silu"), ("use_bias", True),
+                                         ("rope_scaling", {"type": "linear", "factor": 2.0}),
+                                         ("use_sliding_window", True)])
+def test_decoder_rejects_config_values_it_does_not_implement(field, value):
+    """ModelArgs takes every reference config field; the decoder names the ones whose values its
+    decode path does not implement instead of running something else."""
+    from mlx_motif.model import ModelArgs, MotifDecoder
+
+    with pytest.raises(ValueError, match=field):
+        MotifDecoder(ModelArgs(**{field: value}), {}, device="cpu")
