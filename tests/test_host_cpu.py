@@ -361,3 +361,29 @@ def test_decoder_rejects_config_values_it_does_not_implement(field, value):
 
     with pytest.raises(ValueError, match=field):
         MotifDecoder(ModelArgs(**{field: value}), {}, device="cpu")
+
+
+def test_make_mask_follows_the_mlx_lm_contract():
+    """cache.make_mask(N, return_array=..., window_size=...) as mlx-lm calls it (the reference's
+    tests/test_grouped_cache.py:16-45): None for one query, "causal" for several, an explicit
+    (N, offset + N) boolean mask on request, and a sliding window that keeps the last
+    window_size keys of every query."""
+    from mlx_motif.cache import KVCache, MotifGroupedKVCache, MotifGroupedQuantizedKVCache
+
+    cache = MotifGroupedKVCache()
+    cache.offset = 3
+    assert cache.make_mask(1, return_array=False, window_size=None) is None
+    assert cache.make_mask(4, return_array=False, window_size=None) == "causal"
+    mask = cache.make_mask(4, return_array=True, window_size=None)
+    assert tuple(mask.shape) == (4, 7)
+    q = torch.arange(4)[:, None] + 3
+    k = torch.arange(7)[None, :]
+    assert torch.equal(mask, k <= q)
+    assert torch.equal(cache.make_mask(4, return_array=True, window_size=2), (k <= q) & (k > q - 2))
+    qcache = MotifGroupedQuantizedKVCache(group_size=64, bits=8)
+    qcache.offset = 2
+    assert qcache.make_mask(1, return_array=False, window_size=None) is None
+    assert qcache.make_mask(5, return_array=False, window_size=None) == "causal"
+    stock = KVCache()
+    stock.offset = 2
+    assert tuple(stock.make_mask(3, return_array=True, window_size=None).shape) == (3, 5)
