@@ -131,15 +131,21 @@ class ModelArgs:
             raise ValueError(f"num_noise_heads must be an integer when provided; got {self.num_noise_heads!r}")
         if self.num_noise_heads <= 0:
             raise ValueError("num_noise_heads must be greater than zero")
-        if type(self.k_ratio) is not int or self.k_ratio < 1:
-            raise ValueError(f"k_ratio must be an integer >= 1 for grouped attention; got {self.k_ratio!r}")
+        if type(self.k_ratio) is not int:
+            raise ValueError(f"k_ratio must be an integer; got {self.k_ratio!r}")
+        if self.k_ratio < 1:
+            raise ValueError(f"k_ratio must be greater than or equal to 1 for grouped attention; got {self.k_ratio}")
         if self.num_attention_heads <= self.num_noise_heads:
             raise ValueError("num_attention_heads must be greater than num_noise_heads for grouped attention")
         if self.num_attention_heads % self.num_noise_heads:
             raise ValueError("num_attention_heads must be divisible by num_noise_heads")
         width = self.k_ratio + 1
-        if self.num_key_value_heads < width or self.num_key_value_heads % width:
-            raise ValueError("num_key_value_heads must be a positive multiple of k_ratio + 1")
+        if self.num_key_value_heads < width:
+            raise ValueError(f"num_key_value_heads must be at least k_ratio + 1 for grouped attention; "
+                             f"got {self.num_key_value_heads} and {self.k_ratio}")
+        if self.num_key_value_heads % width:
+            raise ValueError(f"num_key_value_heads must be divisible by k_ratio + 1; "
+                             f"got {self.num_key_value_heads} and {self.k_ratio}")
         k_noise = self.num_key_value_heads // width
         if self.num_noise_heads % k_noise:
             raise ValueError("num_noise_heads must be divisible by num_key_value_heads / (k_ratio + 1)")

@@ -31,13 +31,49 @@ def test_model_args_validation():
         ModelArgs(num_attention_heads=30, num_noise_heads=8)
     with pytest.raises(ValueError, match="k_ratio"):
         ModelArgs(k_ratio=0)
-    with pytest.raises(ValueError, match="multiple of k_ratio"):
+    with pytest.raises(ValueError, match=r"divisible by k_ratio \+ 1"):
         ModelArgs(num_key_value_heads=15)
     with pytest.raises(ValueError, match="even"):
         ModelArgs(num_noise_heads=None, num_attention_heads=15, num_key_value_heads=15, head_dim=None,
                   hidden_size=30)
     lit = ModelArgs(num_key_value_heads=8)  # BASELINE's literal "8 KV heads" reading
     assert lit.kv_repeat == 2
+
+
+_TINY_GROUPED = dict(model_type="motif", hidden_size=64, num_hidden_layers=2, intermediate_size=128,
+                     num_attention_heads=10, num_key_value_heads=4, num_noise_heads=2, k_ratio=1, vocab_size=128,
+                     max_position_embeddings=64, head_dim=16, tie_word_embeddings=False, hidden_act="poly_norm")
+_TINY_VANILLA = dict(model_type="motif", hidden_size=64, num_hidden_layers=2, intermediate_size=128,
+                     num_attention_heads=4, num_key_value_heads=4, num_noise_heads=None, vocab_size=128,
+                     max_position_embeddings=64, head_dim=16, tie_word_embeddings=True, hidden_act="poly_norm")
+
+
+@pytest.mark.parametrize("base,overrides,message", [
+    (_TINY_GROUPED, {"num_attention_heads": 0}, "num_attention_heads must be greater than zero"),
+    (_TINY_GROUPED, {"num_key_value_heads": 0}, "num_key_value_heads must be greater than zero"),
+    (_TINY_GROUPED, {"num_noise_heads": 0}, "num_noise_heads must be greater than zero"),
+    (_TINY_GROUPED, {"k_ratio": -1}, "k_ratio must be greater than or equal to 1"),
+    (_TINY_GROUPED, {"num_key_value_heads": 1, "k_ratio": 1}, r"num_key_value_heads must be at least k_ratio \+ 1"),
+    (_TINY_GROUPED, {"num_hidden_layers": -3}, "num_hidden_layers must be greater than zero"),
+    (_TINY_GROUPED, {"max_position_embeddings": 0}, "max_position_embeddings must be greater than zero"),
+    (_TINY_GROUPED, {"hidden_size": 1, "head_dim": None}, "derived head_dim must be greater than zero"),
+    (_TINY_VANILLA, {"num_attention_heads": 3}, "num_attention_heads must be even"),
+    (_TINY_VANILLA, {"num_key_value_heads": 3}, "num_key_value_heads must be even"),
+    (_TINY_VANILLA, {"num_attention_heads": 6, "num_key_value_heads": 4},
+     "num_attention_heads must be divisible by num_key_value_heads"),
+    (_TINY_VANILLA, {"head_dim": 8}, r"head_dim \* num_attention_heads must equal hidden_size"),
+    (_TINY_GROUPED, {"num_attention_heads": 9}, "num_attention_heads must be divisible by num_noise_heads"),
+    (_TINY_GROUPED, {"num_key_value_heads": 5}, r"num_key_value_heads must be divisible by k_ratio \+ 1"),
+    (_TINY_GROUPED, {"hidden_size": 65, "head_dim": None}, "hidden_size must be divisible by num_attention_heads"),
+    (_TINY_GROUPED, {"k_ratio": 3, "num_key_value_heads": 8}, "grouped attention ratio must be divisible by k_ratio"),
+])
+def test_model_args_rejections_carry_the_reference_messages(base, overrides, message):
+    """The structural and head-topology rejections of the reference's tests/test_model.py:72-139,
+    with the message fragments its tests match."""
+    from mlx_motif.model import ModelArgs
+
+    with pytest.raises(ValueError, match=message):
+        ModelArgs(**dict(base, **overrides))
 
 
 def test_resolve_attention_path_truth_table():
